@@ -1,0 +1,385 @@
+"""Benchmark: DINOv3 ViT-S+/16 forward, 224x224, batch 64 per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+Our arm. A step is one forward of 64 images per GPU (one CUDA graph replay). Every rank loads its
+own model replica (data-parallel replicas, no collective on the forward; NCCL only for the
+barrier and the max-over-ranks of the timings).
+  value   images/s over all ranks with the inputs already resident in HBM: K steps timed with CUDA
+          events on the model's stream, the L2 flushed (256 MiB memset) between timed steps,
+          value = N * 64 * K / max over ranks of the summed step time.
+  e2e     the same through the public API with host buffers: dv3_forward on a pinned host input,
+          writing a pinned host output, host<->device copies inside the timed region.
+  roofline the dominant kernel (gate/up GEMM + SwiGLU, 46.5 % of the FLOPs): its algorithmic FLOPs
+          per launch / its average launch time (CUDA events around each launch on the model's
+          stream, over `--profile-iters` direct replays of the launch plan), against the measured
+          bf16/f16 dense peak (MEASURED_PEAKS.json). `traffic` comes from the committed ncu
+          summary in profiles/ when it lists this kernel.
+  cpu_baseline the float64 CPU oracle (C restatement of the reference's own float64 forward,
+          tests/support/reference.rs) on this host, OpenMP over images, rank 0 at N = 1 only.
+Reference arm (--impl reference): the same CPU oracle with all host threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "dinov3-loom_b200"), os.path.join(ROOT, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+BATCH = 64
+METRIC = "images/sec (224², ViT-S+/16) at batch 64 on 1/2/4/8 B200; p50 batch-1 latency"
+UNIT = "images/s"
+GFLOP_PER_IMAGE = 12.2415
+GATEUP_GFLOP_B64 = 2 * 12864 * 384 * 3072 / 1e9  # 30.350 GFLOP per launch at batch 64
+GATEUP_BYTES_B64 = (12864 * 384 + 3072 * 384 + 12864 * 1536) * 2 + 3072 * 4  # algorithmic
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+WORKLOAD = "DINOv3 ViT-S+/16 forward, 224x224, batch 64 per GPU (config 2), fp16 weights/activations, fp32 accumulate"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--profile-iters", type=int, default=20)
+    ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def committed_traffic(kernel: str):
+    """dram read+write bytes per launch of `kernel` at batch 64 from the committed ncu summary
+    (lines `traffic_bytes_per_launch <kernel> <bytes>` in profiles/*.md), else None."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for name in sorted(os.listdir(pdir)):
+        if not name.endswith(".md"):
+            continue
+        for line in open(os.path.join(pdir, name)):
+            m = re.match(r"\s*traffic_bytes_per_launch\s+(\S+)\s+([0-9.eE+]+)", line)
+            if m and m.group(1) == kernel:
+                return float(m.group(2))
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples of one GPU during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device), "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_oracle_throughput(images, budget_s: float, threads: int | None = None):
+    """images/s of the float64 C oracle on this host; returns (value, cores, sample, step_times)."""
+    import numpy as np
+
+    import ref_c
+    from dinov3_b200 import synth
+
+    threads = threads or ref_c.max_threads()
+    model = ref_c.Model(synth.weights(0, "baseline"))
+    n = max(1, threads)
+    sample = np.ascontiguousarray(images[:n] if len(images) >= n else np.resize(images, (n,) + images.shape[1:]))
+    t0 = time.perf_counter()
+    model.forward(sample, threads=threads)
+    dt = time.perf_counter() - t0
+    return n / dt, threads, n, dt, model, sample
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    import ref_c
+    from dinov3_b200 import synth
+
+    threads = ref_c.max_threads()
+    images = synth.images(1000, threads)
+    model = ref_c.Model(synth.weights(0, "baseline"))
+    # One step = one float64 forward of `threads` images (one per thread), OpenMP over images.
+    t0 = time.perf_counter()
+    model.forward(images, threads=threads)
+    est = time.perf_counter() - t0
+    steps = max(1, min(args.steps, int(args.cpu_budget_s * 6 // max(est, 1e-3))))
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        model.forward(images, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        model.forward(images, threads=threads)
+    dt = time.perf_counter() - t0
+    value = threads * steps / dt
+    cpu = {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": f"{steps} steps x {threads} seeded 224x224 images (batch-64 workload sample), "
+                     f"float64 C oracle of tests/support/reference.rs, OpenMP over images "
+                     f"({steps} of the requested {args.steps} steps fit the CPU time budget)"}
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": 1000 * dt / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": BATCH * args.gpus, "batch_per_gpu": BATCH,
+                       "parallelism": f"replicas{args.gpus}"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "host": cpu_model()}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip() + f" x{os.cpu_count()}"
+    except Exception:
+        pass
+    return f"unknown x{os.cpu_count()}"
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import dinov3_b200 as dv
+    from dinov3_b200 import synth
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            t = torch.zeros(1, device="cuda")
+            dist.all_reduce(t)
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    wdir = tempfile.mkdtemp(prefix=f"dv3_bench_{rank}_")
+    wpath = synth.write_weights(os.path.join(wdir, "w.safetensors"), seed=0, flavor="baseline")
+    model = dv.DINOv3.load(wpath, dv.Options(local, BATCH))
+    images = synth.images(1000 + rank * BATCH, BATCH)
+    stream = torch.cuda.ExternalStream(model.stream, device=torch.device("cuda", local))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    n_img = BATCH * 3 * 224 * 224
+
+    class _Dev:
+        def __init__(self, ptr, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+    staged = torch.as_tensor(_Dev(model.input_buffer, n_img), device="cuda")
+    staged.copy_(torch.from_numpy(images).reshape(-1))
+    torch.cuda.synchronize()
+
+    # ---- device-resident throughput ----
+    launches = model.launches_per_forward(BATCH)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            model.run(BATCH)
+        model.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        barrier()
+        clocks = Clocks(local)
+        with clocks:
+            wall0 = time.perf_counter()
+            for s, e in ev:
+                flush.zero_()  # evict L2 between timed steps (outside the events)
+                s.record(stream)
+                model.run(BATCH)
+                e.record(stream)
+            model.synchronize()
+            wall = time.perf_counter() - wall0
+        barrier()
+    total_ms = sum(s.elapsed_time(e) for s, e in ev)
+    total_ms = max_over_ranks(total_ms)
+    value = world * BATCH * args.steps / (total_ms / 1000.0)
+
+    # ---- end to end through the public API (pinned host buffers) ----
+    pin_in = torch.from_numpy(images).pin_memory()
+    pin_out = torch.empty((BATCH, 201, 384), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 200))
+    for _ in range(max(3, args.warmup // 4)):
+        model.forward(pin_in, out=pin_out)
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(e2e_steps)]
+    barrier()
+    for s, e in ev2:
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        s.record(stream)
+        model.forward(pin_in, out=pin_out)
+        e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev2))
+    e2e_value = world * BATCH * e2e_steps / (e2e_ms / 1000.0)
+    assert np.isfinite(pin_out.numpy()).all()
+
+    # ---- batch-1 latency (p50), device-resident and end to end ----
+    lat_dev, lat_e2e = [], []
+    one_in = torch.from_numpy(images[:1]).pin_memory()
+    one_out = torch.empty((1, 201, 384), dtype=torch.float32).pin_memory()
+    for i in range(60):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        model.run(1)
+        e.record(stream)
+        model.synchronize()
+        t0 = time.perf_counter()
+        model.forward(one_in, out=one_out)
+        t1 = time.perf_counter()
+        if i >= 10:
+            lat_dev.append(s.elapsed_time(e))
+            lat_e2e.append((t1 - t0) * 1000)
+
+    # ---- dominant kernel roofline ----
+    prof = model.profile_launches(BATCH, args.profile_iters)
+    by_kernel = {}
+    for name, ms in prof:
+        by_kernel.setdefault(name, []).append(ms)
+    gate_ms = statistics.mean(by_kernel["gemm_gateup_swiglu"])
+    peaks, peak_src = load_peaks()
+    achieved = GATEUP_GFLOP_B64 / gate_ms  # GFLOP/ms == TFLOP/s
+    peak = peaks["bf16_tflops_sustained"]
+    kernel_share = {k: round(sum(v) / sum(ms for _, ms in prof), 4) for k, v in by_kernel.items()}
+
+    steps_launches = launches * args.steps
+    model.synchronize()
+    model.close()
+
+    cpu = None
+    if rank == 0 and world == 1:
+        value_cpu, cores, n, dt, _, _ = cpu_oracle_throughput(images, args.cpu_budget_s)
+        cpu = {"value": value_cpu, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{n} seeded 224x224 images of the batch-64 workload, float64 C oracle of "
+                         f"tests/support/reference.rs, OpenMP over images, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "batch_per_gpu": BATCH,
+                       "seq_len": 201, "parallelism": f"replicas{world}",
+                       "weights": "seeded random-init (baseline flavour: trunc-normal 0.02, biases 0, LN 1/0, LayerScale 0.1)",
+                       "l2": "flushed between timed steps (256 MiB memset)"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": BATCH * 3 * 224 * 224 * 4,
+                    "d2h_bytes_per_step": BATCH * 201 * 384 * 4 + 8},
+            "gpu_launches": steps_launches,
+            "roofline": {"kernel": "gemm_gateup_swiglu", "bound": "tensor", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+                         "traffic": committed_traffic("gemm_gateup_swiglu"),
+                         "algorithmic_bytes": GATEUP_BYTES_B64, "avg_launch_ms": gate_ms},
+            "cpu_baseline": cpu,
+            "p50_batch1_latency_ms": {"device": statistics.median(lat_dev), "e2e": statistics.median(lat_e2e)},
+            "tflops_whole_forward": value / world * GFLOP_PER_IMAGE / 1000.0,
+            "kernel_time_share": kernel_share,
+            "clocks": clocks.summary(),
+            "wall_s_timed_region": wall,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

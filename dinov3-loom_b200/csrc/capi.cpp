@@ -1,0 +1,288 @@
+// capi.cpp - the exported C ABI (include/dinov3.h, include/dinov3_kernels.h). Every entry point
+// converts C++ exceptions into a status code and a thread-local message.
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "dinov3.h"
+#include "dinov3_kernels.h"
+#include "kernels.h"
+#include "model.h"
+#include "weights.h"
+
+struct dv3_model {
+  dv3::Model impl;
+  dv3_model(const std::string &path, dv3_options o) : impl(path, o) {}
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &message) {
+  g_last_error = message;
+  return code;
+}
+
+template <class F>
+int guarded(F &&f) {
+  try {
+    f();
+    return DV3_OK;
+  } catch (const dv3::Error &e) {
+    return fail(e.code, e.what());
+  } catch (const std::bad_alloc &) {
+    return fail(DV3_DEVICE, "out of host memory");
+  } catch (const std::exception &e) {
+    return fail(DV3_DEVICE, e.what());
+  }
+}
+
+int check_model(dv3_model *m) {
+  if (!m) return fail(DV3_INVALID_ARGUMENT, "null model");
+  return DV3_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+dv3_options dv3_default_options(void) {
+  dv3_options o;
+  o.device = 0;
+  o.max_batch = 32;
+  return o;
+}
+
+int dv3_load(const char *path, dv3_options options, dv3_model **out) {
+  if (!out) return fail(DV3_INVALID_ARGUMENT, "null output handle");
+  *out = nullptr;
+  return guarded([&] {
+    if (options.max_batch < 1 || options.max_batch > DV3_MAX_BATCH_LIMIT)
+      throw dv3::Error(DV3_INVALID_ARGUMENT, "max_batch must be 1..=64");
+    if (!path) throw dv3::Error(DV3_INVALID_ARGUMENT, "null path");
+    *out = new dv3_model(path, options);
+  });
+}
+
+int dv3_forward(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] { m->impl.forward(pixels, n, out, out_n); });
+}
+
+int dv3_cls(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] {
+    if (n % DV3_IMAGE_ELEMENTS != 0)
+      throw dv3::Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
+    const size_t batch = n / DV3_IMAGE_ELEMENTS;
+    if (out_n < batch * DV3_HIDDEN)
+      throw dv3::Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * DV3_HIDDEN) + " floats");
+    std::vector<float> full(batch * DV3_TOKENS * DV3_HIDDEN);
+    m->impl.forward(pixels, n, full.data(), full.size());
+    for (size_t i = 0; i < batch; ++i)
+      std::memcpy(out + i * DV3_HIDDEN, full.data() + i * DV3_TOKENS * DV3_HIDDEN, DV3_HIDDEN * sizeof(float));
+  });
+}
+
+int dv3_patch_mean(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] {
+    if (n % DV3_IMAGE_ELEMENTS != 0)
+      throw dv3::Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
+    const size_t batch = n / DV3_IMAGE_ELEMENTS;
+    if (out_n < batch * DV3_HIDDEN)
+      throw dv3::Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * DV3_HIDDEN) + " floats");
+    std::vector<float> full(batch * DV3_TOKENS * DV3_HIDDEN);
+    m->impl.forward(pixels, n, full.data(), full.size());
+    // src/lib.rs:134-148: f32 accumulation of row / 196, rows 5..200 in order.
+    for (size_t i = 0; i < batch; ++i) {
+      float acc[DV3_HIDDEN] = {};
+      const float *img = full.data() + i * DV3_TOKENS * DV3_HIDDEN;
+      for (int t = 5; t < DV3_TOKENS; ++t)
+        for (int c = 0; c < DV3_HIDDEN; ++c) acc[c] += img[t * DV3_HIDDEN + c] / 196.0f;
+      std::memcpy(out + i * DV3_HIDDEN, acc, sizeof acc);
+    }
+  });
+}
+
+int dv3_benchmark(dv3_model *m, const float *pixels, size_t n, size_t samples, dv3_timings *out) {
+  if (int rc = check_model(m)) return rc;
+  if (!out) return fail(DV3_INVALID_ARGUMENT, "null timings");
+  return guarded([&] { *out = m->impl.benchmark(pixels, n, samples); });
+}
+
+void dv3_free(dv3_model *m) { delete m; }
+
+const char *dv3_last_error(void) { return g_last_error.c_str(); }
+
+float *dv3_input_buffer(dv3_model *m) { return m ? m->impl.input_buffer() : nullptr; }
+float *dv3_output_buffer(dv3_model *m) { return m ? m->impl.output_buffer() : nullptr; }
+void *dv3_stream(dv3_model *m) { return m ? static_cast<void *>(m->impl.stream()) : nullptr; }
+
+int dv3_run(dv3_model *m, size_t batch) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] { m->impl.run(batch); });
+}
+
+int dv3_synchronize(dv3_model *m) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] { m->impl.synchronize(); });
+}
+
+int dv3_forward_device(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] { m->impl.forward_device(pixels, n, out, out_n); });
+}
+
+int dv3_launches_per_forward(dv3_model *m, size_t batch, size_t *out) {
+  if (int rc = check_model(m)) return rc;
+  if (!out) return fail(DV3_INVALID_ARGUMENT, "null output");
+  return guarded([&] { *out = m->impl.launches_per_forward(batch); });
+}
+
+int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *ms,
+                         const char **names, size_t capacity, size_t *count) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] {
+    auto r = m->impl.profile_launches(batch, iterations);
+    for (size_t i = 0; i < r.size() && i < capacity; ++i) {
+      if (ms) ms[i] = r[i].second;
+      if (names) names[i] = r[i].first;
+    }
+    if (count) *count = r.size();
+  });
+}
+
+int dv3_pack_f16(const char *name, const float *values, size_t n, uint16_t *out, size_t *bad) {
+  if ((n && (!values || !out)) || !name) return fail(DV3_INVALID_ARGUMENT, "null argument");
+  std::string msg;
+  const size_t at = dv3::pack_f16(name, values, n, out, &msg);
+  if (bad) *bad = at;
+  if (at != SIZE_MAX) return fail(DV3_WEIGHTS, msg);
+  return DV3_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Per-kernel entry points
+// ------------------------------------------------------------------------------------------
+
+}  // extern "C"
+
+namespace {
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_status(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return DV3_OK;
+  cudaGetLastError();
+  return fail(DV3_DEVICE, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <class... P>
+bool all_aligned(P... p) {
+  return (aligned16(p) && ...);
+}
+
+int bad_args(const char *what) { return fail(DV3_INVALID_ARGUMENT, what); }
+
+int gemm_entry(dv3::GemmOp op, const void *a, uint32_t rows, const void *w,
+               const dv3::GemmArgs &args, uint32_t *status, void *stream) {
+  if (rows == 0) return DV3_OK;
+  dv3::GemmMaps maps;
+  std::string err;
+  if (!dv3::make_gemm_maps(op, a, rows, w, &maps, &err)) return bad_args(err.c_str());
+  return launch_status(dv3::launch_gemm(op, maps, rows, args, status, static_cast<cudaStream_t>(stream)),
+                       dv3::gemm_name(op));
+}
+
+}  // namespace
+
+extern "C" {
+
+int dv3k_patchify(const float *images, uint32_t n_images, const float *prefix, uint16_t *patches,
+                  uint16_t *x, uint32_t *status, void *stream) {
+  if (n_images == 0) return DV3_OK;
+  if (!all_aligned(images, prefix, patches, x)) return bad_args("pointers must be 16-byte aligned");
+  return launch_status(dv3::launch_patchify(images, n_images, prefix, reinterpret_cast<__half *>(patches),
+                                            reinterpret_cast<__half *>(x), status,
+                                            static_cast<cudaStream_t>(stream)),
+                       "patchify");
+}
+
+int dv3k_patch_embed(const uint16_t *patches, uint32_t n_patches, const uint16_t *w,
+                     const float *bias, uint16_t *x, uint32_t *status, void *stream) {
+  if (!all_aligned(patches, w, bias, x)) return bad_args("pointers must be 16-byte aligned");
+  if (n_patches % dv3::kPatches != 0) return bad_args("n_patches must be a multiple of 196");
+  dv3::GemmArgs g;
+  g.bias = bias;
+  g.out = reinterpret_cast<__half *>(x);
+  return gemm_entry(dv3::GemmOp::Patch, patches, n_patches, w, g, status, stream);
+}
+
+int dv3k_layernorm_f16(const uint16_t *x, uint32_t rows, const float *gamma, const float *beta,
+                       uint16_t *out, void *stream) {
+  if (!all_aligned(x, gamma, beta, out)) return bad_args("pointers must be 16-byte aligned");
+  return launch_status(dv3::launch_layernorm_f16(reinterpret_cast<const __half *>(x), rows, gamma, beta,
+                                                 reinterpret_cast<__half *>(out),
+                                                 static_cast<cudaStream_t>(stream)),
+                       "layernorm_f16");
+}
+
+int dv3k_layernorm_f32out(const uint16_t *x, uint32_t rows, const float *gamma, const float *beta,
+                          float *out, void *stream) {
+  if (!all_aligned(x, gamma, beta, out)) return bad_args("pointers must be 16-byte aligned");
+  return launch_status(dv3::launch_layernorm_f32(reinterpret_cast<const __half *>(x), rows, gamma, beta,
+                                                 out, static_cast<cudaStream_t>(stream)),
+                       "layernorm_f32out");
+}
+
+int dv3k_qkv_rope(const uint16_t *h, uint32_t rows, const uint16_t *w, const float *bias,
+                  const float *rope_cos, const float *rope_sin, uint16_t *qkv, uint32_t *status,
+                  void *stream) {
+  if (!all_aligned(h, w, bias, rope_cos, rope_sin, qkv)) return bad_args("pointers must be 16-byte aligned");
+  dv3::GemmArgs g;
+  g.bias = bias;
+  g.rope_cos = rope_cos;
+  g.rope_sin = rope_sin;
+  g.out = reinterpret_cast<__half *>(qkv);
+  return gemm_entry(dv3::GemmOp::QkvRope, h, rows, w, g, status, stream);
+}
+
+int dv3k_attention(const uint16_t *qkv, uint32_t rows, uint16_t *out, uint32_t *status, void *stream) {
+  if (rows == 0) return DV3_OK;
+  if (!all_aligned(qkv, out)) return bad_args("pointers must be 16-byte aligned");
+  if (rows % dv3::kTokens != 0) return bad_args("rows must be a multiple of 201");
+  CUtensorMap map;
+  std::string err;
+  if (!dv3::make_attention_map(qkv, rows, &map, &err)) return bad_args(err.c_str());
+  return launch_status(dv3::launch_attention(map, rows, reinterpret_cast<__half *>(out), status,
+                                             static_cast<cudaStream_t>(stream)),
+                       "attention");
+}
+
+int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
+                      const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
+                      void *stream) {
+  if (!all_aligned(a, w, bias, lambda, x)) return bad_args("pointers must be 16-byte aligned");
+  if (k != 384 && k != 1536) return bad_args("k must be 384 or 1536");
+  dv3::GemmArgs g;
+  g.bias = bias;
+  g.lambda = lambda;
+  g.out = reinterpret_cast<__half *>(x);
+  return gemm_entry(k == 384 ? dv3::GemmOp::Resid384 : dv3::GemmOp::Resid1536, a, rows, w, g, status,
+                    stream);
+}
+
+int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_w,
+                       const float *gateup_b, uint16_t *act, uint32_t *status, void *stream) {
+  if (!all_aligned(h, gateup_w, gateup_b, act)) return bad_args("pointers must be 16-byte aligned");
+  dv3::GemmArgs g;
+  g.bias = gateup_b;
+  g.out = reinterpret_cast<__half *>(act);
+  return gemm_entry(dv3::GemmOp::SwiGLU, h, rows, gateup_w, g, status, stream);
+}
+
+uint32_t dv3k_gateup_source_row(uint32_t packed_row) { return dv3::gateup_source_row(packed_row); }
+
+}  // extern "C"

@@ -1,0 +1,161 @@
+// elementwise.cu - the HBM-bound kernels of the forward.
+//
+// patchify: normalised NCHW f32 images -> patch rows [p][768] f16 in (c, dy, dx) order (the
+//   host loop of src/lib.rs:265-280 moved onto the device), plus the CLS/register prefix rows of
+//   the residual stream (the prefix half of kernels/embed_scatter_f32.loom). One thread moves 8
+//   pixels: two 16-byte loads of a 32-byte run of one image row, one 16-byte store. It also
+//   flags any non-finite pixel (the check of src/lib.rs:95), so the host never scans the input.
+//
+// layernorm: one warp per 384-channel row (kernels/layernorm_rowwave_f16.loom and _f32out).
+//   Lane l holds channels 8l..8l+7 (one 16-byte load) and 256+4l..256+4l+3 (one 8-byte load):
+//   both loads are contiguous across the warp. Mean and variance are reduced with shuffles in
+//   two passes over the registers (the reference's E[x^2]-mean^2 is replaced by the better
+//   conditioned centred sum), eps 1e-5, f32 arithmetic.
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace dv3 {
+
+__global__ void __launch_bounds__(256)
+    patchify_kernel(const float *__restrict__ images, int n_images,
+                    const float *__restrict__ prefix, __half *__restrict__ patches,
+                    __half *__restrict__ x, uint32_t *status) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n_patch_chunks = static_cast<int64_t>(n_images) * kPatches * 96;
+  const int64_t n_prefix_chunks = static_cast<int64_t>(n_images) * kPrefix * 48;
+  bool bad = false;
+  if (i < n_patch_chunks) {
+    const int chunk = static_cast<int>(i % 96);  // 8-element chunk of the 768-wide patch row
+    const int64_t prow = i / 96;
+    const int img = static_cast<int>(prow / kPatches);
+    const int p = static_cast<int>(prow % kPatches);
+    const int gy = p / 14, gx = p % 14;
+    const int c = chunk / 32, dy = (chunk / 2) % 16, dx0 = (chunk % 2) * 8;
+    const float *src = images + (static_cast<int64_t>(img) * 3 + c) * 224 * 224 +
+                       (gy * 16 + dy) * 224 + gx * 16 + dx0;
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(src));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(src) + 1);
+    bad = !(isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w) && isfinite(b.x) &&
+            isfinite(b.y) && isfinite(b.z) && isfinite(b.w));
+    const uint4 v = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
+                               pack_half2(b.z, b.w));
+    *reinterpret_cast<uint4 *>(patches + prow * kPatchK + chunk * 8) = v;
+  } else if (i < n_patch_chunks + n_prefix_chunks) {
+    const int64_t j = i - n_patch_chunks;
+    const int chunk = static_cast<int>(j % 48);
+    const int t = static_cast<int>((j / 48) % kPrefix);
+    const int64_t img = j / (48 * kPrefix);
+    const float4 *src = reinterpret_cast<const float4 *>(prefix + t * kHidden + chunk * 8);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    const uint4 v = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
+                               pack_half2(b.z, b.w));
+    *reinterpret_cast<uint4 *>(x + (img * kTokens + t) * kHidden + chunk * 8) = v;
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x % 32) == 0 && status)
+    atomicOr(status + 1, 1u);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <bool kF32Out>
+__global__ void __launch_bounds__(256)
+    layernorm_kernel(const __half *__restrict__ x, int rows, const float *__restrict__ gamma,
+                     const float *__restrict__ beta, void *__restrict__ out) {
+  const int row = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;  // whole warp leaves together
+  const __half *xr = x + static_cast<int64_t>(row) * kHidden;
+  const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xr) + lane);
+  const uint2 b = __ldg(reinterpret_cast<const uint2 *>(xr + 256) + lane);
+  float v[12];
+  {
+    const uint32_t w[6] = {a.x, a.y, a.z, a.w, b.x, b.y};
+#pragma unroll
+    for (int e = 0; e < 6; ++e) {
+      const float2 f = unpack_half2(w[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 12; ++e) s += v[e];
+  const float mean = warp_sum(s) * (1.0f / kHidden);
+  float d = 0.f;
+#pragma unroll
+  for (int e = 0; e < 12; ++e) {
+    v[e] -= mean;
+    d += v[e] * v[e];
+  }
+  const float rstd = rsqrtf(warp_sum(d) * (1.0f / kHidden) + 1e-5f);
+  const int c0 = lane * 8, c1 = 256 + lane * 4;
+  float y[12];
+  {
+    const float4 g0 = __ldg(reinterpret_cast<const float4 *>(gamma + c0));
+    const float4 g1 = __ldg(reinterpret_cast<const float4 *>(gamma + c0) + 1);
+    const float4 g2 = __ldg(reinterpret_cast<const float4 *>(gamma + c1));
+    const float4 b0 = __ldg(reinterpret_cast<const float4 *>(beta + c0));
+    const float4 b1 = __ldg(reinterpret_cast<const float4 *>(beta + c0) + 1);
+    const float4 b2 = __ldg(reinterpret_cast<const float4 *>(beta + c1));
+    const float g[12] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w, g2.x, g2.y, g2.z, g2.w};
+    const float bb[12] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w, b2.x, b2.y, b2.z, b2.w};
+#pragma unroll
+    for (int e = 0; e < 12; ++e) y[e] = v[e] * rstd * g[e] + bb[e];
+  }
+  if constexpr (kF32Out) {
+    float *o = static_cast<float *>(out) + static_cast<int64_t>(row) * kHidden;
+    reinterpret_cast<float4 *>(o + c0)[0] = make_float4(y[0], y[1], y[2], y[3]);
+    reinterpret_cast<float4 *>(o + c0)[1] = make_float4(y[4], y[5], y[6], y[7]);
+    reinterpret_cast<float4 *>(o + c1)[0] = make_float4(y[8], y[9], y[10], y[11]);
+  } else {
+    __half *o = static_cast<__half *>(out) + static_cast<int64_t>(row) * kHidden;
+    reinterpret_cast<uint4 *>(o + c0)[0] =
+        make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]), pack_half2(y[4], y[5]),
+                   pack_half2(y[6], y[7]));
+    reinterpret_cast<uint2 *>(o + c1)[0] = make_uint2(pack_half2(y[8], y[9]), pack_half2(y[10], y[11]));
+  }
+}
+
+cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,
+                            __half *patches, __half *x, uint32_t *status, cudaStream_t stream) {
+  if (n_images == 0) return cudaSuccess;
+  const int64_t total = static_cast<int64_t>(n_images) * (kPatches * 96 + kPrefix * 48);
+  const int blocks = static_cast<int>((total + 255) / 256);
+  patchify_kernel<<<blocks, 256, 0, stream>>>(images, static_cast<int>(n_images), prefix, patches,
+                                              x, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *gamma,
+                                 const float *beta, __half *out, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  layernorm_kernel<false><<<(rows + 7) / 8, 256, 0, stream>>>(x, static_cast<int>(rows), gamma,
+                                                              beta, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
+                                 const float *beta, float *out, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  layernorm_kernel<true><<<(rows + 7) / 8, 256, 0, stream>>>(x, static_cast<int>(rows), gamma,
+                                                             beta, out);
+  return cudaGetLastError();
+}
+
+int sm_count(int device) {
+  static int cache[64] = {};
+  if (device < 0 || device >= 64) return 148;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+}  // namespace dv3

@@ -1,0 +1,81 @@
+// kernels.h - internal C++ interface of the sm_100a kernels (used by the model engine and by
+// the per-kernel C ABI in capi.cpp). All launches are asynchronous on the given stream.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace dv3 {
+
+constexpr int kTokens = 201;
+constexpr int kPatches = 196;
+constexpr int kPrefix = 5;
+constexpr int kHidden = 384;
+constexpr int kQkv = 1152;
+constexpr int kMlp = 1536;
+constexpr int kGateUp = 3072;
+constexpr int kPatchK = 768;
+constexpr int kImageElements = 3 * 224 * 224;
+
+// ---- tensor maps (tma.cpp) ----
+// 2D f16 tensor [rows][cols] (row-major, `cols` contiguous), box = box_cols x box_rows, 128-byte
+// swizzle (box_cols must be 64), out-of-bounds elements read as zero.
+bool encode_map_f16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                    uint32_t box_cols, uint32_t box_rows, std::string *err);
+
+// ---- GEMM operations (gemm.cu) ----
+enum class GemmOp { Patch, QkvRope, Resid384, Resid1536, SwiGLU };
+
+struct GemmShape {
+  int bn;      // tile width along N
+  int n;       // output width of the GEMM
+  int k;       // reduction length
+};
+GemmShape gemm_shape(GemmOp op);
+
+// Tensor maps of one GEMM launch: A = activations [rows][k], B = weights [n][k].
+struct GemmMaps {
+  CUtensorMap a;
+  CUtensorMap b;
+};
+bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, GemmMaps *maps,
+                    std::string *err);
+
+struct GemmArgs {
+  const float *bias = nullptr;
+  const float *lambda = nullptr;    // Resid*
+  const float *rope_cos = nullptr;  // QkvRope
+  const float *rope_sin = nullptr;
+  __half *out = nullptr;  // Patch: x; QkvRope: qkv; Resid*: x (in place); SwiGLU: act
+};
+
+cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const GemmArgs &args,
+                        uint32_t *status, cudaStream_t stream);
+const char *gemm_name(GemmOp op);
+
+// ---- attention (attention.cu) ----
+bool make_attention_map(const void *qkv, uint32_t rows, CUtensorMap *map, std::string *err);
+cudaError_t launch_attention(const CUtensorMap &map, uint32_t rows, __half *out, uint32_t *status,
+                             cudaStream_t stream);
+
+// ---- bandwidth kernels (elementwise.cu) ----
+cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,
+                            __half *patches, __half *x, uint32_t *status, cudaStream_t stream);
+cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *gamma,
+                                 const float *beta, __half *out, cudaStream_t stream);
+cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
+                                 const float *beta, float *out, cudaStream_t stream);
+
+// Packed gate/up row order: 64 gate rows, the matching 64 up rows, then the next 64 of each.
+inline uint32_t gateup_source_row(uint32_t packed) {
+  const uint32_t block = packed / 128, within = packed % 128;
+  return within < 64 ? block * 64 + within : kMlp + block * 64 + (within - 64);
+}
+
+int sm_count(int device);
+
+}  // namespace dv3

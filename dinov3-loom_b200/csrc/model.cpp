@@ -1,0 +1,451 @@
+// model.cpp - the resident model: load (src/lib.rs:49-88), the launch plan (src/lib.rs:149-263),
+// one CUDA graph per batch size (src/engine.rs:87-129), forward with chunking
+// (src/lib.rs:90-114), and the graph-vs-direct benchmark (src/engine.rs:130-190).
+//
+// Device memory: one allocation holds every packed weight (f16 matrices, f32 vectors, 256-byte
+// aligned), one holds the activations sized for max_batch images:
+//   image   f32 [B][3][224][224]   the staged input
+//   patches f16 [196B][768]        patchified input (A operand of the patch GEMM)
+//   x       f16 [201B][384]        residual stream
+//   h       f16 [201B][384]        LayerNorm output
+//   qkv     f16 [201B][1152]       q | k | v (RoPE applied)
+//   attn    f16 [201B][384]        attention output
+//   act     f16 [201B][1536]       SwiGLU output
+//   out     f32 [201B][384]        final LayerNorm output
+//   status  u32 [2]                device failure bits, non-finite input flag (sticky until read)
+// The QKV buffer needs no headroom rows: attention reads through TMA, whose out-of-bounds rows
+// are zero.
+#include "model.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+
+#include "weights.h"
+
+namespace dv3 {
+
+cudaError_t configure_gemm_kernels();
+cudaError_t configure_attention_kernel();
+
+namespace {
+size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+}  // namespace
+
+void Model::activate() const { cudaSetDevice(device_); }
+
+void Model::cuda(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return;
+  failed_ = true;
+  cudaGetLastError();  // clear a non-sticky error so later host calls report afresh
+  throw Error(DV3_DEVICE, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void Model::check_usable() const {
+  if (failed_) throw Error(DV3_POISONED, "session is unusable after a GPU failure");
+}
+
+Model::Model(const std::string &path, dv3_options options)
+    : device_(options.device), max_batch_(options.max_batch) {
+  // Options first, before any file access (tests/model.rs:5-27).
+  if (options.max_batch < 1 || options.max_batch > DV3_MAX_BATCH_LIMIT)
+    throw Error(DV3_INVALID_ARGUMENT, "max_batch must be 1..=64");
+  // Weights next, before any GPU initialisation (tests/model.rs:29-59).
+  std::map<std::string, Packed> packed;
+  try {
+    packed = load_weights(path);
+  } catch (const WeightsError &e) {
+    throw Error(DV3_WEIGHTS, e.what());
+  }
+  // Engine::new (src/engine.rs:40-46): the kernels are built for sm_100a only.
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    throw Error(DV3_DEVICE, "no CUDA device is available");
+  }
+  if (device_ < 0 || device_ >= count)
+    throw Error(DV3_DEVICE, "CUDA device " + std::to_string(device_) + " does not exist");
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device_) != cudaSuccess)
+    throw Error(DV3_DEVICE, "cannot query CUDA device " + std::to_string(device_));
+  if (prop.major != 10 || prop.minor != 0)
+    throw Error(DV3_DEVICE, "these kernels are built for sm_100 (B200), found sm_" +
+                                std::to_string(prop.major) + std::to_string(prop.minor));
+  activate();
+  try {
+    cuda(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "create stream");
+    cuda(configure_gemm_kernels(), "configure GEMM kernels");
+    cuda(configure_attention_kernel(), "configure attention kernel");
+
+    // Weights: one blob, every tensor 256-byte aligned.
+    std::map<std::string, size_t> offset;
+    size_t total = 0;
+    for (auto &kv : packed) {
+      offset[kv.first] = total;
+      total += align256(kv.second.bytes());
+    }
+    std::vector<uint8_t> host(total, 0);
+    for (auto &kv : packed) std::memcpy(host.data() + offset[kv.first], kv.second.data(), kv.second.bytes());
+    cuda(cudaMalloc(&weight_blob_, total), "allocate weights");
+    cuda(cudaMemcpy(weight_blob_, host.data(), total, cudaMemcpyHostToDevice), "upload weights");
+    auto hp = [&](const std::string &n) {
+      return reinterpret_cast<const __half *>(static_cast<uint8_t *>(weight_blob_) + offset.at(n));
+    };
+    auto fp = [&](const std::string &n) {
+      return reinterpret_cast<const float *>(static_cast<uint8_t *>(weight_blob_) + offset.at(n));
+    };
+    w_.patch_w = hp("patch_w");
+    w_.patch_b = fp("patch_b");
+    w_.prefix = fp("prefix");
+    w_.norm_w = fp("norm_w");
+    w_.norm_b = fp("norm_b");
+    w_.rope_cos = fp("rope_cos");
+    w_.rope_sin = fp("rope_sin");
+    for (int i = 0; i < 12; ++i) {
+      const std::string s = "l" + std::to_string(i) + "_";
+      LayerWeights &l = w_.layer[i];
+      l.qkv_w = hp(s + "qkv_w");
+      l.gateup_w = hp(s + "gateup_w");
+      l.o_w = hp(s + "o_w");
+      l.down_w = hp(s + "down_w");
+      l.qkv_b = fp(s + "qkv_b");
+      l.gateup_b = fp(s + "gateup_b");
+      l.o_b = fp(s + "o_b");
+      l.down_b = fp(s + "down_b");
+      l.norm1_w = fp(s + "norm1_w");
+      l.norm1_b = fp(s + "norm1_b");
+      l.norm2_w = fp(s + "norm2_w");
+      l.norm2_b = fp(s + "norm2_b");
+      l.ls1 = fp(s + "ls1");
+      l.ls2 = fp(s + "ls2");
+    }
+
+    // Activations for max_batch images.
+    const size_t B = max_batch_, R = kTokens * B, P = kPatches * B;
+    const size_t sizes[9] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
+                             R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
+                             R * kMlp * 2,           R * kHidden * 4, 256};
+    size_t at[9], act_total = 0;
+    for (int i = 0; i < 9; ++i) {
+      at[i] = act_total;
+      act_total += align256(sizes[i]);
+    }
+    cuda(cudaMalloc(&act_blob_, act_total), "allocate activations");
+    uint8_t *a = static_cast<uint8_t *>(act_blob_);
+    image_ = reinterpret_cast<float *>(a + at[0]);
+    patches_ = reinterpret_cast<__half *>(a + at[1]);
+    x_ = reinterpret_cast<__half *>(a + at[2]);
+    h_ = reinterpret_cast<__half *>(a + at[3]);
+    qkv_ = reinterpret_cast<__half *>(a + at[4]);
+    attn_ = reinterpret_cast<__half *>(a + at[5]);
+    act_ = reinterpret_cast<__half *>(a + at[6]);
+    out_ = reinterpret_cast<float *>(a + at[7]);
+    status_ = reinterpret_cast<uint32_t *>(a + at[8]);
+    cuda(cudaMemset(status_, 0, 256), "clear status");
+    cuda(cudaMallocHost(reinterpret_cast<void **>(&status_host_), 2 * sizeof(uint32_t)),
+         "allocate pinned status");
+    status_host_[0] = status_host_[1] = 0;
+  } catch (...) {
+    release();
+    throw;
+  }
+}
+
+Model::~Model() { release(); }
+
+void Model::release() {
+  cudaSetDevice(device_);
+  for (auto &kv : plans_)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+  plans_.clear();
+  if (stream_) cudaStreamSynchronize(stream_);
+  if (status_host_) cudaFreeHost(status_host_);
+  if (act_blob_) cudaFree(act_blob_);
+  if (weight_blob_) cudaFree(weight_blob_);
+  if (stream_) cudaStreamDestroy(stream_);
+  status_host_ = nullptr;
+  act_blob_ = weight_blob_ = nullptr;
+  stream_ = nullptr;
+  cudaGetLastError();
+}
+
+// The launch plan of one batch size (src/lib.rs:149-263): patchify, patch GEMM (with the
+// embed scatter), LN1 of layer 0, then per layer QKV+RoPE, attention, o-proj+LS1+residual,
+// LN2, gate/up+SwiGLU, down-proj+LS2+residual, and LN1 of the next layer or the final LN.
+Plan &Model::prepare(size_t b) {
+  auto it = plans_.find(b);
+  if (it != plans_.end()) return it->second;
+  const uint32_t r = static_cast<uint32_t>(kTokens * b), p = static_cast<uint32_t>(kPatches * b);
+  std::string err;
+  auto need = [&](bool ok) {
+    if (!ok) {
+      failed_ = true;
+      throw Error(DV3_DEVICE, "tensor map: " + err);
+    }
+  };
+  Plan plan;
+  auto add = [&](const char *name, std::function<cudaError_t(cudaStream_t)> f) {
+    plan.launches.push_back({name, true, std::move(f)});
+    ++plan.kernels;
+  };
+  uint32_t *st = status_;
+  const DeviceWeights w = w_;
+  float *image = image_, *out = out_;
+  __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
+
+  GemmMaps patch_maps;
+  need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, &patch_maps, &err));
+  CUtensorMap attn_map;
+  need(make_attention_map(qkv, r, &attn_map, &err));
+
+  add("patchify", [=](cudaStream_t s) {
+    return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s);
+  });
+  add(gemm_name(GemmOp::Patch), [=](cudaStream_t s) {
+    GemmArgs g;
+    g.bias = w.patch_b;
+    g.out = x;
+    return launch_gemm(GemmOp::Patch, patch_maps, p, g, st, s);
+  });
+  add("layernorm_f16", [=](cudaStream_t s) {
+    return launch_layernorm_f16(x, r, w.layer[0].norm1_w, w.layer[0].norm1_b, h, s);
+  });
+  for (int i = 0; i < 12; ++i) {
+    const LayerWeights &l = w.layer[i];
+    GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
+    need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, &qkv_maps, &err));
+    need(make_gemm_maps(GemmOp::Resid384, attn, r, l.o_w, &o_maps, &err));
+    need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, &gu_maps, &err));
+    need(make_gemm_maps(GemmOp::Resid1536, act, r, l.down_w, &down_maps, &err));
+    add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
+      GemmArgs g;
+      g.bias = l.qkv_b;
+      g.rope_cos = w.rope_cos;
+      g.rope_sin = w.rope_sin;
+      g.out = qkv;
+      return launch_gemm(GemmOp::QkvRope, qkv_maps, r, g, st, s);
+    });
+    add("attention", [=](cudaStream_t s) { return launch_attention(attn_map, r, attn, st, s); });
+    add(gemm_name(GemmOp::Resid384), [=](cudaStream_t s) {
+      GemmArgs g;
+      g.bias = l.o_b;
+      g.lambda = l.ls1;
+      g.out = x;
+      return launch_gemm(GemmOp::Resid384, o_maps, r, g, st, s);
+    });
+    add("layernorm_f16", [=](cudaStream_t s) {
+      return launch_layernorm_f16(x, r, l.norm2_w, l.norm2_b, h, s);
+    });
+    add(gemm_name(GemmOp::SwiGLU), [=](cudaStream_t s) {
+      GemmArgs g;
+      g.bias = l.gateup_b;
+      g.out = act;
+      return launch_gemm(GemmOp::SwiGLU, gu_maps, r, g, st, s);
+    });
+    add(gemm_name(GemmOp::Resid1536), [=](cudaStream_t s) {
+      GemmArgs g;
+      g.bias = l.down_b;
+      g.lambda = l.ls2;
+      g.out = x;
+      return launch_gemm(GemmOp::Resid1536, down_maps, r, g, st, s);
+    });
+    if (i < 11) {
+      const LayerWeights &n = w.layer[i + 1];
+      add("layernorm_f16", [=](cudaStream_t s) {
+        return launch_layernorm_f16(x, r, n.norm1_w, n.norm1_b, h, s);
+      });
+    } else {
+      add("layernorm_f32out", [=](cudaStream_t s) {
+        return launch_layernorm_f32(x, r, w.norm_w, w.norm_b, out, s);
+      });
+    }
+  }
+
+  // Record the plan as one CUDA graph (the HRX execution graph of src/engine.rs:87-129).
+  cudaGraph_t graph = nullptr;
+  cuda(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+  for (auto &l : plan.launches) {
+    cudaError_t e = l.enqueue(stream_);
+    if (e != cudaSuccess) {
+      cudaStreamEndCapture(stream_, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      cuda(e, l.name);
+    }
+  }
+  cuda(cudaStreamEndCapture(stream_, &graph), "end capture");
+  cudaError_t e = cudaGraphInstantiate(&plan.exec, graph, 0);
+  cudaGraphDestroy(graph);
+  cuda(e, "instantiate graph");
+  return plans_.emplace(b, std::move(plan)).first->second;
+}
+
+void Model::check_status() {
+  cuda(cudaMemcpyAsync(status_host_, status_, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_),
+       "read status");
+  cuda(cudaStreamSynchronize(stream_), "synchronize");
+  status_pending_ = false;
+  const uint32_t fault = status_host_[0], nonfinite = status_host_[1];
+  if (fault || nonfinite) {
+    cuda(cudaMemsetAsync(status_, 0, 2 * sizeof(uint32_t), stream_), "clear status");
+    status_host_[0] = status_host_[1] = 0;
+  }
+  if (fault) {
+    failed_ = true;
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "a kernel wait expired (device status 0x%x)", fault);
+    throw Error(DV3_POISONED, std::string(buf) + "; session is unusable after a GPU failure");
+  }
+  if (nonfinite) throw Error(DV3_INVALID_ARGUMENT, "input must be finite");
+}
+
+void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out_floats) {
+  if (n_floats % kImageElements != 0)
+    throw Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
+  const size_t batch = n_floats / kImageElements;
+  const size_t per = static_cast<size_t>(kTokens) * kHidden;
+  if (out_floats < batch * per)
+    throw Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * per) + " floats");
+  if (batch && (!pixels || !out)) throw Error(DV3_INVALID_ARGUMENT, "null buffer");
+  activate();
+  for (size_t i = 0; i < batch; i += max_batch_) {
+    check_usable();
+    const size_t b = std::min(max_batch_, batch - i);
+    Plan &plan = prepare(b);
+    cuda(cudaMemcpyAsync(image_, pixels + i * kImageElements, b * kImageElements * sizeof(float),
+                         cudaMemcpyHostToDevice, stream_),
+         "upload input");
+    cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+    cuda(cudaMemcpyAsync(out + i * per, out_, b * per * sizeof(float), cudaMemcpyDeviceToHost, stream_),
+         "read output");
+    status_pending_ = true;
+    check_status();
+  }
+}
+
+void Model::forward_device(const float *pixels, size_t n_floats, float *out, size_t out_floats) {
+  if (n_floats % kImageElements != 0)
+    throw Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
+  const size_t batch = n_floats / kImageElements;
+  const size_t per = static_cast<size_t>(kTokens) * kHidden;
+  if (out_floats < batch * per)
+    throw Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * per) + " floats");
+  if (batch && (!pixels || !out)) throw Error(DV3_INVALID_ARGUMENT, "null buffer");
+  activate();
+  for (size_t i = 0; i < batch; i += max_batch_) {
+    check_usable();
+    const size_t b = std::min(max_batch_, batch - i);
+    Plan &plan = prepare(b);
+    cuda(cudaMemcpyAsync(image_, pixels + i * kImageElements, b * kImageElements * sizeof(float),
+                         cudaMemcpyDeviceToDevice, stream_),
+         "copy input");
+    cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+    cuda(cudaMemcpyAsync(out + i * per, out_, b * per * sizeof(float), cudaMemcpyDeviceToDevice, stream_),
+         "copy output");
+    status_pending_ = true;
+  }
+  if (batch) check_status();
+}
+
+void Model::run(size_t batch) {
+  check_usable();
+  if (batch < 1 || batch > max_batch_)
+    throw Error(DV3_INVALID_ARGUMENT, "batch must be 1..=max_batch");
+  activate();
+  Plan &plan = prepare(batch);
+  cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+  status_pending_ = true;
+}
+
+void Model::synchronize() {
+  check_usable();
+  activate();
+  check_status();
+}
+
+size_t Model::launches_per_forward(size_t batch) {
+  check_usable();
+  if (batch < 1 || batch > max_batch_)
+    throw Error(DV3_INVALID_ARGUMENT, "batch must be 1..=max_batch");
+  activate();
+  return prepare(batch).kernels;
+}
+
+dv3_timings Model::benchmark(const float *pixels, size_t n_floats, size_t samples) {
+  if (n_floats == 0 || n_floats > max_batch_ * kImageElements)
+    throw Error(DV3_INVALID_ARGUMENT, "benchmark requires one nonempty batch");
+  std::vector<float> first(n_floats / kImageElements * kTokens * kHidden);
+  forward(pixels, n_floats, first.data(), first.size());
+  if (samples < 10) throw Error(DV3_INVALID_ARGUMENT, "use at least ten timing samples");
+  check_usable();
+  const size_t b = n_floats / kImageElements;
+  Plan &plan = prepare(b);
+  std::vector<double> times[2];
+  for (size_t i = 0; i < samples + 10; ++i) {
+    const int order[2] = {static_cast<int>(i % 2), static_cast<int>(1 - i % 2)};
+    for (int mode : order) {
+      const auto t0 = std::chrono::steady_clock::now();
+      if (mode == 0) {
+        cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+      } else {
+        for (auto &l : plan.launches) cuda(l.enqueue(stream_), l.name);
+      }
+      cuda(cudaStreamSynchronize(stream_), "synchronize");
+      const auto t1 = std::chrono::steady_clock::now();
+      if (i >= 10) times[mode].push_back(std::chrono::duration<double, std::milli>(t1 - t0).count());
+    }
+  }
+  check_status();
+  auto summarize = [](std::vector<double> t) {
+    std::sort(t.begin(), t.end());
+    dv3_distribution d;
+    d.median_ms = t[t.size() / 2];
+    d.p95_ms = t[(t.size() * 95 + 99) / 100 - 1];
+    return d;
+  };
+  dv3_timings out;
+  out.samples = samples;
+  out.graph = summarize(times[0]);
+  out.direct = summarize(times[1]);
+  return out;
+}
+
+std::vector<std::pair<const char *, double>> Model::profile_launches(size_t batch,
+                                                                     size_t iterations) {
+  check_usable();
+  if (batch < 1 || batch > max_batch_)
+    throw Error(DV3_INVALID_ARGUMENT, "batch must be 1..=max_batch");
+  if (iterations < 1) throw Error(DV3_INVALID_ARGUMENT, "iterations must be >= 1");
+  activate();
+  Plan &plan = prepare(batch);
+  const size_t n = plan.launches.size();
+  std::vector<cudaEvent_t> ev(2 * n);
+  for (auto &e : ev) cuda(cudaEventCreate(&e), "create event");
+  std::vector<double> total(n, 0.0);
+  try {
+    for (size_t it = 0; it < iterations + 3; ++it) {
+      for (size_t j = 0; j < n; ++j) {
+        cuda(cudaEventRecord(ev[2 * j], stream_), "record event");
+        cuda(plan.launches[j].enqueue(stream_), plan.launches[j].name);
+        cuda(cudaEventRecord(ev[2 * j + 1], stream_), "record event");
+      }
+      cuda(cudaStreamSynchronize(stream_), "synchronize");
+      if (it >= 3)
+        for (size_t j = 0; j < n; ++j) {
+          float ms = 0;
+          cuda(cudaEventElapsedTime(&ms, ev[2 * j], ev[2 * j + 1]), "elapsed time");
+          total[j] += ms;
+        }
+    }
+  } catch (...) {
+    for (auto &e : ev) cudaEventDestroy(e);
+    throw;
+  }
+  for (auto &e : ev) cudaEventDestroy(e);
+  check_status();
+  std::vector<std::pair<const char *, double>> result;
+  for (size_t j = 0; j < n; ++j)
+    result.emplace_back(plan.launches[j].name, total[j] / static_cast<double>(iterations));
+  return result;
+}
+
+}  // namespace dv3

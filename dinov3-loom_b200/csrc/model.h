@@ -1,0 +1,94 @@
+// model.h - the resident model: mirrors DINOv3 (src/lib.rs) and Engine (src/engine.rs).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "dinov3.h"
+#include "kernels.h"
+
+namespace dv3 {
+
+// An error with the C ABI status it maps to.
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+struct LayerWeights {
+  const __half *qkv_w, *gateup_w, *o_w, *down_w;
+  const float *qkv_b, *gateup_b, *o_b, *down_b;
+  const float *norm1_w, *norm1_b, *norm2_w, *norm2_b, *ls1, *ls2;
+};
+
+struct DeviceWeights {
+  const __half *patch_w;
+  const float *patch_b, *prefix, *norm_w, *norm_b, *rope_cos, *rope_sin;
+  LayerWeights layer[12];
+};
+
+// One step of the launch plan (src/engine.rs:21-27): a named closure that enqueues one kernel
+// (or, for the status clear, one memset) on a stream.
+struct Launch {
+  const char *name;
+  bool kernel;
+  std::function<cudaError_t(cudaStream_t)> enqueue;
+};
+
+struct Plan {
+  std::vector<Launch> launches;
+  cudaGraphExec_t exec = nullptr;
+  size_t kernels = 0;
+};
+
+class Model {
+ public:
+  Model(const std::string &path, dv3_options options);
+  ~Model();
+  Model(const Model &) = delete;
+  Model &operator=(const Model &) = delete;
+
+  void forward(const float *pixels, size_t n_floats, float *out, size_t out_floats);
+  void forward_device(const float *pixels, size_t n_floats, float *out, size_t out_floats);
+  void run(size_t batch);
+  void synchronize();
+  dv3_timings benchmark(const float *pixels, size_t n_floats, size_t samples);
+  size_t launches_per_forward(size_t batch);
+  std::vector<std::pair<const char *, double>> profile_launches(size_t batch, size_t iterations);
+
+  float *input_buffer() const { return image_; }
+  float *output_buffer() const { return out_; }
+  cudaStream_t stream() const { return stream_; }
+  size_t max_batch() const { return max_batch_; }
+
+ private:
+  void check_usable() const;
+  void cuda(cudaError_t e, const char *what);  // poisons and throws on failure
+  Plan &prepare(size_t batch);                  // build + capture once per batch size
+  void check_status();                          // read the device status words (synchronous)
+  void activate() const;
+  void release();  // free every device resource (idempotent)
+
+  int device_;
+  size_t max_batch_;
+  bool failed_ = false;
+  cudaStream_t stream_ = nullptr;
+  void *weight_blob_ = nullptr;
+  void *act_blob_ = nullptr;
+  DeviceWeights w_{};
+  __half *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *act_ = nullptr,
+         *patches_ = nullptr;
+  float *image_ = nullptr, *out_ = nullptr;
+  uint32_t *status_ = nullptr;       // device: [0] failure bits, [1] non-finite input
+  uint32_t *status_host_ = nullptr;  // pinned mirror
+  bool status_pending_ = false;      // work enqueued since the last status check
+  std::map<size_t, Plan> plans_;
+};
+
+}  // namespace dv3

@@ -1,0 +1,54 @@
+// tma.cpp - CUtensorMap encoding through the driver entry point (the library links the CUDA
+// runtime statically and does not link libcuda, so it loads on machines without a driver).
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "kernels.h"
+
+namespace dv3 {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string *err) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn && err) *err = "cuTensorMapEncodeTiled is unavailable";
+  return fn;
+}
+
+bool encode_map_f16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                    uint32_t box_cols, uint32_t box_rows, std::string *err) {
+  auto fn = encode_fn(err);
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0 || rows == 0 ||
+      box_cols * 2 != 128 || box_rows == 0 || box_rows > 256) {
+    if (err) *err = "tensor map: base must be 16-byte aligned, rows of whole 16-byte units";
+    return false;
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) {
+      char buf[128];
+      std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+      *err = buf;
+    }
+    return false;
+  }
+  return true;
+}
+
+}  // namespace dv3

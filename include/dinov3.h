@@ -1,0 +1,156 @@
+/*
+ * dinov3.h - C ABI of the B200 (sm_100a) DINOv3 ViT-S+/16 forward.
+ *
+ * This is the drop-in boundary for the reference crate's public model API (src/lib.rs of
+ * zacharydenton/dinov3-loom, crate `dinov3-hrx`). Each entry point below names the Rust item it
+ * replaces. Conventions follow the reference:
+ *   - A model owns its device, stream, packed weights, resident activations (sized for
+ *     `max_batch` images), one CUDA graph per batch size it has seen, and its error state.
+ *   - The caller owns every host buffer it passes; the library never keeps a pointer to one.
+ *   - One caller per model at a time (the reference takes `&mut self`); separate models are
+ *     independent and may run concurrently, one per device or several on one device.
+ *   - Errors: every function returning int returns 0 on success or a nonzero DV3_* status.
+ *     dv3_last_error() then gives the message of the calling thread's last failure. The texts
+ *     carry the reference's messages ("max_batch must be 1..=64", "input must contain complete
+ *     3x224x224 images", "input must be finite", "tensor patch_w[0] cannot be represented as
+ *     finite float16: ...", "session is unusable after a GPU failure").
+ *   - After a CUDA error or a device-side timeout the model is poisoned: every later call
+ *     returns DV3_POISONED (src/engine.rs:36,93,168-171,198-200,210-212,265-267).
+ *
+ * Shapes: an image is 3x224x224 normalised float32 NCHW (DV3_IMAGE_ELEMENTS floats); the output
+ * of one image is 201 tokens x 384 float32 (CLS, 4 registers, 196 patches).
+ */
+#ifndef DINOV3_H
+#define DINOV3_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define DV3_IMAGE_ELEMENTS (3 * 224 * 224) /* src/lib.rs:11 */
+#define DV3_TOKENS 201                     /* src/lib.rs:12 */
+#define DV3_HIDDEN 384                     /* src/lib.rs:13 */
+#define DV3_MAX_BATCH_LIMIT 64
+
+enum {
+  DV3_OK = 0,
+  DV3_INVALID_ARGUMENT = 1, /* options, shapes, non-finite or incomplete input */
+  DV3_WEIGHTS = 2,          /* unreadable, malformed or unrepresentable weights */
+  DV3_DEVICE = 3,           /* no usable sm_100 device, or a CUDA call failed */
+  DV3_POISONED = 4,         /* an earlier GPU failure made this model unusable */
+};
+
+typedef struct dv3_model dv3_model;
+
+/* Options (src/lib.rs:15-27). Defaults: device 0, max_batch 32. */
+typedef struct {
+  int32_t device;
+  size_t max_batch; /* resident capacity, 1..=64; larger inputs are processed in chunks */
+} dv3_options;
+
+/* Distribution / ForwardTimings (src/engine.rs:272-284): host-clock milliseconds. */
+typedef struct {
+  double median_ms;
+  double p95_ms;
+} dv3_distribution;
+
+typedef struct {
+  size_t samples;
+  dv3_distribution graph;  /* one CUDA graph launch per sample */
+  dv3_distribution direct; /* the same launch list issued kernel by kernel */
+} dv3_timings;
+
+dv3_options dv3_default_options(void);
+
+/* DINOv3::load (src/lib.rs:49-88). Checks the options first (before touching the file), then
+ * reads and packs the weights (before touching the GPU), then opens the device (which must be
+ * sm_100), uploads, allocates and builds the kernels' state. */
+int dv3_load(const char *safetensors_path, dv3_options options, dv3_model **out);
+
+/* DINOv3::forward (src/lib.rs:90-114). `pixels` holds n_floats = k*DV3_IMAGE_ELEMENTS floats
+ * (k >= 0); `out` must have room for k*201*384 floats (out_floats). Synchronous. Inputs larger
+ * than max_batch are processed in chunks of max_batch. Non-finite input is an error; it is
+ * detected on the device while the input is read, so `out` is unspecified on that error.
+ * Host buffers may be pageable; pinned buffers transfer faster. */
+int dv3_forward(dv3_model *m, const float *pixels, size_t n_floats, float *out, size_t out_floats);
+
+/* DINOv3::cls (src/lib.rs:126-132): the CLS token of each image, k*384 floats. */
+int dv3_cls(dv3_model *m, const float *pixels, size_t n_floats, float *out, size_t out_floats);
+
+/* DINOv3::patch_mean (src/lib.rs:134-148): mean of the 196 patch tokens, k*384 floats. */
+int dv3_patch_mean(dv3_model *m, const float *pixels, size_t n_floats, float *out,
+                   size_t out_floats);
+
+/* DINOv3::benchmark (src/lib.rs:116-124, src/engine.rs:130-190): stages one non-empty batch of
+ * at most max_batch images, then alternates graph replay and direct dispatch for 10 warm-up
+ * plus `samples` (>= 10) rounds, each synchronised and timed with the host clock. */
+int dv3_benchmark(dv3_model *m, const float *pixels, size_t n_floats, size_t samples,
+                  dv3_timings *out);
+
+/* Drop the model and every device resource it owns. NULL is allowed. */
+void dv3_free(dv3_model *m);
+
+/* Message of the calling thread's last failure ("" if none). Valid until the next call on
+ * this thread. */
+const char *dv3_last_error(void);
+
+/* ---- Device-resident path (no reference counterpart: the reference always copies through
+ * host memory). For callers whose images are already in device memory of the model's device,
+ * and for measurement. ---- */
+
+/* The model's resident input buffer: max_batch*DV3_IMAGE_ELEMENTS floats of device memory on
+ * the model's device. Images staged there are consumed by dv3_run. */
+float *dv3_input_buffer(dv3_model *m);
+
+/* The model's resident output buffer: max_batch*201*384 floats of device memory. */
+float *dv3_output_buffer(dv3_model *m);
+
+/* The model's CUDA stream (a cudaStream_t), on which all of its work is ordered. */
+void *dv3_stream(dv3_model *m);
+
+/* Enqueue one forward of the first `batch` images of the input buffer (1 <= batch <=
+ * max_batch) into the output buffer, as one CUDA graph launch on the model's stream. Does not
+ * wait. Non-finite input and device faults are reported by the next dv3_synchronize. */
+int dv3_run(dv3_model *m, size_t batch);
+
+/* Wait for the model's stream and report any error raised by work enqueued since the last
+ * check (DV3_INVALID_ARGUMENT for non-finite input; DV3_POISONED for a device fault). */
+int dv3_synchronize(dv3_model *m);
+
+/* dv3_forward on device pointers (same device as the model): copies each chunk into the input
+ * buffer, runs it and copies its output out, all on the model's stream, then synchronises. */
+int dv3_forward_device(dv3_model *m, const float *device_pixels, size_t n_floats,
+                       float *device_out, size_t out_floats);
+
+/* Number of kernel launches in one forward of `batch` images (the graph's kernel nodes). */
+int dv3_launches_per_forward(dv3_model *m, size_t batch, size_t *out);
+
+/* Per-kernel device time of one forward of `batch` staged images: every launch of the plan is
+ * issued directly and bracketed by CUDA events on the model's stream, `iterations` times after
+ * 3 warm-up rounds. Writes up to `capacity` entries (launch order) of average milliseconds and
+ * a static kernel name, and the count to *count. */
+int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *ms,
+                         const char **names, size_t capacity, size_t *count);
+
+/* ---- Weight packing (src/weights.rs:6-17), usable without a GPU. ---- */
+
+/* Round each float to IEEE binary16 (round to nearest, ties to even), failing on the first
+ * value whose result is not finite: returns DV3_WEIGHTS with *bad_index set and the message
+ * "tensor <name>[<index>] cannot be represented as finite float16: <value>". */
+int dv3_pack_f16(const char *name, const float *values, size_t n, uint16_t *out,
+                 size_t *bad_index);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DINOV3_H */

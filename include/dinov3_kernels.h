@@ -1,0 +1,115 @@
+/*
+ * dinov3_kernels.h - C ABI of the individual sm_100a kernels of the DINOv3 ViT-S+/16 forward.
+ *
+ * One entry point per kernel specialisation of the reference (kernels/*.loom of
+ * zacharydenton/dinov3-loom, listed in specifications(), src/lib.rs:281-300). These are what the
+ * reference's engine dispatches per launch (src/engine.rs:87-129: a kernel index, one scalar
+ * `m_size`/`token_count`, a grid and buffer bindings); here each takes plain device pointers,
+ * the row count and a stream. The model API (dinov3.h) records the same kernels into one CUDA
+ * graph per batch size.
+ *
+ * Common rules:
+ *   - All pointers are device pointers on the current device, 16-byte aligned.
+ *   - f16 tensors are IEEE binary16 (uint16_t storage), f32 tensors float.
+ *   - `rows` is the number of token rows (201 per image) or patch rows (196 per image).
+ *     rows == 0 launches nothing and returns 0.
+ *   - `status` is an optional device array of two uint32_t words (NULL allowed). Word 0
+ *     collects device-side failure bits (a bounded wait that expired; the kernel then exits
+ *     without finishing). Word 1 is set nonzero by dv3k_patchify when an input value is not
+ *     finite. The caller clears and reads them.
+ *   - `stream` is a cudaStream_t (NULL: the legacy default stream). Launches are asynchronous.
+ *   - Return value: 0, DV3_INVALID_ARGUMENT (shape/alignment) or DV3_DEVICE (launch failed),
+ *     with the message in dv3_last_error().
+ *
+ * Weight layouts (the load-time packing contract, src/weights.rs:62-144):
+ *   patch_w  [384][768] f16, columns in (c, dy, dx) order (the conv weight flattened);
+ *   patch_b  [384] f32;  prefix [5][384] f32 = CLS token then the 4 register tokens;
+ *   qkv_w    [1152][384] f16 = q rows, k rows, v rows;  qkv_b [1152] f32 with the k part 0;
+ *   o_w      [384][384] f16;  down_w [384][1536] f16;  o_b, down_b, ls1, ls2 [384] f32;
+ *   gateup_w [3072][384] f16 and gateup_b [3072] f32 in the interleaved order of
+ *            dv3k_gateup_source_row() (64 gate rows, then the matching 64 up rows, ...);
+ *   rope_cos, rope_sin [196][64] f32 (per patch: row freqs 0..15, column freqs 0..15, row,
+ *            column; angle 2*pi*(2*(pos+0.5)/14-1)/100^(j/16));
+ *   LayerNorm gamma/beta [384] f32.
+ */
+#ifndef DINOV3_KERNELS_H
+#define DINOV3_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Device-side patchify and prefix placement. Replaces the host loop patchify (src/lib.rs:
+ * 265-280) and the prefix half of kernels/embed_scatter_f32.loom:
+ *   patches[i*196 + gy*14 + gx][(c*16 + dy)*16 + dx] = f16(images[i][c][gy*16+dy][gx*16+dx])
+ *   x[i*201 + t][:] = f16(prefix[t][:])  for t < 5
+ * Sets status[1] when any input value is not finite (the check of src/lib.rs:95). */
+int dv3k_patchify(const float *images, uint32_t n_images, const float *prefix, uint16_t *patches,
+                  uint16_t *x, uint32_t *status, void *stream);
+
+/* Patch embedding GEMM and scatter. Replaces kernels/matmul_bias_f16_wmma.loom (k=768, n=384)
+ * and the patch half of kernels/embed_scatter_f32.loom:
+ *   x[(p/196)*201 + 5 + p%196][n] = f16(sum_k patches[p][k] * w[n][k] + bias[n]),
+ * with f32 accumulation, for p < n_patches. */
+int dv3k_patch_embed(const uint16_t *patches, uint32_t n_patches, const uint16_t *w,
+                     const float *bias, uint16_t *x, uint32_t *status, void *stream);
+
+/* LayerNorm over 384 channels, eps 1e-5, f16 -> f16. Replaces
+ * kernels/layernorm_rowwave_f16.loom. */
+int dv3k_layernorm_f16(const uint16_t *x, uint32_t rows, const float *gamma, const float *beta,
+                       uint16_t *out, void *stream);
+
+/* The final LayerNorm, f16 -> f32. Replaces kernels/layernorm_rowwave_f32out.loom. */
+int dv3k_layernorm_f32out(const uint16_t *x, uint32_t rows, const float *gamma,
+                          const float *beta, float *out, void *stream);
+
+/* QKV projection with 2D-axial RoPE. Replaces kernels/matmul_qkv_rope_f16_wmma.loom (k=384,
+ * n=1152, head_dim 64, prefix 5, tokens_per_image 201, rope_channels 768):
+ *   y = h @ w^T + bias (f32);  for columns < 768 of patch rows (t = row % 201 >= 5, p = t-5),
+ *   within each 64-wide head: c < 32: y_c cos[p][c] - y_{c+32} sin[p][c];
+ *                             c >= 32: y_c cos[p][c] + y_{c-32} sin[p][c];
+ *   qkv[row][:] = f16(y). */
+int dv3k_qkv_rope(const uint16_t *h, uint32_t rows, const uint16_t *w, const float *bias,
+                  const float *rope_cos, const float *rope_sin, uint16_t *qkv, uint32_t *status,
+                  void *stream);
+
+/* Multi-head attention per image (6 heads x 64, 201 tokens, scale 0.125) reading q, k, v from
+ * the fused QKV rows (stride 1152) and writing head h to columns 64h..64h+63 of out [rows][384].
+ * Replaces kernels/attention_online_f16_wmma_cf16.loom. Probabilities are rounded to f16 before
+ * the PV product; the normaliser is the f32 sum of the unrounded weights. rows must be a
+ * multiple of 201. */
+int dv3k_attention(const uint16_t *qkv, uint32_t rows, uint16_t *out, uint32_t *status,
+                   void *stream);
+
+/* Projection with LayerScale and residual: x[row][n] = f16(x + lambda[n] * (a @ w^T + bias)[n])
+ * for n < 384, in place. k is 384 (attention output projection) or 1536 (MLP down projection).
+ * Replaces kernels/matmul_resid_f16_wmma.loom (both specialisations) and, for batch 1, the
+ * split-K pair kernels/matmul_splitk_f16_wmma.loom + kernels/splitk_reduce_f16.loom. */
+int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
+                      const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
+                      void *stream);
+
+/* Gate/up projection with SwiGLU: act[row][j] = f16(silu(g) * u), g = h@Wg^T+bg, u = h@Wu^T+bu,
+ * j < 1536, from the interleaved gateup_w / gateup_b. Replaces
+ * kernels/matmul_swiglu_f16_wmma.loom (k=384, n=1536). */
+int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_w,
+                       const float *gateup_b, uint16_t *act, uint32_t *status, void *stream);
+
+/* Row of the reference's concatenated gate||up matrix ([3072][384], src/weights.rs:103-108)
+ * that packed row `packed_row` (< 3072) of gateup_w holds. Host function. */
+uint32_t dv3k_gateup_source_row(uint32_t packed_row);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DINOV3_KERNELS_H */

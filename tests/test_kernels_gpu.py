@@ -1,0 +1,224 @@
+"""Each sm_100a kernel, called through the per-kernel C ABI (include/dinov3_kernels.h), against
+a float64 numpy restatement of the same op on the same f16 inputs.
+
+Tolerances: outputs stored as f16 may differ from the float64 value rounded to f16 by one f16
+rounding step plus the f32-accumulation difference, so |gpu - ref| <= 4e-3 * max(1, |ref|);
+patchify is a pure conversion and must be bit-exact.
+"""
+import numpy as np
+import pytest
+
+import ref_numpy
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from dinov3_b200 import _lib  # noqa: E402
+
+DEV = "cuda:0"
+
+
+def lib():
+    return _lib.load()
+
+
+def t16(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float16)).to(DEV)
+
+
+def t32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(DEV)
+
+
+def status():
+    return torch.zeros(2, dtype=torch.int32, device=DEV)
+
+
+def ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def check_rc(rc):
+    assert rc == 0, _lib.last_error()
+
+
+def assert_close16(got, ref):
+    got = got.float().cpu().numpy().astype(np.float64)
+    err = np.abs(got - ref) / np.maximum(1.0, np.abs(ref))
+    assert err.max() <= 4e-3, f"max scaled error {err.max():.3e}"
+
+
+def rows_of(b):
+    return 201 * b
+
+
+def f16(a):
+    return np.asarray(a, dtype=np.float16).astype(np.float64)
+
+
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_layernorm(b):
+    rng = np.random.default_rng(b)
+    r = rows_of(b)
+    x = f16(rng.standard_normal((r, 384)) * 3 + rng.standard_normal((r, 1)))
+    g = rng.standard_normal(384) * 0.3 + 1
+    be = rng.standard_normal(384) * 0.1
+    ref = ref_numpy.norm(x, g.astype(np.float32), be.astype(np.float32))
+    xd, gd, bd = t16(x), t32(g), t32(be)
+    out16 = torch.empty((r, 384), dtype=torch.float16, device=DEV)
+    out32 = torch.empty((r, 384), dtype=torch.float32, device=DEV)
+    check_rc(lib().dv3k_layernorm_f16(ptr(xd), r, ptr(gd), ptr(bd), ptr(out16), stream()))
+    check_rc(lib().dv3k_layernorm_f32out(ptr(xd), r, ptr(gd), ptr(bd), ptr(out32), stream()))
+    torch.cuda.synchronize()
+    assert_close16(out16, ref)
+    assert np.abs(out32.cpu().numpy() - ref).max() < 1e-4
+
+
+@pytest.mark.parametrize("b", [1, 2, 5])
+def test_patchify_and_prefix(b):
+    rng = np.random.default_rng(10 + b)
+    imgs = rng.standard_normal((b, 3, 224, 224)).astype(np.float32)
+    prefix = rng.standard_normal((5, 384)).astype(np.float32)
+    patches = torch.empty((196 * b, 768), dtype=torch.float16, device=DEV)
+    x = torch.full((201 * b, 384), 7.0, dtype=torch.float16, device=DEV)
+    st = status()
+    check_rc(lib().dv3k_patchify(ptr(t32(imgs)), b, ptr(t32(prefix)), ptr(patches), ptr(x), ptr(st), stream()))
+    torch.cuda.synchronize()
+    want = np.concatenate([ref_numpy.patchify(im) for im in imgs]).astype(np.float16)
+    np.testing.assert_array_equal(patches.cpu().numpy().view(np.uint16), want.view(np.uint16))
+    xs = x.cpu().numpy().reshape(b, 201, 384)
+    for i in range(b):
+        np.testing.assert_array_equal(xs[i, :5], prefix.astype(np.float16))
+        assert np.all(xs[i, 5:] == 7.0)  # patch rows untouched
+    assert st.cpu().tolist() == [0, 0]
+    imgs[b - 1, 2, 100, 37] = np.inf
+    check_rc(lib().dv3k_patchify(ptr(t32(imgs)), b, ptr(t32(prefix)), ptr(patches), ptr(x), ptr(st), stream()))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist()[1] != 0
+
+
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_patch_embed(b):
+    rng = np.random.default_rng(20 + b)
+    p = 196 * b
+    a = f16(rng.standard_normal((p, 768)))
+    w = f16(rng.standard_normal((384, 768)) / np.sqrt(768))
+    bias = rng.standard_normal(384) * 0.1
+    ref = a @ w.T + bias.astype(np.float32)
+    x = torch.full((201 * b, 384), -3.0, dtype=torch.float16, device=DEV)
+    st = status()
+    check_rc(lib().dv3k_patch_embed(ptr(t16(a)), p, ptr(t16(w)), ptr(t32(bias)), ptr(x), ptr(st), stream()))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist() == [0, 0]
+    xs = x.reshape(b, 201, 384)
+    assert torch.all(xs[:, :5] == -3.0)  # prefix rows untouched
+    assert_close16(xs[:, 5:].reshape(p, 384), ref)
+
+
+def rope_ref(y, rows):
+    cos, sin = ref_numpy.rope_tables()
+    cos = cos.astype(np.float32).astype(np.float64)
+    sin = sin.astype(np.float32).astype(np.float64)
+    y = y.copy()
+    for row in range(rows):
+        t = row % 201
+        if t < 5:
+            continue
+        c, s = cos[t - 5], sin[t - 5]
+        for base in range(0, 768, 64):
+            v = y[row, base:base + 64].copy()
+            rot = np.concatenate([-v[32:], v[:32]])
+            y[row, base:base + 64] = v * c + rot * s
+    return y
+
+
+@pytest.mark.parametrize("b", [1, 3])
+def test_qkv_rope(b):
+    rng = np.random.default_rng(30 + b)
+    r = rows_of(b)
+    h = f16(rng.standard_normal((r, 384)))
+    w = f16(rng.standard_normal((1152, 384)) / np.sqrt(384))
+    bias = rng.standard_normal(1152) * 0.1
+    bias[384:768] = 0
+    ref = rope_ref(h @ w.T + bias.astype(np.float32), r)
+    cos, sin = ref_numpy.rope_tables()
+    out = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
+    check_rc(lib().dv3k_qkv_rope(ptr(t16(h)), r, ptr(t16(w)), ptr(t32(bias)), ptr(t32(cos)),
+                                 ptr(t32(sin)), ptr(out), ptr(status()), stream()))
+    torch.cuda.synchronize()
+    assert_close16(out, ref)
+
+
+def attention_ref(qkv, b):
+    out = np.zeros((201 * b, 384))
+    for i in range(b):
+        blk = qkv[201 * i:201 * (i + 1)]
+        for hd in range(6):
+            q = blk[:, hd * 64:(hd + 1) * 64]
+            k = blk[:, 384 + hd * 64:384 + (hd + 1) * 64]
+            v = blk[:, 768 + hd * 64:768 + (hd + 1) * 64]
+            s = q @ k.T * 0.125
+            e = np.exp(s - s.max(axis=1, keepdims=True))
+            out[201 * i:201 * (i + 1), hd * 64:(hd + 1) * 64] = (e / e.sum(axis=1, keepdims=True)) @ v
+    return out
+
+
+@pytest.mark.parametrize("b", [1, 3, 8])
+def test_attention(b):
+    rng = np.random.default_rng(40 + b)
+    r = rows_of(b)
+    qkv = f16(rng.standard_normal((r, 1152)) * 1.5)
+    ref = attention_ref(qkv, b)
+    out = torch.full((r, 384), 9.0, dtype=torch.float16, device=DEV)
+    st = status()
+    check_rc(lib().dv3k_attention(ptr(t16(qkv)), r, ptr(out), ptr(st), stream()))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist() == [0, 0]
+    assert_close16(out, ref)
+
+
+@pytest.mark.parametrize("k", [384, 1536])
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_matmul_resid(k, b):
+    rng = np.random.default_rng(50 + b + k)
+    r = rows_of(b)
+    a = f16(rng.standard_normal((r, k)))
+    w = f16(rng.standard_normal((384, k)) / np.sqrt(k))
+    bias = rng.standard_normal(384) * 0.1
+    lam = rng.random(384) * 0.2 + 0.05
+    x0 = f16(rng.standard_normal((r, 384)))
+    ref = x0 + lam.astype(np.float32) * (a @ w.T + bias.astype(np.float32))
+    x = t16(x0)
+    check_rc(lib().dv3k_matmul_resid(ptr(t16(a)), r, k, ptr(t16(w)), ptr(t32(bias)), ptr(t32(lam)),
+                                     ptr(x), ptr(status()), stream()))
+    torch.cuda.synchronize()
+    assert_close16(x, ref)
+
+
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_matmul_swiglu(b):
+    rng = np.random.default_rng(60 + b)
+    r = rows_of(b)
+    h = f16(rng.standard_normal((r, 384)))
+    wg = f16(rng.standard_normal((1536, 384)) / np.sqrt(384) * 2)
+    wu = f16(rng.standard_normal((1536, 384)) / np.sqrt(384))
+    bg = rng.standard_normal(1536) * 0.1
+    bu = rng.standard_normal(1536) * 0.1
+    g = h @ wg.T + bg.astype(np.float32)
+    u = h @ wu.T + bu.astype(np.float32)
+    ref = g / (1 + np.exp(-g)) * u
+    concat_w = np.concatenate([wg, wu])
+    concat_b = np.concatenate([bg, bu])
+    src = np.array([lib().dv3k_gateup_source_row(i) for i in range(3072)])
+    act = torch.empty((r, 1536), dtype=torch.float16, device=DEV)
+    check_rc(lib().dv3k_matmul_swiglu(ptr(t16(h)), r, ptr(t16(concat_w[src])), ptr(t32(concat_b[src])),
+                                      ptr(act), ptr(status()), stream()))
+    torch.cuda.synchronize()
+    assert_close16(act, ref)

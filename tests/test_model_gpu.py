@@ -1,0 +1,200 @@
+"""The whole forward through the model C ABI (include/dinov3.h) against the float64 oracle, and
+the reference's GPU-test properties (tests/model.rs:61-99):
+  * all-token and CLS cosine > 0.9999 per image vs the float64 forward, plus a stated max-abs
+    error bound (MAX_ABS below);
+  * batched vs single-image cosine > 0.99999;
+  * bitwise repeat determinism;
+  * incomplete and non-finite input are errors, and the session stays usable after them.
+Weights: seeded random-init ("baseline" = the benchmark distribution; "stress" = nonzero
+biases, gammas, betas and per-channel LayerScale, so every epilogue term is exercised).
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import ref_c
+import ref_numpy
+from dinov3_b200 import synth
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import dinov3_b200 as dv  # noqa: E402
+
+# Largest |gpu - float64| over every output element allowed in these tests (outputs are
+# LayerNorm-normalised, O(1)); f16 weights and activations with f32 accumulation.
+MAX_ABS = 0.08
+
+
+@pytest.fixture(scope="module")
+def models(weights_file):
+    cache = {}
+
+    def get(flavor="baseline", max_batch=4, seed=None):
+        seed = {"baseline": 0, "stress": 1}[flavor] if seed is None else seed
+        key = (flavor, max_batch, seed)
+        if key not in cache:
+            cache[key] = dv.DINOv3.load(weights_file(seed, flavor), dv.Options(0, max_batch))
+        return cache[key]
+
+    yield get
+    for m in cache.values():
+        m.close()
+
+
+@pytest.fixture(scope="module")
+def oracles(weights_dict):
+    cache = {}
+
+    def get(flavor):
+        if flavor not in cache:
+            seed = {"baseline": 0, "stress": 1}[flavor]
+            cache[flavor] = ref_c.Model(weights_dict(seed, flavor))
+        return cache[flavor]
+
+    return get
+
+
+def cos(a, b):
+    return ref_numpy.cosine(a, b)
+
+
+@pytest.mark.parametrize("flavor", ["baseline", "stress"])
+def test_full_reference_and_changing_batch(models, oracles, flavor):
+    """tests/model.rs:61-99 with seeded weights and the reference test's own input."""
+    model = models(flavor, max_batch=4)
+    images = synth.reference_test_images(4)
+    batched = model.forward(images)
+    want = oracles(flavor).forward(images, threads=0)
+    for i in range(4):
+        got = model.forward(images[i:i + 1])[0]
+        assert cos(got, want[i]) > 0.9999, f"full image {i}"
+        assert cos(got[0], want[i][0]) > 0.9999, f"CLS image {i}"
+        assert cos(batched[i], got) > 0.99999, f"batch image {i}"
+        assert np.abs(got - want[i]).max() < MAX_ABS
+    np.testing.assert_array_equal(model.forward(images), batched)  # bitwise repeat
+    with pytest.raises(dv.DINOv3Error) as e:
+        model.forward(np.zeros(3, np.float32))
+    assert "complete 3×224×224 images" in str(e.value)
+    with pytest.raises(dv.DINOv3Error) as e:
+        model.forward(np.full((1, 3, 224, 224), np.nan, np.float32))
+    assert "input must be finite" in str(e.value)
+    np.testing.assert_array_equal(model.forward(images), batched)  # still usable
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "*.npz"))), ids=os.path.basename)
+def test_gpu_matches_golden_fixtures(models, path):
+    g = np.load(path)
+    model = models(str(g["flavor"]), max_batch=4, seed=int(g["weight_seed"]))
+    img = synth.images(int(g["image_arg"]), 1) if str(g["image_source"]) == "seeded" else synth.reference_test_images(1)
+    out = model.forward(img)[0].astype(np.float64)
+    rows = g["rows"]
+    assert cos(out[rows], g["values"]) > 0.9999
+    for i, r in enumerate(rows):
+        assert cos(out[r], g["values"][i]) > 0.999, f"row {r}"
+    assert np.abs(out[rows] - g["values"]).max() < MAX_ABS
+    np.testing.assert_allclose(np.linalg.norm(out, axis=1), g["row_norms"], rtol=2e-3)
+
+
+def test_seeded_images_against_oracle_with_error_bound(models, oracles):
+    model = models("stress", max_batch=4)
+    images = synth.images(123, 3)
+    got = model.forward(images)
+    want = oracles("stress").forward(images, threads=0)
+    err = np.abs(got - want)
+    for i in range(3):
+        assert cos(got[i], want[i]) > 0.9999
+        assert cos(got[i, 0], want[i, 0]) > 0.9999
+    assert err.max() < MAX_ABS, err.max()
+
+
+def test_chunking_matches_single_images(models):
+    """5 images through max_batch=2 (chunks 2, 2, 1) equal per-image forwards bitwise, except
+    that batch size 1 and 2 are different graphs, so compare against the same chunk sizes."""
+    model = models("stress", max_batch=2)
+    images = synth.images(7, 5)
+    out = model.forward(images)
+    np.testing.assert_array_equal(out[:2], model.forward(images[:2]))
+    np.testing.assert_array_equal(out[2:4], model.forward(images[2:4]))
+    np.testing.assert_array_equal(out[4:], model.forward(images[4:]))
+    for i in range(5):
+        assert cos(out[i], model.forward(images[i:i + 1])[0]) > 0.99999
+
+
+def test_cls_and_patch_mean(models):
+    model = models("stress", max_batch=4)
+    images = synth.images(8, 3)
+    full = model.forward(images)
+    np.testing.assert_array_equal(model.cls(images), full[:, 0])
+    pm = model.patch_mean(images)
+    want = np.zeros((3, 384), np.float32)
+    for r in range(5, 201):  # src/lib.rs:134-148 accumulation order
+        want += full[:, r] / np.float32(196.0)
+    np.testing.assert_array_equal(pm, want)
+
+
+def test_empty_input_returns_empty(models):
+    model = models("baseline", max_batch=4)
+    assert model.forward(np.zeros(0, np.float32)).shape == (0, 201, 384)
+
+
+def test_device_path_matches_host_path(models):
+    model = models("stress", max_batch=4)
+    images = synth.images(9, 3)
+    host = model.forward(images)
+    dev = model.forward_device(torch.from_numpy(images).cuda())
+    np.testing.assert_array_equal(dev.cpu().numpy(), host)
+    # staged input + graph replay + resident output
+    inp = device_view(model.input_buffer, 3 * 3 * 224 * 224)
+    inp.copy_(torch.from_numpy(images).reshape(-1))
+    torch.cuda.synchronize()
+    model.run(3)
+    model.synchronize()
+    out = device_view(model.output_buffer, 3 * 201 * 384).cpu().numpy()
+    np.testing.assert_array_equal(out.reshape(3, 201, 384), host)
+
+
+class _DeviceArray:
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+def device_view(ptr, n):
+    """A torch view (no copy) of n float32 at a device address owned by the model."""
+    return torch.as_tensor(_DeviceArray(ptr, n), device="cuda")
+
+
+def test_full_size_batch_properties(models, oracles):
+    """Batch 64 (the benchmark configuration): per-image results match single-image forwards,
+    two images match the oracle, and repeats are bitwise identical."""
+    model = models("baseline", max_batch=64)
+    images = synth.images(2024, 64)
+    out = model.forward(images)
+    assert np.isfinite(out).all()
+    for i in (0, 17, 63):
+        assert cos(out[i], model.forward(images[i:i + 1])[0]) > 0.99999
+    want = oracles("baseline").forward(images[[5, 63]], threads=0)
+    assert cos(out[5], want[0]) > 0.9999 and cos(out[63], want[1]) > 0.9999
+    np.testing.assert_array_equal(model.forward(images), out)
+
+
+def test_benchmark_and_profile(models):
+    model = models("baseline", max_batch=4)
+    images = synth.images(3, 2)
+    t = model.benchmark(images, 10)
+    assert t.samples == 10 and 0 < t.graph.median_ms <= t.graph.p95_ms
+    assert 0 < t.direct.median_ms <= t.direct.p95_ms
+    with pytest.raises(dv.DINOv3Error):
+        model.benchmark(images, 5)
+    with pytest.raises(dv.DINOv3Error):
+        model.benchmark(np.zeros(0, np.float32), 10)
+    prof = model.profile_launches(2, 2)
+    assert len(prof) == model.launches_per_forward(2) == 75
+    assert all(ms > 0 for _, ms in prof)
