@@ -37,8 +37,23 @@ def status():
     return torch.zeros(2, dtype=torch.int32, device=DEV)
 
 
+_KEEP = []
+
+
 def ptr(t):
-    return t.data_ptr() if t is not None else None
+    """Device address of `t`, holding a reference until the test ends: a temporary freed at once
+    would hand its memory to the next allocation before the asynchronous kernel reads it."""
+    if t is None:
+        return None
+    _KEEP.append(t)
+    return t.data_ptr()
+
+
+@pytest.fixture(autouse=True)
+def _keepalive():
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
 
 
 def stream():
