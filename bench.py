@@ -55,6 +55,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile-iters", type=int, default=20)
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--forward-only", action="store_true",
+                    help="profiling driver: load, stage one batch, replay warmup+steps forwards, exit")
+    ap.add_argument("--batch", type=int, default=BATCH, help="images per forward (--forward-only)")
     return ap.parse_args()
 
 
@@ -259,6 +262,16 @@ def run_ours(args):
     staged = torch.as_tensor(_Dev(model.input_buffer, n_img), device="cuda")
     staged.copy_(torch.from_numpy(images).reshape(-1))
     torch.cuda.synchronize()
+
+    if args.forward_only:
+        b = max(1, min(args.batch, BATCH))
+        for _ in range(args.warmup + args.steps):
+            model.run(b)
+        model.synchronize()
+        print(json.dumps({"forward_only": True, "batch": b, "forwards": args.warmup + args.steps,
+                          "launches_per_forward": model.launches_per_forward(b)}), flush=True)
+        model.close()
+        return
 
     # ---- device-resident throughput ----
     launches = model.launches_per_forward(BATCH)

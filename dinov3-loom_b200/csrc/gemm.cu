@@ -11,10 +11,12 @@
 // One thread issues tcgen05.mma (M=128, N=BN, K=16 steps) into an f32 accumulator in TMEM;
 // TMEM holds two accumulators so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// Warp roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
-// (lane 0), warps 2-5 = epilogue. Epilogue warp w may read TMEM lanes 32*(w%4)..+31, so each
-// epilogue thread owns one output row of the 128-row tile and processes it in 32-column
-// chunks (tcgen05.ld 32x32b.x32).
+// Warp roles (320 threads): warp 0 lane 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
+// (lane 0), warps 2-9 = epilogue. An epilogue warp may read only TMEM lanes 32*(w%4)..+31, so
+// two warps share each lane quarter: warps 2-5 take the left half of the tile's columns and
+// warps 6-9 the right half. Each epilogue thread owns one output row and walks its half in
+// 32-column chunks (tcgen05.ld 32x32b.x32). Two warps per SM sub-partition hide the latency of
+// the epilogue arithmetic, which otherwise limits the whole GEMM.
 //
 // Tiles are walked m-major with the N tile fastest (tile t -> m = t / n_tiles, n = t % n_tiles)
 // by a grid of min(tiles, SMs) persistent CTAs, so the CTAs working at one time share A rows
@@ -26,7 +28,8 @@ namespace dv3 {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kEpilogueWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;  // 320
 
 template <int BN>
 struct GemmCfg {
@@ -37,8 +40,7 @@ struct GemmCfg {
   static constexpr int kTiles = kStages * kStage;
   static constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
   static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
-  static constexpr int kSmemBytes = 1024 + kTiles + kBarBytes;
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static constexpr int kExtraOffset = kTiles + ((kBarBytes + 127) / 128) * 128;
 };
 
 __device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
@@ -52,6 +54,7 @@ __device__ __forceinline__ void store_half32(__half *dst, const float (&v)[32]) 
   }
 }
 
+// 32 consecutive floats at an address shared by the whole warp (one broadcast per float4).
 __device__ __forceinline__ void load_bias32(const float *b, float (&v)[32]) {
   const float4 *p = reinterpret_cast<const float4 *>(b);
 #pragma unroll
@@ -65,19 +68,23 @@ __device__ __forceinline__ void load_bias32(const float *b, float (&v)[32]) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Epilogues. `taddr` addresses column 0 of this tile's accumulator at the warp's lane quarter;
-// `row` is this thread's output row (it may be >= M on the last M tile: loads from TMEM still
-// run, because tcgen05.ld is warp-collective, but global accesses are skipped).
+// Epilogues. run<COLS>() processes COLS accumulator columns starting at `taddr` (this warp's
+// lane quarter) that belong to output columns n0..n0+COLS-1; `row` is this thread's output row
+// (it may be >= M on the last M tile: TMEM loads still run, because tcgen05.ld is
+// warp-collective, but global accesses are skipped). kSmem bytes of shared memory are set up by
+// init() (all threads, before the first barrier) and passed to run().
 // ---------------------------------------------------------------------------------------------
 struct EpiPatch {
   const float *bias;
   __half *x;
-  template <int BN>
-  __device__ void run(uint32_t taddr, int row, int n0, int M) const {
+  static constexpr int kSmem = 0;
+  __device__ void init(uint8_t *, int, int) const {}
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int row, int n0, int M, const uint8_t *) const {
     const bool ok = row < M;
     const int token = (row / kPatches) * kTokens + kPrefix + row % kPatches;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 0; c < COLS; c += 32) {
       uint32_t r[32];
       tmem_load32(taddr + c, r);
       float v[32];
@@ -89,21 +96,40 @@ struct EpiPatch {
   }
 };
 
+// RoPE angles depend only on (position along one axis, frequency index j < 16): channel c of
+// patch p uses row position p/14 when c%32 < 16 and column position p%14 otherwise, frequency
+// c%16 (src/weights.rs:127-144). init() copies those 14x16 cos/sin values of each axis out of
+// the packed [196][64] table into shared memory (rows padded to 17 floats so that the 32 rows
+// of a warp fall in distinct banks); the packed entries for channels c and c+32 are equal.
 struct EpiQkvRope {
   const float *bias;
   const float *cosv;
   const float *sinv;
   __half *out;
-  template <int BN>
-  __device__ void run(uint32_t taddr, int row, int n0, int M) const {
+  static constexpr int kPad = 17;
+  static constexpr int kTab = 14 * kPad;                  // floats per (axis, function)
+  static constexpr int kSmem = 4 * kTab * sizeof(float);  // cos_y, sin_y, cos_x, sin_x
+  __device__ void init(uint8_t *smem, int tid, int nthreads) const {
+    float *t = reinterpret_cast<float *>(smem);
+    for (int i = tid; i < 4 * 14 * 16; i += nthreads) {
+      const int which = i / 224, pos = (i / 16) % 14, j = i % 16;
+      // axis 0 (rows): patch pos*14, channel j; axis 1 (columns): patch pos, channel 16+j
+      const int src = (which < 2) ? (pos * 14) * 64 + j : pos * 64 + 16 + j;
+      t[which * kTab + pos * kPad + j] = __ldg(((which & 1) ? sinv : cosv) + src);
+    }
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int row, int n0, int M, const uint8_t *smem) const {
+    static_assert(COLS % 64 == 0, "a thread owns whole heads");
     const bool ok = row < M;
     const int t = row % kTokens;
     const bool patch_row = t >= kPrefix;
     const int p = patch_row ? t - kPrefix : 0;
-    const float *cr = cosv + p * 64;
-    const float *sr = sinv + p * 64;
+    const float *tab = reinterpret_cast<const float *>(smem);
+    const float *cy = tab + (p / 14) * kPad, *sy = tab + kTab + (p / 14) * kPad;
+    const float *cx = tab + 2 * kTab + (p % 14) * kPad, *sx = tab + 3 * kTab + (p % 14) * kPad;
 #pragma unroll 1
-    for (int h = 0; h < BN; h += 64) {
+    for (int h = 0; h < COLS; h += 64) {
       uint32_t ra[32], rb[32];
       tmem_load32x2(taddr + h, ra, taddr + h + 32, rb);
       const int col = n0 + h;  // first column of this 64-wide head
@@ -118,11 +144,11 @@ struct EpiQkvRope {
       if (patch_row && col < 2 * kHidden) {  // q and k columns of patch tokens rotate
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float c0 = __ldg(cr + i), s0 = __ldg(sr + i);
-          const float c1 = __ldg(cr + 32 + i), s1 = __ldg(sr + 32 + i);
+          const float c = i < 16 ? cy[i] : cx[i - 16];
+          const float s = i < 16 ? sy[i] : sx[i - 16];
           const float a = lo[i], b = hi[i];
-          lo[i] = a * c0 - b * s0;
-          hi[i] = b * c1 + a * s1;
+          lo[i] = a * c - b * s;
+          hi[i] = b * c + a * s;
         }
       }
       if (ok) {
@@ -138,17 +164,19 @@ struct EpiResid {
   const float *bias;
   const float *lambda;
   __half *x;
-  template <int BN>
-  __device__ void run(uint32_t taddr, int row, int n0, int M) const {
+  static constexpr int kSmem = 0;
+  __device__ void init(uint8_t *, int, int) const {}
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int row, int n0, int M, const uint8_t *) const {
     const bool ok = row < M;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 0; c < COLS; c += 32) {
       uint32_t r[32];
       tmem_load32(taddr + c, r);
-      float b[32], l[32];
-      load_bias32(bias + n0 + c, b);
-      load_bias32(lambda + n0 + c, l);
       if (ok) {
+        float b[32], l[32];
+        load_bias32(bias + n0 + c, b);
+        load_bias32(lambda + n0 + c, l);
         __half *xr = x + static_cast<size_t>(row) * kHidden + n0 + c;
         const uint4 *src = reinterpret_cast<const uint4 *>(xr);
         float v[32];
@@ -174,11 +202,14 @@ struct EpiResid {
 struct EpiSwiGLU {
   const float *bias;  // packed like the weight rows
   __half *act;
-  template <int BN>
-  __device__ void run(uint32_t taddr, int row, int n0, int M) const {
+  static constexpr int kSmem = 0;
+  __device__ void init(uint8_t *, int, int) const {}
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int row, int n0, int M, const uint8_t *) const {
+    static_assert(COLS % 128 == 0, "a thread owns whole 64 gate + 64 up groups");
     const bool ok = row < M;
 #pragma unroll 1
-    for (int g = 0; g < BN; g += 128) {
+    for (int g = 0; g < COLS; g += 128) {
 #pragma unroll 1
       for (int half = 0; half < 64; half += 32) {
         uint32_t rg[32], ru[32];
@@ -190,13 +221,18 @@ struct EpiSwiGLU {
         for (int i = 0; i < 32; ++i) {
           const float a = gv[i] + u2f(rg[i]);
           const float u = uv[i] + u2f(ru[i]);
-          gv[i] = a / (1.0f + __expf(-a)) * u;
+          gv[i] = __fdividef(a, 1.0f + __expf(-a)) * u;  // silu(a) * u
         }
         if (ok) store_half32(act + static_cast<size_t>(row) * kMlp + (n0 + g) / 2 + half, gv);
       }
     }
   }
 };
+
+template <int BN, class Epi>
+__host__ __device__ constexpr int gemm_smem_bytes() {
+  return 1024 + GemmCfg<BN>::kExtraOffset + Epi::kSmem;
+}
 
 // ---------------------------------------------------------------------------------------------
 // The kernel
@@ -206,6 +242,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 int M, int n_tiles_n, int k_blocks, Epi epi, uint32_t *status) {
   using C = GemmCfg<BN>;
+  static_assert(gemm_smem_bytes<BN, Epi>() <= 227 * 1024, "shared memory budget");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t *smem = smem_raw + pad;
@@ -216,6 +253,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint8_t *extra = smem + C::kExtraOffset;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -227,7 +265,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * kEpilogueWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -238,6 +276,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  epi.init(extra, threadIdx.x, kGemmThreads);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -315,7 +354,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    const int q = warp & 3;
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;       // which half of the tile's columns
+    constexpr int kCols = BN / 2;
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int acc = 0;
@@ -331,9 +372,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       const int m0 = (tile / n_tiles_n) * BM;
-      const int n0 = (tile % n_tiles_n) * BN;
-      epi.template run<BN>(tmem_base + lane_base + static_cast<uint32_t>(acc * BN),
-                           m0 + row_in_tile, n0, M);
+      const int n0 = (tile % n_tiles_n) * BN + half * kCols;
+      epi.template run<kCols>(
+          tmem_base + lane_base + static_cast<uint32_t>(acc * BN + half * kCols), m0 + row_in_tile,
+          n0, M, extra);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
@@ -384,31 +426,28 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, Gemm
 }
 
 template <int BN, class Epi>
+static cudaError_t configure_one() {
+  return cudaFuncSetAttribute(gemm_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              gemm_smem_bytes<BN, Epi>());
+}
+
+template <int BN, class Epi>
 static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k, const Epi &epi,
                               uint32_t *status, cudaStream_t stream) {
-  using C = GemmCfg<BN>;
   static bool configured[64] = {};  // per template instance and device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, Epi>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
+    cudaError_t e = configure_one<BN, Epi>();
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const int n_tiles_n = n / BN;
   const int tiles = static_cast<int>((rows + BM - 1) / BM) * n_tiles_n;
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  gemm_kernel<BN, Epi><<<grid, kGemmThreads, C::kSmemBytes, stream>>>(
+  gemm_kernel<BN, Epi><<<grid, kGemmThreads, gemm_smem_bytes<BN, Epi>(), stream>>>(
       maps.a, maps.b, static_cast<int>(rows), n_tiles_n, k / BK, epi, status);
   return cudaGetLastError();
-}
-
-template <int BN, class Epi>
-static cudaError_t configure_one() {
-  return cudaFuncSetAttribute(gemm_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              GemmCfg<BN>::kSmemBytes);
 }
 
 // Set the shared-memory limits of every GEMM instance on the current device (done at load, so
