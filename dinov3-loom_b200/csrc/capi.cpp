@@ -191,7 +191,7 @@ int gemm_entry(dv3::GemmOp op, const void *a, uint32_t rows, const void *w,
   if (rows == 0) return DV3_OK;
   dv3::GemmMaps maps;
   std::string err;
-  if (!dv3::make_gemm_maps(op, a, rows, w, &maps, &err)) return bad_args(err.c_str());
+  if (!dv3::make_gemm_maps(op, a, rows, w, args.out, &maps, &err)) return bad_args(err.c_str());
   return launch_status(dv3::launch_gemm(op, maps, rows, args, status, static_cast<cudaStream_t>(stream)),
                        dv3::gemm_name(op));
 }
@@ -272,6 +272,26 @@ int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16
   g.out = reinterpret_cast<__half *>(x);
   return gemm_entry(k == 384 ? dv3::GemmOp::Resid384 : dv3::GemmOp::Resid1536, a, rows, w, g, status,
                     stream);
+}
+
+int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
+                                const float *bias, const float *lambda, uint16_t *x,
+                                const float *gamma, const float *beta, uint16_t *h,
+                                float *out_f32, uint32_t *status, void *stream) {
+  if (!all_aligned(a, w, bias, lambda, x, gamma, beta, h, out_f32))
+    return bad_args("pointers must be 16-byte aligned");
+  if (k != 384 && k != 1536) return bad_args("k must be 384 or 1536");
+  if ((h == nullptr) == (out_f32 == nullptr)) return bad_args("exactly one of h and out_f32");
+  dv3::GemmArgs g;
+  g.bias = bias;
+  g.lambda = lambda;
+  g.out = reinterpret_cast<__half *>(x);
+  g.gamma = gamma;
+  g.beta = beta;
+  g.ln_out = reinterpret_cast<__half *>(h);
+  g.ln_out_f32 = out_f32;
+  return gemm_entry(k == 384 ? dv3::GemmOp::ResidLN384 : dv3::GemmOp::ResidLN1536, a, rows, w, g,
+                    status, stream);
 }
 
 int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_w,

@@ -1,0 +1,405 @@
+// gemm_epilogues.cuh - the fused epilogues of the tcgen05 GEMM (gemm.cu).
+//
+// Interface of an epilogue type E:
+//   static constexpr int  kSmem;       bytes of shared memory for staged per-column vectors
+//   static constexpr bool kTmaStore;   the output leaves through per-warp TMA bulk stores
+//   void init(uint8_t *smem, int tid, int n)
+//       all CTA threads, before the first barrier: stage per-column vectors (bias, LayerScale,
+//       gamma, beta, RoPE angles) into shared memory, so the per-row work reads them as
+//       shared-memory broadcasts instead of global loads
+//   template <int COLS> void run(uint32_t taddr, int n0, EpiCtx &ctx)
+//       processes COLS accumulator columns starting at TMEM address `taddr` (this warp's lane
+//       quarter) that belong to output columns n0..n0+COLS-1 of output row ctx.row. ctx.row may
+//       be >= M on the last M tile: TMEM loads still run, because tcgen05.ld is
+//       warp-collective, but global accesses are skipped (TMA stores clip such rows).
+//
+// Output path of kTmaStore epilogues: each warp owns 32 rows (its TMEM lane quarter) and emits
+// 32 columns at a time: the 32x32 f16 block goes into one of the warp's two 2 KB shared-memory
+// buffers in the 64-byte-swizzled layout (row r holds its 16-byte chunk j at chunk
+// j ^ ((r >> 1) & 3), so the 32 row writes of a warp hit every bank group evenly), and lane 0
+// sends it to global memory with one cp.async.bulk.tensor store. The per-row scattered stores
+// of a row-per-thread epilogue (32 rows touched per warp instruction) are replaced by full-line
+// TMA writes that run in the background.
+#pragma once
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace dv3 {
+
+constexpr int kEpilogueWarps = 8;
+constexpr int kEpilogueThreads = 32 * kEpilogueWarps;
+constexpr int kStageBlockBytes = 32 * 64;  // 32 rows x 32 f16 columns
+
+struct EpiCtx {
+  int row;     // output row of this thread
+  int M;       // rows of the GEMM
+  int half;    // column half of the tile (0: warps 2-5, 1: warps 6-9)
+  int r;       // row within the tile == TMEM lane
+  int lane;
+  int row0;    // first row of this warp's 32 rows
+  uint8_t *smem;       // epilogue's staged vectors
+  uint8_t *staging;    // this warp's two staging blocks
+  int buf;             // staging block to use next
+  const CUtensorMap *out_map;
+};
+
+__device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
+
+__device__ __forceinline__ void stage_floats(float *dst, const float *src, int n, int tid,
+                                             int nthreads) {
+  for (int i = tid; i < n; i += nthreads) dst[i] = __ldg(src + i);
+}
+
+// 32 consecutive floats from shared memory at an address common to the warp (broadcast).
+__device__ __forceinline__ void lds32(const float *s, float (&v)[32]) {
+  const float4 *p = reinterpret_cast<const float4 *>(s);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 q = p[j];
+    v[4 * j + 0] = q.x;
+    v[4 * j + 1] = q.y;
+    v[4 * j + 2] = q.z;
+    v[4 * j + 3] = q.w;
+  }
+}
+
+__device__ __forceinline__ void ldg_half32(const __half *src, uint4 (&q)[4]) {
+  const uint4 *p = reinterpret_cast<const uint4 *>(src);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) q[j] = p[j];
+}
+
+__device__ __forceinline__ void unpack_half32(const uint4 (&q)[4], float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t w[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_half2(w[e]);
+      v[8 * j + 2 * e] = f.x;
+      v[8 * j + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[32], int j) {
+  return make_uint4(pack_half2(v[8 * j + 0], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                    pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+}
+
+__device__ __forceinline__ void store_half32(__half *dst, const float (&v)[32]) {
+  uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d[j] = pack8(v, j);
+}
+
+// Emit this warp's 32 rows x 32 columns (f16 of v, one row per lane) at output column `col`
+// through a staging block and a TMA store.
+__device__ __forceinline__ void tma_emit32(EpiCtx &c, const float (&v)[32], int col) {
+  uint8_t *blk = c.staging + c.buf * kStageBlockBytes;
+  if (c.lane == 0) bulk_wait_read<1>();  // the store that last used this block has read it
+  __syncwarp();
+  uint8_t *rowp = blk + c.lane * 64;
+  const int sw = (c.lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4 *>(rowp + ((j ^ sw) << 4)) = pack8(v, j);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (c.lane == 0) {
+    tma_store_2d(c.out_map, blk, col, c.row0);
+    bulk_commit();
+  }
+  c.buf ^= 1;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Patch embedding: x[(p/196)*201 + 5 + p%196][n] = f16(acc + b[n]). The destination rows are
+// not contiguous (5 prefix rows per image interleave), so the rows are written directly.
+// ---------------------------------------------------------------------------------------------
+struct EpiPatch {
+  const float *bias;
+  __half *x;
+  static constexpr int kSmem = kHidden * 4;
+  static constexpr bool kTmaStore = false;
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    stage_floats(reinterpret_cast<float *>(smem), bias, kHidden, tid, n);
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+    const float *sb = reinterpret_cast<const float *>(c.smem);
+    const bool ok = c.row < c.M;
+    const int token = (c.row / kPatches) * kTokens + kPrefix + c.row % kPatches;
+#pragma unroll 1
+    for (int k = 0; k < COLS; k += 32) {
+      uint32_t r[32];
+      tmem_load32(taddr + k, r);
+      float v[32];
+      lds32(sb + n0 + k, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += u2f(r[i]);
+      if (ok) store_half32(x + static_cast<size_t>(token) * kHidden + n0 + k, v);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// QKV projection with 2D-axial RoPE on the q and k columns of patch rows.
+// RoPE angles depend only on (position along one axis, frequency index j < 16): channel c of
+// patch p uses row position p/14 when c%32 < 16 and column position p%14 otherwise, frequency
+// c%16 (src/weights.rs:127-144). init() copies those 14x16 cos/sin values of each axis out of
+// the packed [196][64] table (rows padded to 17 floats so the 32 rows of a warp fall in distinct
+// banks); the packed entries for channels c and c+32 are equal. Columns >= 1152 (the zero-filled
+// tail of the last 256-wide tile) are neither computed nor stored.
+// ---------------------------------------------------------------------------------------------
+struct EpiQkvRope {
+  const float *bias;
+  const float *cosv;
+  const float *sinv;
+  static constexpr int kPad = 17;
+  static constexpr int kTab = 14 * kPad;                   // floats per (axis, function)
+  static constexpr int kRopeBytes = ((4 * kTab * 4 + 15) / 16) * 16;
+  static constexpr int kSmem = kRopeBytes + kQkv * 4;       // + bias
+  static constexpr bool kTmaStore = true;
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    float *t = reinterpret_cast<float *>(smem);
+    for (int i = tid; i < 4 * 14 * 16; i += n) {
+      const int which = i / 224, pos = (i / 16) % 14, j = i % 16;
+      // axis 0 (rows): patch pos*14, channel j; axis 1 (columns): patch pos, channel 16+j
+      const int src = (which < 2) ? (pos * 14) * 64 + j : pos * 64 + 16 + j;
+      t[which * kTab + pos * kPad + j] = __ldg(((which & 1) ? sinv : cosv) + src);
+    }
+    stage_floats(reinterpret_cast<float *>(smem + kRopeBytes), bias, kQkv, tid, n);
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+    static_assert(COLS % 64 == 0, "a thread owns whole heads");
+    const int t = c.row % kTokens;
+    const bool patch_row = t >= kPrefix;
+    const int p = patch_row ? t - kPrefix : 0;
+    const float *tab = reinterpret_cast<const float *>(c.smem);
+    const float *sb = reinterpret_cast<const float *>(c.smem + kRopeBytes);
+    const float *cy = tab + (p / 14) * kPad, *sy = tab + kTab + (p / 14) * kPad;
+    const float *cx = tab + 2 * kTab + (p % 14) * kPad, *sx = tab + 3 * kTab + (p % 14) * kPad;
+#pragma unroll 1
+    for (int h = 0; h < COLS; h += 64) {
+      const int col = n0 + h;  // first column of this 64-wide head
+      if (col >= kQkv) break;  // warp-uniform
+      uint32_t ra[32], rb[32];
+      tmem_load32x2(taddr + h, ra, taddr + h + 32, rb);
+      float lo[32], hi[32];
+      lds32(sb + col, lo);
+      lds32(sb + col + 32, hi);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        lo[i] += u2f(ra[i]);
+        hi[i] += u2f(rb[i]);
+      }
+      if (patch_row && col < 2 * kHidden) {  // q and k columns of patch tokens rotate
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float cs = i < 16 ? cy[i] : cx[i - 16];
+          const float sn = i < 16 ? sy[i] : sx[i - 16];
+          const float a = lo[i], b = hi[i];
+          lo[i] = a * cs - b * sn;
+          hi[i] = b * cs + a * sn;
+        }
+      }
+      tma_emit32(c, lo, col);
+      tma_emit32(c, hi, col + 32);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Residual update with LayerScale: x[row][n] = f16(x + lambda[n] (acc + b[n])), in place. The
+// residual row is read one 32-column chunk ahead of its use; the result leaves by TMA store.
+// ---------------------------------------------------------------------------------------------
+struct EpiResid {
+  const float *bias;
+  const float *lambda;
+  const __half *x;
+  static constexpr int kSmem = 2 * kHidden * 4;
+  static constexpr bool kTmaStore = true;
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    float *s = reinterpret_cast<float *>(smem);
+    stage_floats(s, bias, kHidden, tid, n);
+    stage_floats(s + kHidden, lambda, kHidden, tid, n);
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+    const float *sb = reinterpret_cast<const float *>(c.smem);
+    const float *sl = sb + kHidden;
+    const bool ok = c.row < c.M;
+    const __half *xr = x + static_cast<size_t>(c.row) * kHidden + n0;
+    uint4 cur[4] = {}, nxt[4] = {};
+    if (ok) ldg_half32(xr, cur);
+#pragma unroll 1
+    for (int k = 0; k < COLS; k += 32) {
+      if (ok && k + 32 < COLS) ldg_half32(xr + k + 32, nxt);
+      uint32_t r[32];
+      tmem_load32(taddr + k, r);
+      float v[32], b[32], l[32];
+      unpack_half32(cur, v);
+      lds32(sb + n0 + k, b);
+      lds32(sl + n0 + k, l);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += l[i] * (u2f(r[i]) + b[i]);
+      tma_emit32(c, v, n0 + k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Gate/up with SwiGLU: the weight rows are packed 64 gate rows, the matching 64 up rows, ...;
+// act[row][j] = f16(silu(g + bg) (u + bu)), silu through the hardware tanh (one MUFU op).
+// ---------------------------------------------------------------------------------------------
+struct EpiSwiGLU {
+  const float *bias;  // packed like the weight rows
+  static constexpr int kSmem = kGateUp * 4;
+  static constexpr bool kTmaStore = true;
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    stage_floats(reinterpret_cast<float *>(smem), bias, kGateUp, tid, n);
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+    static_assert(COLS % 128 == 0, "a thread owns whole 64 gate + 64 up groups");
+    const float *sb = reinterpret_cast<const float *>(c.smem);
+#pragma unroll 1
+    for (int g = 0; g < COLS; g += 128) {
+#pragma unroll 1
+      for (int half = 0; half < 64; half += 32) {
+        uint32_t rg[32], ru[32];
+        tmem_load32x2(taddr + g + half, rg, taddr + g + 64 + half, ru);
+        float gv[32], uv[32];
+        lds32(sb + n0 + g + half, gv);
+        lds32(sb + n0 + g + 64 + half, uv);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i] + u2f(rg[i])) * (uv[i] + u2f(ru[i]));
+        tma_emit32(c, gv, (n0 + g) / 2 + half);
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Residual update fused with the following LayerNorm, for full-row tiles (BN = 384):
+//   x[row] = f16(x + lambda (acc + b))                        (matmul_resid_f16_wmma.loom)
+//   h[row] = f16(LN(x[row]))  or  out[row] = LN(x[row]) f32   (layernorm_rowwave_*.loom)
+// The two threads that own a row (one per column half) each hold 192 columns: pass 1 writes x
+// and puts the f16-rounded x back into TMEM (over the accumulator) while summing it; the halves
+// meet in shared memory for the mean; pass 2 sums squared deviations (same exchange); pass 3
+// normalises. eps 1e-5, f32 arithmetic, biased variance. Rows are written directly.
+// ---------------------------------------------------------------------------------------------
+struct EpiResidLN {
+  const float *bias;
+  const float *lambda;
+  __half *x;
+  const float *gamma;
+  const float *beta;
+  __half *h;       // f16 LayerNorm output, or
+  float *out_f32;  // f32 LayerNorm output (the final norm) when non-null
+  static constexpr int kRed = 4 * kHidden * 4;            // after bias, lambda, gamma, beta
+  static constexpr int kSmem = kRed + 4 * 128 * 4;         // + [sum | sq][half][row]
+  static constexpr bool kTmaStore = false;
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    float *s = reinterpret_cast<float *>(smem);
+    stage_floats(s, bias, kHidden, tid, n);
+    stage_floats(s + kHidden, lambda, kHidden, tid, n);
+    stage_floats(s + 2 * kHidden, gamma, kHidden, tid, n);
+    stage_floats(s + 3 * kHidden, beta, kHidden, tid, n);
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+    const float *sb = reinterpret_cast<const float *>(c.smem);
+    const float *sl = sb + kHidden, *sg = sb + 2 * kHidden, *sbe = sb + 3 * kHidden;
+    float *red = reinterpret_cast<float *>(c.smem + kRed);
+    const int row = c.row, half = c.half, r = c.r;
+    const bool ok = row < c.M;
+    __half *xr = x + static_cast<size_t>(row) * kHidden + n0;
+    uint4 cur[4] = {}, nxt[4] = {};
+    if (ok) ldg_half32(xr, cur);
+    float s = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < COLS; k += 32) {
+      if (ok && k + 32 < COLS) ldg_half32(xr + k + 32, nxt);
+      uint32_t acc[32];
+      tmem_load32(taddr + k, acc);
+      float v[32];
+      if (ok) {
+        float b[32], l[32];
+        unpack_half32(cur, v);
+        lds32(sb + n0 + k, b);
+        lds32(sl + n0 + k, l);
+        uint4 *dst = reinterpret_cast<uint4 *>(xr + k);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * j + 2 * e;
+            pk[e] = pack_half2(v[i] + l[i] * (u2f(acc[i]) + b[i]),
+                               v[i + 1] + l[i + 1] * (u2f(acc[i + 1]) + b[i + 1]));
+            const float2 rounded = unpack_half2(pk[e]);  // the LayerNorm reads the stored f16
+            v[i] = rounded.x;
+            v[i + 1] = rounded.y;
+          }
+          dst[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        s += v[i];
+        acc[i] = __float_as_uint(v[i]);
+      }
+      tmem_st32(taddr + k, acc);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+    }
+    tmem_st_wait();
+    red[half * 128 + r] = s;
+    named_barrier(1, kEpilogueThreads);
+    const float mean = (red[r] + red[128 + r]) * (1.0f / kHidden);
+    float d = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < COLS; k += 32) {
+      uint32_t v[32];
+      tmem_load32(taddr + k, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float t = u2f(v[i]) - mean;
+        d += t * t;
+      }
+    }
+    red[256 + half * 128 + r] = d;
+    named_barrier(1, kEpilogueThreads);
+    const float rstd = rsqrtf((red[256 + r] + red[384 + r]) * (1.0f / kHidden) + 1e-5f);
+#pragma unroll 1
+    for (int k = 0; k < COLS; k += 32) {
+      uint32_t v[32];
+      tmem_load32(taddr + k, v);
+      float g[32], b[32], y[32];
+      lds32(sg + n0 + k, g);
+      lds32(sbe + n0 + k, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) y[i] = (u2f(v[i]) - mean) * rstd * g[i] + b[i];
+      if (ok) {
+        if (out_f32) {
+          float4 *o = reinterpret_cast<float4 *>(out_f32 + static_cast<size_t>(row) * kHidden + n0 + k);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+        } else {
+          store_half32(h + static_cast<size_t>(row) * kHidden + n0 + k, y);
+        }
+      }
+    }
+    named_barrier(1, kEpilogueThreads);  // `red` is reused by the next tile
+  }
+};
+
+}  // namespace dv3

@@ -26,9 +26,16 @@ constexpr int kImageElements = 3 * 224 * 224;
 // swizzle (box_cols must be 64), out-of-bounds elements read as zero.
 bool encode_map_f16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
                     uint32_t box_cols, uint32_t box_rows, std::string *err);
+// The same with a 32-, 64- or 128-byte swizzle (box_cols * 2 must equal the swizzle width).
+bool encode_map_f16_swizzled(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                             uint32_t box_cols, uint32_t box_rows, uint32_t swizzle_bytes,
+                             std::string *err);
 
 // ---- GEMM operations (gemm.cu) ----
-enum class GemmOp { Patch, QkvRope, Resid384, Resid1536, SwiGLU };
+// Resid*: x += lambda (A W^T + b) on 128-column tiles. ResidLN*: the same on full 384-column
+// rows, followed in the same kernel by the LayerNorm of the updated row into ln_out (f16) or
+// ln_out_f32.
+enum class GemmOp { Patch, QkvRope, Resid384, Resid1536, SwiGLU, ResidLN384, ResidLN1536 };
 
 struct GemmShape {
   int bn;      // tile width along N
@@ -41,9 +48,11 @@ GemmShape gemm_shape(GemmOp op);
 struct GemmMaps {
   CUtensorMap a;
   CUtensorMap b;
+  CUtensorMap c;  // the epilogue's output, for epilogues that store through TMA
 };
-bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, GemmMaps *maps,
-                    std::string *err);
+// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch and ResidLN*).
+bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
+                    GemmMaps *maps, std::string *err);
 
 struct GemmArgs {
   const float *bias = nullptr;
@@ -51,6 +60,10 @@ struct GemmArgs {
   const float *rope_cos = nullptr;  // QkvRope
   const float *rope_sin = nullptr;
   __half *out = nullptr;  // Patch: x; QkvRope: qkv; Resid*: x (in place); SwiGLU: act
+  const float *gamma = nullptr;  // ResidLN*: LayerNorm weight and bias
+  const float *beta = nullptr;
+  __half *ln_out = nullptr;      // ResidLN*: f16 LayerNorm output, or
+  float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
 };
 
 cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const GemmArgs &args,

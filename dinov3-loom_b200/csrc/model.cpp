@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 
 #include "weights.h"
@@ -170,8 +171,18 @@ void Model::release() {
 }
 
 // The launch plan of one batch size (src/lib.rs:149-263): patchify, patch GEMM (with the
-// embed scatter), LN1 of layer 0, then per layer QKV+RoPE, attention, o-proj+LS1+residual,
-// LN2, gate/up+SwiGLU, down-proj+LS2+residual, and LN1 of the next layer or the final LN.
+// embed scatter), LN1 of layer 0, then per layer QKV+RoPE, attention, o-proj+LS1+residual+LN2,
+// gate/up+SwiGLU, and down-proj+LS2+residual+(LN1 of the next layer | final LN). The reference
+// launches each LayerNorm separately (87 launches at b > 1); here each one after layer 0's
+// first rides in the epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches).
+// Full-row tiles give ceil(201b/128) CTAs, too few for small batches, which therefore keep the
+// 128-column residual GEMMs and separate LayerNorm launches (3 + 12*7 = 87 launches).
+// DV3_FUSE_LAYERNORM=0/1 in the environment overrides the choice (for measurement).
+bool Model::fuse_layernorm(size_t b) const {
+  if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
+  return b >= kFuseLayerNormMinBatch;
+}
+
 Plan &Model::prepare(size_t b) {
   auto it = plans_.find(b);
   if (it != plans_.end()) return it->second;
@@ -194,7 +205,7 @@ Plan &Model::prepare(size_t b) {
   __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
 
   GemmMaps patch_maps;
-  need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, &patch_maps, &err));
+  need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, x, &patch_maps, &err));
   CUtensorMap attn_map;
   need(make_attention_map(qkv, r, &attn_map, &err));
 
@@ -210,13 +221,16 @@ Plan &Model::prepare(size_t b) {
   add("layernorm_f16", [=](cudaStream_t s) {
     return launch_layernorm_f16(x, r, w.layer[0].norm1_w, w.layer[0].norm1_b, h, s);
   });
+  const bool fuse = fuse_layernorm(b);
+  const GemmOp o_op = fuse ? GemmOp::ResidLN384 : GemmOp::Resid384;
+  const GemmOp down_op = fuse ? GemmOp::ResidLN1536 : GemmOp::Resid1536;
   for (int i = 0; i < 12; ++i) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
-    need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, &qkv_maps, &err));
-    need(make_gemm_maps(GemmOp::Resid384, attn, r, l.o_w, &o_maps, &err));
-    need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, &gu_maps, &err));
-    need(make_gemm_maps(GemmOp::Resid1536, act, r, l.down_w, &down_maps, &err));
+    need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, qkv, &qkv_maps, &err));
+    need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err));
+    need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, act, &gu_maps, &err));
+    need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err));
     add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;
@@ -226,38 +240,52 @@ Plan &Model::prepare(size_t b) {
       return launch_gemm(GemmOp::QkvRope, qkv_maps, r, g, st, s);
     });
     add("attention", [=](cudaStream_t s) { return launch_attention(attn_map, r, attn, st, s); });
-    add(gemm_name(GemmOp::Resid384), [=](cudaStream_t s) {
+    // o-proj + LayerScale 1 + residual, and LN2 of this layer (fused or separate): x -> x, h
+    add(gemm_name(o_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.o_b;
       g.lambda = l.ls1;
       g.out = x;
-      return launch_gemm(GemmOp::Resid384, o_maps, r, g, st, s);
+      g.gamma = l.norm2_w;
+      g.beta = l.norm2_b;
+      g.ln_out = h;
+      return launch_gemm(o_op, o_maps, r, g, st, s);
     });
-    add("layernorm_f16", [=](cudaStream_t s) {
-      return launch_layernorm_f16(x, r, l.norm2_w, l.norm2_b, h, s);
-    });
+    if (!fuse)
+      add("layernorm_f16", [=](cudaStream_t s) {
+        return launch_layernorm_f16(x, r, l.norm2_w, l.norm2_b, h, s);
+      });
     add(gemm_name(GemmOp::SwiGLU), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.gateup_b;
       g.out = act;
       return launch_gemm(GemmOp::SwiGLU, gu_maps, r, g, st, s);
     });
-    add(gemm_name(GemmOp::Resid1536), [=](cudaStream_t s) {
+    // down-proj + LayerScale 2 + residual, fused with LN1 of the next layer (f16 h) or, after
+    // the last layer, with the final LayerNorm (f32 output)
+    const bool last = i == 11;
+    const float *ng = last ? w.norm_w : w.layer[i + 1].norm1_w;
+    const float *nb = last ? w.norm_b : w.layer[i + 1].norm1_b;
+    add(gemm_name(down_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.down_b;
       g.lambda = l.ls2;
       g.out = x;
-      return launch_gemm(GemmOp::Resid1536, down_maps, r, g, st, s);
+      g.gamma = ng;
+      g.beta = nb;
+      g.ln_out = last ? nullptr : h;
+      g.ln_out_f32 = last ? out : nullptr;
+      return launch_gemm(down_op, down_maps, r, g, st, s);
     });
-    if (i < 11) {
-      const LayerWeights &n = w.layer[i + 1];
-      add("layernorm_f16", [=](cudaStream_t s) {
-        return launch_layernorm_f16(x, r, n.norm1_w, n.norm1_b, h, s);
-      });
-    } else {
-      add("layernorm_f32out", [=](cudaStream_t s) {
-        return launch_layernorm_f32(x, r, w.norm_w, w.norm_b, out, s);
-      });
+    if (!fuse) {
+      if (last)
+        add("layernorm_f32out", [=](cudaStream_t s) {
+          return launch_layernorm_f32(x, r, ng, nb, out, s);
+        });
+      else
+        add("layernorm_f16", [=](cudaStream_t s) {
+          return launch_layernorm_f16(x, r, ng, nb, h, s);
+        });
     }
   }
 

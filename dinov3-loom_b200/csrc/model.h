@@ -47,6 +47,11 @@ struct Plan {
   size_t kernels = 0;
 };
 
+// Smallest batch whose plan fuses each LayerNorm into the residual GEMM before it. Measured on
+// B200, the full-row tiles that fusion needs lose to the 128-wide tiles plus a separate
+// LayerNorm at every batch size up to 64, so no resident batch fuses by default.
+constexpr size_t kFuseLayerNormMinBatch = DV3_MAX_BATCH_LIMIT + 1;
+
 class Model {
  public:
   Model(const std::string &path, dv3_options options);
@@ -71,6 +76,7 @@ class Model {
   void check_usable() const;
   void cuda(cudaError_t e, const char *what);  // poisons and throws on failure
   Plan &prepare(size_t batch);                  // build + capture once per batch size
+  bool fuse_layernorm(size_t batch) const;      // plan variant for this batch size
   void check_status();                          // read the device status words (synchronous)
   void activate() const;
   void release();  // free every device resource (idempotent)

@@ -107,6 +107,30 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// Store a box from shared memory to global memory at element coordinates (x, y); the box's
+// rows past the tensor's extent are not written. Completion is tracked per thread in bulk
+// groups (bulk_commit / bulk_wait_*).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N of this thread's bulk groups are incomplete (writes done).
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA and
 // the tensor cores read shared memory through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -194,6 +218,29 @@ __device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[32]) {
   asm volatile("" : DV3_R32(r));
 }
 
+// 32 lanes x 32 consecutive 32-bit columns from registers: thread i writes lane taddr.lane + i.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Barrier over the `nthreads` threads (a multiple of 32) that use named barrier `id` (1..15).
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Load 32 columns and wait for them.
 __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
   tmem_ld32(taddr, r);
@@ -232,6 +279,19 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n, boo
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Hardware tanh approximation (one MUFU operation).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// silu(a) = a * sigmoid(a) = h + h * tanh(h) with h = a / 2.
+__device__ __forceinline__ float silu(float a) {
+  const float h = 0.5f * a;
+  return fmaf(h, tanh_approx(h), h);
 }
 
 __device__ __forceinline__ float2 unpack_half2(uint32_t v) {

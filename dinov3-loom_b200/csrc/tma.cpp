@@ -26,10 +26,25 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string *err) {
 
 bool encode_map_f16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
                     uint32_t box_cols, uint32_t box_rows, std::string *err) {
+  return encode_map_f16_swizzled(map, base, cols, rows, box_cols, box_rows, 128, err);
+}
+
+bool encode_map_f16_swizzled(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                             uint32_t box_cols, uint32_t box_rows, uint32_t swizzle_bytes,
+                             std::string *err) {
   auto fn = encode_fn(err);
   if (!fn) return false;
+  CUtensorMapSwizzle sw;
+  switch (swizzle_bytes) {
+    case 32: sw = CU_TENSOR_MAP_SWIZZLE_32B; break;
+    case 64: sw = CU_TENSOR_MAP_SWIZZLE_64B; break;
+    case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
+    default:
+      if (err) *err = "tensor map: unsupported swizzle";
+      return false;
+  }
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0 || rows == 0 ||
-      box_cols * 2 != 128 || box_rows == 0 || box_rows > 256) {
+      box_cols * 2 != swizzle_bytes || box_rows == 0 || box_rows > 256) {
     if (err) *err = "tensor map: base must be 16-byte aligned, rows of whole 16-byte units";
     return false;
   }
@@ -38,7 +53,7 @@ bool encode_map_f16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t 
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t elem[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
-                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     if (err) {

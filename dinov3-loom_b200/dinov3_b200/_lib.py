@@ -77,6 +77,7 @@ SIGNATURES = {
     "dv3k_qkv_rope": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_attention": ([_P, _U32, _P, _P, _P], _I),
     "dv3k_matmul_resid": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P], _I),
+    "dv3k_matmul_resid_layernorm": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_swiglu": ([_P, _U32, _P, _P, _P, _P, _P], _I),
     "dv3k_gateup_source_row": ([_U32], _U32),
 }

@@ -95,6 +95,18 @@ int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16
                       const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
                       void *stream);
 
+/* Projection with LayerScale and residual followed by the LayerNorm of the updated rows, in one
+ * kernel on full 384-column row tiles. Replaces kernels/matmul_resid_f16_wmma.loom followed by
+ * kernels/layernorm_rowwave_f16.loom (or kernels/layernorm_rowwave_f32out.loom for the final
+ * norm), which the reference launches separately (src/lib.rs:200-211,227-253):
+ *   x[row] = f16(x + lambda * (a @ w^T + bias));
+ *   h[row] = f16(LN(x[row]) * gamma + beta), or, when h is NULL, out_f32[row] = the same in f32.
+ * The LayerNorm reads the f16-rounded x, eps 1e-5. k is 384 or 1536. */
+int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
+                                const float *bias, const float *lambda, uint16_t *x,
+                                const float *gamma, const float *beta, uint16_t *h,
+                                float *out_f32, uint32_t *status, void *stream);
+
 /* Gate/up projection with SwiGLU: act[row][j] = f16(silu(g) * u), g = h@Wg^T+bg, u = h@Wu^T+bu,
  * j < 1536, from the interleaved gateup_w / gateup_b. Replaces
  * kernels/matmul_swiglu_f16_wmma.loom (k=384, n=1536). */

@@ -217,6 +217,39 @@ def test_matmul_resid(k, b):
     assert_close16(x, ref)
 
 
+@pytest.mark.parametrize("f32_out", [False, True])
+@pytest.mark.parametrize("k", [384, 1536])
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_matmul_resid_layernorm(k, b, f32_out):
+    rng = np.random.default_rng(70 + b + k + f32_out)
+    r = rows_of(b)
+    a = f16(rng.standard_normal((r, k)))
+    w = f16(rng.standard_normal((384, k)) / np.sqrt(k))
+    bias = rng.standard_normal(384) * 0.1
+    lam = rng.random(384) * 0.2 + 0.05
+    x0 = f16(rng.standard_normal((r, 384)) + rng.standard_normal((r, 1)))
+    g = rng.standard_normal(384) * 0.3 + 1
+    be = rng.standard_normal(384) * 0.1
+    ref_x = x0 + lam.astype(np.float32) * (a @ w.T + bias.astype(np.float32))
+    x = t16(x0)
+    h = None if f32_out else torch.empty((r, 384), dtype=torch.float16, device=DEV)
+    o = torch.empty((r, 384), dtype=torch.float32, device=DEV) if f32_out else None
+    st = status()
+    check_rc(lib().dv3k_matmul_resid_layernorm(ptr(t16(a)), r, k, ptr(t16(w)), ptr(t32(bias)),
+                                               ptr(t32(lam)), ptr(x), ptr(t32(g)), ptr(t32(be)),
+                                               ptr(h), ptr(o), ptr(st), stream()))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist() == [0, 0]
+    assert_close16(x, ref_x)
+    # the LayerNorm normalises the stored f16 rows
+    ref_ln = ref_numpy.norm(x.float().cpu().numpy().astype(np.float64), g.astype(np.float32),
+                            be.astype(np.float32))
+    if f32_out:
+        assert np.abs(o.cpu().numpy() - ref_ln).max() < 1e-4
+    else:
+        assert_close16(h, ref_ln)
+
+
 @pytest.mark.parametrize("b", [1, 3, 64])
 def test_matmul_swiglu(b):
     rng = np.random.default_rng(60 + b)

@@ -196,6 +196,27 @@ def test_benchmark_and_profile(models):
     with pytest.raises(dv.DINOv3Error):
         model.benchmark(np.zeros(0, np.float32), 10)
     prof = model.profile_launches(2, 2)
-    # patchify, patch GEMM, LN1 of layer 0, then 7 per layer (src/lib.rs:149-263 has 87 at b>1)
+    # small batches: patchify, patch GEMM, LN1 of layer 0, then per layer QKV, attention, o,
+    # LN2, gate/up, down, LN (the reference's plan, src/lib.rs:149-263, also has 87 at b > 1)
     assert len(prof) == model.launches_per_forward(2) == 3 + 12 * 7
     assert all(ms > 0 for _, ms in prof)
+    assert sum(name.startswith("layernorm") for name, _ in prof) == 25
+
+
+def test_fused_layernorm_plan(weights_file, monkeypatch):
+    """The plan variant that rides each LayerNorm after the first in the preceding residual GEMM
+    (3 + 12*5 launches; DV3_FUSE_LAYERNORM=1, read when a batch size's graph is built) gives the
+    same result as the default plan within f16 rounding."""
+    path = weights_file(1, "stress")
+    images = synth.images(31, 16)
+    with dv.DINOv3.load(path, dv.Options(0, 16)) as model:
+        assert model.launches_per_forward(16) == 3 + 12 * 7
+        split = model.forward(images)
+    monkeypatch.setenv("DV3_FUSE_LAYERNORM", "1")
+    with dv.DINOv3.load(path, dv.Options(0, 16)) as model:
+        assert model.launches_per_forward(16) == 3 + 12 * 5
+        fused = model.forward(images)
+        prof = model.profile_launches(16, 1)
+    assert [n for n, _ in prof].count("gemm_down_resid_layernorm") == 12
+    for i in range(16):
+        assert cos(fused[i], split[i]) > 0.99999
