@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the QKV rows of the previous kernel are complete from here on
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(&bars[0], 5 * 16384);
@@ -235,9 +237,8 @@ cudaError_t launch_attention(const CUtensorMap &map, uint32_t rows, __half *out,
     configured[dev] = true;
   }
   const dim3 grid(2, 6, rows / kTokens);
-  attention_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(map, static_cast<int>(rows), out,
-                                                               status);
-  return cudaGetLastError();
+  return launch_pdl(attention_kernel, grid, dim3(kAttnThreads), kAttnSmem, stream, map,
+                    static_cast<int>(rows), out, status);
 }
 
 }  // namespace dv3

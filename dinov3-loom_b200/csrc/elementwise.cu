@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(256)
     patchify_kernel(const float *__restrict__ images, int n_images,
                     const float *__restrict__ prefix, __half *__restrict__ patches,
                     __half *__restrict__ x, uint32_t *status) {
+  pdl_wait();  // the input upload (and the previous forward's readers) are done from here on
+  pdl_trigger();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n_patch_chunks = static_cast<int64_t>(n_images) * kPatches * 96;
   const int64_t n_prefix_chunks = static_cast<int64_t>(n_images) * kPrefix * 48;
@@ -65,6 +67,8 @@ template <bool kF32Out>
 __global__ void __launch_bounds__(256)
     layernorm_kernel(const __half *__restrict__ x, int rows, const float *__restrict__ gamma,
                      const float *__restrict__ beta, void *__restrict__ out) {
+  pdl_wait();  // the rows written by the previous kernel are complete from here on
+  pdl_trigger();
   const int row = blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= rows) return;  // whole warp leaves together
@@ -125,25 +129,22 @@ cudaError_t launch_patchify(const float *images, uint32_t n_images, const float 
   if (n_images == 0) return cudaSuccess;
   const int64_t total = static_cast<int64_t>(n_images) * (kPatches * 96 + kPrefix * 48);
   const int blocks = static_cast<int>((total + 255) / 256);
-  patchify_kernel<<<blocks, 256, 0, stream>>>(images, static_cast<int>(n_images), prefix, patches,
-                                              x, status);
-  return cudaGetLastError();
+  return launch_pdl(patchify_kernel, dim3(blocks), dim3(256), 0, stream, images,
+                    static_cast<int>(n_images), prefix, patches, x, status);
 }
 
 cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, __half *out, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
-  layernorm_kernel<false><<<(rows + 7) / 8, 256, 0, stream>>>(x, static_cast<int>(rows), gamma,
-                                                              beta, out);
-  return cudaGetLastError();
+  return launch_pdl(layernorm_kernel<false>, dim3((rows + 7) / 8), dim3(256), 0, stream, x,
+                    static_cast<int>(rows), gamma, beta, static_cast<void *>(out));
 }
 
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, float *out, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
-  layernorm_kernel<true><<<(rows + 7) / 8, 256, 0, stream>>>(x, static_cast<int>(rows), gamma,
-                                                             beta, out);
-  return cudaGetLastError();
+  return launch_pdl(layernorm_kernel<true>, dim3((rows + 7) / 8), dim3(256), 0, stream, x,
+                    static_cast<int>(rows), gamma, beta, static_cast<void *>(out));
 }
 
 int sm_count(int device) {

@@ -110,10 +110,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
-  epi.init(extra, threadIdx.x, kGemmThreads);
+  epi.init(extra, threadIdx.x, kGemmThreads);  // weights only: may overlap the previous kernel
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // activations of the previous kernel are complete from here on
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = ((M + BM - 1) / BM) * n_tiles_n;
 
@@ -212,6 +214,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile / n_tiles_n) * BM;
+      const int n0 = (tile % n_tiles_n) * BN + half * kCols;
+      ctx.row = m0 + row_in_tile;
+      ctx.row0 = m0 + q * 32;
+      typename Epi::Pre pre = epi.prefetch(n0, ctx);
       const bool waited = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) {
@@ -221,12 +228,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m0 = (tile / n_tiles_n) * BM;
-      const int n0 = (tile % n_tiles_n) * BN + half * kCols;
-      ctx.row = m0 + row_in_tile;
-      ctx.row0 = m0 + q * 32;
       epi.template run<kCols>(
-          tmem_base + lane_base + static_cast<uint32_t>(acc * BN + half * kCols), n0, ctx);
+          tmem_base + lane_base + static_cast<uint32_t>(acc * BN + half * kCols), n0, ctx, pre);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == C::kAccBufs) {
@@ -317,9 +320,9 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
   const int n_tiles_n = (n + BN - 1) / BN;
   const int tiles = static_cast<int>((rows + BM - 1) / BM) * n_tiles_n;
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
-  gemm_kernel<BN, Epi><<<grid, kGemmThreads, gemm_smem_bytes<BN, Epi>(), stream>>>(
-      maps.a, maps.b, maps.c, static_cast<int>(rows), n_tiles_n, k / BK, epi, status);
-  return cudaGetLastError();
+  return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
+                    gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c,
+                    static_cast<int>(rows), n_tiles_n, k / BK, epi, status);
 }
 
 // Set the shared-memory limits of every GEMM instance on the current device (done at load, so

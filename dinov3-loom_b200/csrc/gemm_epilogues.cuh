@@ -7,7 +7,10 @@
 //       all CTA threads, before the first barrier: stage per-column vectors (bias, LayerScale,
 //       gamma, beta, RoPE angles) into shared memory, so the per-row work reads them as
 //       shared-memory broadcasts instead of global loads
-//   template <int COLS> void run(uint32_t taddr, int n0, EpiCtx &ctx)
+//   struct Pre; Pre prefetch(int n0, const EpiCtx &ctx)
+//       called before the wait for the tile's accumulator: loads that do not depend on the
+//       MMAs (the residual row) start here and overlap the wait
+//   template <int COLS> void run(uint32_t taddr, int n0, EpiCtx &ctx, Pre &pre)
 //       processes COLS accumulator columns starting at TMEM address `taddr` (this warp's lane
 //       quarter) that belong to output columns n0..n0+COLS-1 of output row ctx.row. ctx.row may
 //       be >= M on the last M tile: TMEM loads still run, because tcgen05.ld is
@@ -43,6 +46,8 @@ struct EpiCtx {
   int buf;             // staging block to use next
   const CUtensorMap *out_map;
 };
+
+struct NoPre {};
 
 __device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
 
@@ -122,11 +127,13 @@ struct EpiPatch {
   __half *x;
   static constexpr int kSmem = kHidden * 4;
   static constexpr bool kTmaStore = false;
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     stage_floats(reinterpret_cast<float *>(smem), bias, kHidden, tid, n);
   }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
     const float *sb = reinterpret_cast<const float *>(c.smem);
     const bool ok = c.row < c.M;
     const int token = (c.row / kPatches) * kTokens + kPrefix + c.row % kPatches;
@@ -161,6 +168,8 @@ struct EpiQkvRope {
   static constexpr int kRopeBytes = ((4 * kTab * 4 + 15) / 16) * 16;
   static constexpr int kSmem = kRopeBytes + kQkv * 4;       // + bias
   static constexpr bool kTmaStore = true;
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     float *t = reinterpret_cast<float *>(smem);
     for (int i = tid; i < 4 * 14 * 16; i += n) {
@@ -172,7 +181,7 @@ struct EpiQkvRope {
     stage_floats(reinterpret_cast<float *>(smem + kRopeBytes), bias, kQkv, tid, n);
   }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
     static_assert(COLS % 64 == 0, "a thread owns whole heads");
     const int t = c.row % kTokens;
     const bool patch_row = t >= kPrefix;
@@ -221,19 +230,29 @@ struct EpiResid {
   const __half *x;
   static constexpr int kSmem = 2 * kHidden * 4;
   static constexpr bool kTmaStore = true;
+  struct Pre {
+    uint4 q[4];
+  };
+  // The first 32 columns of the residual row, before the accumulator wait.
+  __device__ Pre prefetch(int n0, const EpiCtx &c) const {
+    Pre p{};
+    if (c.row < c.M) ldg_half32(x + static_cast<size_t>(c.row) * kHidden + n0, p.q);
+    return p;
+  }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     float *s = reinterpret_cast<float *>(smem);
     stage_floats(s, bias, kHidden, tid, n);
     stage_floats(s + kHidden, lambda, kHidden, tid, n);
   }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
     const float *sb = reinterpret_cast<const float *>(c.smem);
     const float *sl = sb + kHidden;
     const bool ok = c.row < c.M;
     const __half *xr = x + static_cast<size_t>(c.row) * kHidden + n0;
-    uint4 cur[4] = {}, nxt[4] = {};
-    if (ok) ldg_half32(xr, cur);
+    uint4 cur[4], nxt[4] = {};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cur[j] = pre.q[j];
 #pragma unroll 1
     for (int k = 0; k < COLS; k += 32) {
       if (ok && k + 32 < COLS) ldg_half32(xr + k + 32, nxt);
@@ -260,11 +279,13 @@ struct EpiSwiGLU {
   const float *bias;  // packed like the weight rows
   static constexpr int kSmem = kGateUp * 4;
   static constexpr bool kTmaStore = true;
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     stage_floats(reinterpret_cast<float *>(smem), bias, kGateUp, tid, n);
   }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
     static_assert(COLS % 128 == 0, "a thread owns whole 64 gate + 64 up groups");
     const float *sb = reinterpret_cast<const float *>(c.smem);
 #pragma unroll 1
@@ -304,6 +325,8 @@ struct EpiResidLN {
   static constexpr int kRed = 4 * kHidden * 4;            // after bias, lambda, gamma, beta
   static constexpr int kSmem = kRed + 4 * 128 * 4;         // + [sum | sq][half][row]
   static constexpr bool kTmaStore = false;
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     float *s = reinterpret_cast<float *>(smem);
     stage_floats(s, bias, kHidden, tid, n);
@@ -312,7 +335,7 @@ struct EpiResidLN {
     stage_floats(s + 3 * kHidden, beta, kHidden, tid, n);
   }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c) const {
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
     const float *sb = reinterpret_cast<const float *>(c.smem);
     const float *sl = sb + kHidden, *sg = sb + 2 * kHidden, *sbe = sb + 3 * kHidden;
     float *red = reinterpret_cast<float *>(c.smem + kRed);

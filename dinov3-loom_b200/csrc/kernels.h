@@ -91,4 +91,23 @@ inline uint32_t gateup_source_row(uint32_t packed) {
 
 int sm_count(int device);
 
+// Launch `kernel` with programmatic stream serialization (see pdl_wait in sm100.cuh), so its
+// launch and set-up overlap the tail of the previous kernel on the stream; inside stream capture
+// the edge becomes a programmatic dependency of the graph.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args &&...args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 }  // namespace dv3

@@ -35,6 +35,17 @@ __device__ __forceinline__ void report(uint32_t *status, uint32_t bit) {
   if (status) atomicOr(status, bit);
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may
+// start while the kernel before it on the stream is still running: it does its set-up (barrier
+// init, TMEM allocation, staging of weights), then pdl_wait() blocks until that kernel has
+// completed and its writes are visible, before any read of activations or any global write.
+// pdl_trigger() lets the next kernel start its own set-up once every CTA of this one has issued
+// it. Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------------
