@@ -149,6 +149,15 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def host_threads() -> int:
+    """Every core this process may run on (torchrun sets OMP_NUM_THREADS=1 for its workers, so
+    the OpenMP default is not used)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_oracle_throughput(images, budget_s: float, threads: int | None = None):
     """images/s of the float64 C oracle on this host; returns (value, cores, sample, step_times)."""
     import numpy as np
@@ -156,7 +165,7 @@ def cpu_oracle_throughput(images, budget_s: float, threads: int | None = None):
     import ref_c
     from dinov3_b200 import synth
 
-    threads = threads or ref_c.max_threads()
+    threads = threads or host_threads()
     model = ref_c.Model(synth.weights(0, "baseline"))
     n = max(1, threads)
     sample = np.ascontiguousarray(images[:n] if len(images) >= n else np.resize(images, (n,) + images.shape[1:]))
@@ -175,7 +184,7 @@ def run_reference(args):
     import ref_c
     from dinov3_b200 import synth
 
-    threads = ref_c.max_threads()
+    threads = host_threads()
     images = synth.images(1000, threads)
     model = ref_c.Model(synth.weights(0, "baseline"))
     # One step = one float64 forward of `threads` images (one per thread), OpenMP over images.

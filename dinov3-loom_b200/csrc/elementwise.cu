@@ -6,7 +6,7 @@
 //   pixels: two 16-byte loads of a 32-byte run of one image row, one 16-byte store. It also
 //   flags any non-finite pixel (the check of src/lib.rs:95), so the host never scans the input.
 //
-// layernorm: one warp per 384-channel row (kernels/layernorm_rowwave_f16.loom and _f32out).
+// layernorm: a warp per two 384-channel rows (kernels/layernorm_rowwave_f16.loom and _f32out).
 //   Lane l holds channels 8l..8l+7 (one 16-byte load) and 256+4l..256+4l+3 (one 8-byte load):
 //   both loads are contiguous across the warp. Mean and variance are reduced with shuffles in
 //   two passes over the registers (the reference's E[x^2]-mean^2 is replaced by the better
@@ -63,41 +63,32 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Rows per warp: both rows' loads are issued before either is reduced, so each warp keeps two
+// independent memory round trips in flight and the grid (12,864 rows at batch 64) fits in one
+// wave of resident warps.
+constexpr int kLnRowsPerWarp = 2;
+constexpr int kLnRowsPerBlock = 8 * kLnRowsPerWarp;
+
 template <bool kF32Out>
 __global__ void __launch_bounds__(256)
     layernorm_kernel(const __half *__restrict__ x, int rows, const float *__restrict__ gamma,
                      const float *__restrict__ beta, void *__restrict__ out) {
   pdl_wait();  // the rows written by the previous kernel are complete from here on
   pdl_trigger();
-  const int row = blockIdx.x * 8 + threadIdx.x / 32;
+  const int row0 = (blockIdx.x * 8 + threadIdx.x / 32) * kLnRowsPerWarp;
   const int lane = threadIdx.x % 32;
-  if (row >= rows) return;  // whole warp leaves together
-  const __half *xr = x + static_cast<int64_t>(row) * kHidden;
-  const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xr) + lane);
-  const uint2 b = __ldg(reinterpret_cast<const uint2 *>(xr + 256) + lane);
-  float v[12];
-  {
-    const uint32_t w[6] = {a.x, a.y, a.z, a.w, b.x, b.y};
-#pragma unroll
-    for (int e = 0; e < 6; ++e) {
-      const float2 f = unpack_half2(w[e]);
-      v[2 * e] = f.x;
-      v[2 * e + 1] = f.y;
-    }
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int e = 0; e < 12; ++e) s += v[e];
-  const float mean = warp_sum(s) * (1.0f / kHidden);
-  float d = 0.f;
-#pragma unroll
-  for (int e = 0; e < 12; ++e) {
-    v[e] -= mean;
-    d += v[e] * v[e];
-  }
-  const float rstd = rsqrtf(warp_sum(d) * (1.0f / kHidden) + 1e-5f);
+  if (row0 >= rows) return;  // whole warp leaves together
   const int c0 = lane * 8, c1 = 256 + lane * 4;
-  float y[12];
+  uint4 a[kLnRowsPerWarp];
+  uint2 b[kLnRowsPerWarp];
+#pragma unroll
+  for (int k = 0; k < kLnRowsPerWarp; ++k) {
+    const int row = row0 + k < rows ? row0 + k : row0;
+    const __half *xr = x + static_cast<int64_t>(row) * kHidden;
+    a[k] = __ldg(reinterpret_cast<const uint4 *>(xr) + lane);
+    b[k] = __ldg(reinterpret_cast<const uint2 *>(xr + 256) + lane);
+  }
+  float g[12], bb[12];
   {
     const float4 g0 = __ldg(reinterpret_cast<const float4 *>(gamma + c0));
     const float4 g1 = __ldg(reinterpret_cast<const float4 *>(gamma + c0) + 1);
@@ -105,22 +96,53 @@ __global__ void __launch_bounds__(256)
     const float4 b0 = __ldg(reinterpret_cast<const float4 *>(beta + c0));
     const float4 b1 = __ldg(reinterpret_cast<const float4 *>(beta + c0) + 1);
     const float4 b2 = __ldg(reinterpret_cast<const float4 *>(beta + c1));
-    const float g[12] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w, g2.x, g2.y, g2.z, g2.w};
-    const float bb[12] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w, b2.x, b2.y, b2.z, b2.w};
+    const float gg[12] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w, g2.x, g2.y, g2.z, g2.w};
+    const float bv[12] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w, b2.x, b2.y, b2.z, b2.w};
+#pragma unroll
+    for (int e = 0; e < 12; ++e) {
+      g[e] = gg[e];
+      bb[e] = bv[e];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kLnRowsPerWarp; ++k) {
+    const int row = row0 + k;
+    float v[12];
+    const uint32_t w[6] = {a[k].x, a[k].y, a[k].z, a[k].w, b[k].x, b[k].y};
+#pragma unroll
+    for (int e = 0; e < 6; ++e) {
+      const float2 f = unpack_half2(w[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 12; ++e) s += v[e];
+    const float mean = warp_sum(s) * (1.0f / kHidden);
+    float d = 0.f;
+#pragma unroll
+    for (int e = 0; e < 12; ++e) {
+      v[e] -= mean;
+      d += v[e] * v[e];
+    }
+    const float rstd = rsqrtf(warp_sum(d) * (1.0f / kHidden) + 1e-5f);
+    float y[12];
 #pragma unroll
     for (int e = 0; e < 12; ++e) y[e] = v[e] * rstd * g[e] + bb[e];
-  }
-  if constexpr (kF32Out) {
-    float *o = static_cast<float *>(out) + static_cast<int64_t>(row) * kHidden;
-    reinterpret_cast<float4 *>(o + c0)[0] = make_float4(y[0], y[1], y[2], y[3]);
-    reinterpret_cast<float4 *>(o + c0)[1] = make_float4(y[4], y[5], y[6], y[7]);
-    reinterpret_cast<float4 *>(o + c1)[0] = make_float4(y[8], y[9], y[10], y[11]);
-  } else {
-    __half *o = static_cast<__half *>(out) + static_cast<int64_t>(row) * kHidden;
-    reinterpret_cast<uint4 *>(o + c0)[0] =
-        make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]), pack_half2(y[4], y[5]),
-                   pack_half2(y[6], y[7]));
-    reinterpret_cast<uint2 *>(o + c1)[0] = make_uint2(pack_half2(y[8], y[9]), pack_half2(y[10], y[11]));
+    if (row >= rows) break;
+    if constexpr (kF32Out) {
+      float *o = static_cast<float *>(out) + static_cast<int64_t>(row) * kHidden;
+      reinterpret_cast<float4 *>(o + c0)[0] = make_float4(y[0], y[1], y[2], y[3]);
+      reinterpret_cast<float4 *>(o + c0)[1] = make_float4(y[4], y[5], y[6], y[7]);
+      reinterpret_cast<float4 *>(o + c1)[0] = make_float4(y[8], y[9], y[10], y[11]);
+    } else {
+      __half *o = static_cast<__half *>(out) + static_cast<int64_t>(row) * kHidden;
+      reinterpret_cast<uint4 *>(o + c0)[0] =
+          make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]), pack_half2(y[4], y[5]),
+                     pack_half2(y[6], y[7]));
+      reinterpret_cast<uint2 *>(o + c1)[0] =
+          make_uint2(pack_half2(y[8], y[9]), pack_half2(y[10], y[11]));
+    }
   }
 }
 
@@ -136,14 +158,16 @@ cudaError_t launch_patchify(const float *images, uint32_t n_images, const float 
 cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, __half *out, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
-  return launch_pdl(layernorm_kernel<false>, dim3((rows + 7) / 8), dim3(256), 0, stream, x,
+  return launch_pdl(layernorm_kernel<false>, dim3((rows + kLnRowsPerBlock - 1) / kLnRowsPerBlock),
+                    dim3(256), 0, stream, x,
                     static_cast<int>(rows), gamma, beta, static_cast<void *>(out));
 }
 
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, float *out, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
-  return launch_pdl(layernorm_kernel<true>, dim3((rows + 7) / 8), dim3(256), 0, stream, x,
+  return launch_pdl(layernorm_kernel<true>, dim3((rows + kLnRowsPerBlock - 1) / kLnRowsPerBlock),
+                    dim3(256), 0, stream, x,
                     static_cast<int>(rows), gamma, beta, static_cast<void *>(out));
 }
 
