@@ -12,10 +12,10 @@ barrier and the max-over-ranks of the timings).
   e2e     the same through the public API with host buffers: dv3_forward on a pinned host input,
           writing a pinned host output, host<->device copies inside the timed region.
   roofline the dominant kernel (gate/up GEMM + SwiGLU, 46.5 % of the FLOPs): its algorithmic FLOPs
-          per launch / its average launch time (CUDA events around each launch on the model's
-          stream, over `--profile-iters` direct replays of the launch plan), against the measured
-          bf16/f16 dense peak (MEASURED_PEAKS.json). `traffic` comes from the committed ncu
-          summary in profiles/ when it lists this kernel.
+          per launch / its average launch time (CUDA event nodes between the launches of a graph
+          replay of the forward on the model's stream, `--profile-iters` replays), against the
+          measured bf16/f16 dense peak (MEASURED_PEAKS.json). `traffic` comes from the committed
+          ncu summary in profiles/ when it lists this kernel.
   cpu_baseline the float64 CPU oracle (C restatement of the reference's own float64 forward,
           tests/support/reference.rs) on this host, OpenMP over images, rank 0 at N = 1 only.
 Reference arm (--impl reference): the same CPU oracle with all host threads, rank 0 only.

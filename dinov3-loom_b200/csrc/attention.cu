@@ -7,7 +7,8 @@
 //   2. S = Q K^T: 4 tcgen05.mma (M=128, N=208, K=16) into TMEM columns 0..207, f32.
 //   3. 8 warps: the two warps of each TMEM lane quarter split a query row's keys (0..127 and
 //      128..207). Pass 1 takes the row max over the 201 valid keys (the halves meet in shared
-//      memory); pass 2 forms w = exp(0.125 s - 0.125 max), sums w in f32 and writes P = f16(w)
+//      memory); pass 2 forms w = exp(0.125 s - 0.125 max) (one FFMA and the hardware exp2), sums
+//      w in f32 and writes P = f16(w)
 //      (keys >= 201 zero) into shared memory in the K-major layout the MMA reads: keys 0..191 as
 //      three 128-byte-swizzled 64-key blocks over the now dead Q and K tiles, keys 192..207 as a
 //      32-byte-swizzled 16-key block.
@@ -79,6 +80,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   pdl_wait();  // the QKV rows of the previous kernel are complete from here on
   pdl_trigger();
 
+  // Thread 0 drives the pipeline and alone polls the mbarriers (bounded waits); the other warps
+  // sleep in __syncthreads, leaving issue slots to the co-resident CTA.
   if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(&bars[0], 5 * 16384);
     const int qx = head * 64, kx = kHidden + head * 64, vx = 2 * kHidden + head * 64;
@@ -87,7 +90,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     tma_load_2d(smem + kK + 16384, &tm, &bars[0], kx, tok0 + 128);
     tma_load_2d(smem + kV, &tm, &bars[0], vx, tok0);
     tma_load_2d(smem + kV + 16384, &tm, &bars[0], vx, tok0 + 128);
-    if (mbar_wait(&bars[0], 0, abort_flag)) {
+    bool ok = mbar_wait(&bars[0], 0, abort_flag);
+    if (ok) {
       tc_fence_after();
       const uint64_t qd = sw128_desc(smem_u32(smem + kQ));
       const uint64_t kd = sw128_desc(smem_u32(smem + kK));
@@ -95,43 +99,45 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
       for (int k = 0; k < 4; ++k) umma_f16(tmem, qd + 2 * k, kd + 2 * k, idesc, k > 0);
       umma_commit(&bars[1]);
-    } else {
+      ok = mbar_wait(&bars[1], 0, abort_flag);
+    }
+    if (!ok) {
       report(status, kErrAttentionWait);
       *abort_flag = 1;
     }
   }
+  tc_fence_before();
+  __syncthreads();  // S is in TMEM (or the kernel is unwinding)
+  tc_fence_after();
 
   const int r = quarter * 32 + lane;  // query row in the tile == TMEM lane
   const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
   // Key chunks of 32 owned by this half: 0..3 (keys 0..127) or 4..6 (keys 128..223, of which
   // 128..207 exist in S and 128..200 are valid).
   const int c_begin = half ? 4 : 0, c_end = half ? 7 : 4;
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars[1], 0, abort_flag));
+  const bool ok = !*abort_flag;
   if (ok) {
-    tc_fence_after();
     float mx = -INFINITY;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
       uint32_t v[32];
+      tmem_load32(trow + c * 32, v);
       if (c < 6) {
-        tmem_load32(trow + c * 32, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
       } else {  // keys 192..223: only 192..200 are valid
-        tmem_load32(trow + c * 32, v);
 #pragma unroll
         for (int i = 0; i < kValidKeys - 192; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
       }
     }
     red_max[half * 128 + r] = mx;
-  } else if (lane == 0) {
-    report(status, kErrAttentionWait);
-    *abort_flag = 1;
   }
   __syncthreads();
   float sum = 0.f;
-  if (!*abort_flag) {
-    const float mxs = fmaxf(red_max[r], red_max[128 + r]) * 0.125f;
+  if (ok) {
+    // w = exp(0.125 s - 0.125 max) = 2^(s c - max c), c = 0.125 log2(e)
+    constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
+    const float mxc = fmaxf(red_max[r], red_max[128 + r]) * kScaleLog2;
 #pragma unroll 1
     for (int c = c_begin; c < c_end; ++c) {
       uint32_t v[32];
@@ -140,7 +146,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int key = c * 32 + i;
-        p[i] = key < kValidKeys ? __expf(__uint_as_float(v[i]) * 0.125f - mxs) : 0.f;
+        p[i] = key < kValidKeys ? ex2_approx(fmaf(__uint_as_float(v[i]), kScaleLog2, -mxc)) : 0.f;
         sum += p[i];
       }
       if (c < 6) {  // keys c*32 .. c*32+31 into 128-byte-swizzled block c/2 (over Q and K)
@@ -184,11 +190,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     }
     umma_f16(tmem, sw32_desc(smem_u32(smem + kPTail)), sw128_desc(vbase + 12 * 2048), idesc, 1);
     umma_commit(&bars[2]);
+    if (!mbar_wait(&bars[2], 0, abort_flag)) {
+      report(status, kErrAttentionWait);
+      *abort_flag = 1;
+    }
   }
+  tc_fence_before();
+  __syncthreads();  // O is in TMEM (or the kernel is unwinding)
+  tc_fence_after();
 
-  const bool o_ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait(&bars[2], 0, abort_flag));
-  if (o_ok) {
-    tc_fence_after();
+  if (!*abort_flag) {
     uint32_t o[32];
     tmem_load32(trow + half * 32, o);
     const int q_local = qt * 128 + r;
@@ -204,8 +215,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
                             pack_half2(__uint_as_float(o[8 * j + 4]) * inv, __uint_as_float(o[8 * j + 5]) * inv),
                             pack_half2(__uint_as_float(o[8 * j + 6]) * inv, __uint_as_float(o[8 * j + 7]) * inv));
     }
-  } else if (lane == 0) {
-    report(status, kErrAttentionWait);
   }
 
   tc_fence_before();

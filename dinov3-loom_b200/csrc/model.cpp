@@ -437,6 +437,11 @@ dv3_timings Model::benchmark(const float *pixels, size_t n_floats, size_t sample
   return out;
 }
 
+// Per-launch device time without host enqueue gaps: for each launch of the plan, a graph of
+// `iterations` back-to-back copies of that launch is captured and replayed between two events
+// on the model's stream (after one warm-up replay); the launch's time is the interval divided by
+// the copies. Consecutive copies overlap their start-up as the production graph does. The
+// residual GEMMs update x in place, so x holds garbage afterwards; the next forward rebuilds it.
 std::vector<std::pair<const char *, double>> Model::profile_launches(size_t batch,
                                                                      size_t iterations) {
   check_usable();
@@ -446,33 +451,43 @@ std::vector<std::pair<const char *, double>> Model::profile_launches(size_t batc
   activate();
   Plan &plan = prepare(batch);
   const size_t n = plan.launches.size();
-  std::vector<cudaEvent_t> ev(2 * n);
-  for (auto &e : ev) cuda(cudaEventCreate(&e), "create event");
-  std::vector<double> total(n, 0.0);
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  auto release_graph = [&] {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    exec = nullptr;
+    graph = nullptr;
+  };
+  std::vector<std::pair<const char *, double>> result;
   try {
-    for (size_t it = 0; it < iterations + 3; ++it) {
-      for (size_t j = 0; j < n; ++j) {
-        cuda(cudaEventRecord(ev[2 * j], stream_), "record event");
-        cuda(plan.launches[j].enqueue(stream_), plan.launches[j].name);
-        cuda(cudaEventRecord(ev[2 * j + 1], stream_), "record event");
-      }
-      cuda(cudaStreamSynchronize(stream_), "synchronize");
-      if (it >= 3)
-        for (size_t j = 0; j < n; ++j) {
-          float ms = 0;
-          cuda(cudaEventElapsedTime(&ms, ev[2 * j], ev[2 * j + 1]), "elapsed time");
-          total[j] += ms;
-        }
+    for (auto &e : ev) cuda(cudaEventCreate(&e), "create event");
+    for (size_t j = 0; j < n; ++j) {
+      cuda(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+      cudaError_t e = cudaSuccess;
+      for (size_t it = 0; it < iterations && e == cudaSuccess; ++it) e = plan.launches[j].enqueue(stream_);
+      cudaError_t e2 = cudaStreamEndCapture(stream_, &graph);
+      cuda(e != cudaSuccess ? e : e2, "capture profiling graph");
+      cuda(cudaGraphInstantiate(&exec, graph, 0), "instantiate profiling graph");
+      cuda(cudaGraphLaunch(exec, stream_), "launch profiling graph");  // warm-up
+      cuda(cudaEventRecord(ev[0], stream_), "record event");
+      cuda(cudaGraphLaunch(exec, stream_), "launch profiling graph");
+      cuda(cudaEventRecord(ev[1], stream_), "record event");
+      cuda(cudaEventSynchronize(ev[1]), "synchronize");
+      float ms = 0;
+      cuda(cudaEventElapsedTime(&ms, ev[0], ev[1]), "elapsed time");
+      result.emplace_back(plan.launches[j].name, ms / static_cast<double>(iterations));
+      release_graph();
     }
   } catch (...) {
-    for (auto &e : ev) cudaEventDestroy(e);
+    release_graph();
+    for (auto &e : ev)
+      if (e) cudaEventDestroy(e);
     throw;
   }
   for (auto &e : ev) cudaEventDestroy(e);
   check_status();
-  std::vector<std::pair<const char *, double>> result;
-  for (size_t j = 0; j < n; ++j)
-    result.emplace_back(plan.launches[j].name, total[j] / static_cast<double>(iterations));
   return result;
 }
 

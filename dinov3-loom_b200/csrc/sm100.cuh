@@ -292,6 +292,13 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// Hardware base-2 exponential approximation (one MUFU operation; subnormal results flush to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Hardware tanh approximation (one MUFU operation).
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;

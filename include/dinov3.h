@@ -131,10 +131,12 @@ int dv3_forward_device(dv3_model *m, const float *device_pixels, size_t n_floats
 /* Number of kernel launches in one forward of `batch` images (the graph's kernel nodes). */
 int dv3_launches_per_forward(dv3_model *m, size_t batch, size_t *out);
 
-/* Per-kernel device time of one forward of `batch` staged images: every launch of the plan is
- * issued directly and bracketed by CUDA events on the model's stream, `iterations` times after
- * 3 warm-up rounds. Writes up to `capacity` entries (launch order) of average milliseconds and
- * a static kernel name, and the count to *count. */
+/* Per-kernel device time of the launches of one forward of `batch` staged images: each launch
+ * of the plan is captured `iterations` times back to back into a CUDA graph, replayed once to
+ * warm up and once between two events on the model's stream; its time is the interval divided
+ * by `iterations`. Writes up to `capacity` entries (launch order) of average milliseconds and a
+ * static kernel name, and the count to *count. Leaves the model's activations undefined (the
+ * next forward recomputes them). */
 int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *ms,
                          const char **names, size_t capacity, size_t *count);
 
