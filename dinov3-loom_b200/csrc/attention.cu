@@ -1,75 +1,210 @@
-// attention.cu - per-(image, head, 128-query tile) attention on tcgen05 tensor cores.
-// Replaces kernels/attention_online_f16_wmma_cf16.loom (6 heads x 64, 201 tokens, scale 0.125).
+// attention.cu - multi-head attention of the forward on tcgen05 tensor cores: one persistent
+// CTA per SM walks (image, head) work items. Replaces kernels/attention_online_f16_wmma_cf16.loom
+// (6 heads x 64, 201 tokens, scale 0.125).
 //
-// All 201 keys of an image fit one tile, so the softmax is exact in one pass instead of online:
-//   1. TMA brings Q (128 rows) and K, V (256 rows: this image's 201 plus following rows, masked)
-//      of this head out of the fused QKV rows into 128-byte-swizzled shared memory.
-//   2. S = Q K^T: 4 tcgen05.mma (M=128, N=208, K=16) into TMEM columns 0..207, f32.
-//   3. 8 warps: the two warps of each TMEM lane quarter split a query row's keys (0..127 and
-//      128..207). Pass 1 takes the row max over the 201 valid keys (the halves meet in shared
-//      memory); pass 2 forms w = exp(0.125 s - 0.125 max) (one FFMA and the hardware exp2), sums
-//      w in f32 and writes P = f16(w)
-//      (keys >= 201 zero) into shared memory in the K-major layout the MMA reads: keys 0..191 as
-//      three 128-byte-swizzled 64-key blocks over the now dead Q and K tiles, keys 192..207 as a
-//      32-byte-swizzled 16-key block.
-//   4. O = P V: 13 tcgen05.mma (M=128, N=64, K=16 keys; V is the MN-major B operand) into TMEM
-//      columns 0..63 (S is consumed by then). Each thread divides its 32 of the 64 output columns
-//      by the row sum, rounds to f16 and stores them to out[token][64h..64h+63].
+// A work item covers the 201 queries of one head of one image as two 128-row tiles (tile 1 holds
+// tokens 128..200 and rows that are dropped) against all 201 keys. Every key fits one tile, so
+// the softmax is exact in one pass over S instead of online.
+//
+// Global memory is seen through per-image 3D tensor maps [image][201 tokens][columns]: token
+// rows past 201 read as zeros and are clipped on store, so no tile reaches into the next image.
+//
+// Roles (352 threads):
+//   warp 8     TMA producer. Per item: Q as two 128-token boxes, K and V as 208-token boxes of
+//              this head's columns of the fused QKV rows, 128-byte swizzle, into one of two
+//              shared-memory stages, so item i+1 loads while item i computes.
+//   warps 9/10 MMA issuers of tile 0 / tile 1 (lane 0); warp 9 also allocates TMEM (512
+//              columns). Tile t owns TMEM columns 256t..256t+255:
+//                S_t = Q_t K^T   M=128, N=208, K=64 (4 MMAs)         columns   0..207, f32
+//                P_t = f16 probabilities written by the softmax       columns   0..103 (2 keys
+//                      per column, over the consumed S)
+//                O_t = P_t V     A read from TMEM, V the MN-major B   columns 128..191, f32
+//                                operand in shared memory, K=208 (13 MMAs)
+//              Each issuer walks the items in order: S_t (needs the item's loads and tile t's
+//              TMEM released), then PV_t (needs P_t); a stage is released after both tiles' PVs
+//              of its item. An MMA holds its issuing thread about 80 cycles whatever its N (PV's
+//              13 MMAs of N=64 cost about 1000 cycles, S's 4 of N=208 about 430), so one issuer
+//              per tile keeps either tile from waiting behind the other's issue. Tile 1 starts
+//              when tile 0's first P is written: from then on one tile's softmax overlaps the
+//              other tile's MMAs and output instead of both competing for the exp2 unit.
+//   warps 0-3  softmax and output of tile 0, warps 4-7 of tile 1 (warp 7 idles: tile 1 rows
+//              96..127 are tokens 224..255). One query row per thread (TMEM lane 32*(w%4)+lane).
+//              Pass 1: row max over the 201 valid keys. Pass 2: w = exp(0.125 (s - max)) =
+//              2^(s c - max c) with c = 0.125 log2(e) (one FFMA and the hardware exp2), f32 sum of
+//              w, P = f16(w) (keys >= 201 zero) stored to TMEM. Once O is in TMEM: O / sum rounded
+//              to f16 into a per-warp 32-row staging tile (128-byte swizzle), written out by one
+//              TMA store per warp.
 // The probabilities are rounded to f16 before PV and the normaliser is the f32 sum of the
-// unrounded weights, as in the reference kernel (:214-216). Query rows past the image's 201 are
-// computed and dropped; rows past the batch read as zeros (TMA out-of-bounds fill).
-// Footprint: 256 TMEM columns and ~89 KB of shared memory, so two CTAs share an SM and one CTA's
-// loads and MMAs overlap the other's softmax.
+// unrounded weights, as in the reference kernel (:214-216).
+//
+// Every wait is bounded; on a timeout the kernel records kErrAttentionWait, raises the CTA's
+// abort flag, lets its own copies and MMAs in flight land, frees TMEM and returns.
 #include "kernels.h"
 #include "sm100.cuh"
 
 namespace dv3 {
 
 namespace {
-constexpr int kAttnThreads = 256;
-constexpr int kQ = 0;            // 128 x 64 f16 (16 KB); P keys 0..63 afterwards
-constexpr int kK = 16384;        // 256 x 64 f16 (32 KB); P keys 64..191 afterwards
-constexpr int kV = 49152;        // 256 x 64 f16 (32 KB)
-constexpr int kPTail = 81920;    // 128 x 16 f16, 32-byte swizzle (4 KB): P keys 192..207
-constexpr int kRed = 86016;      // [2 halves][128 rows] max, then [2][128] sum (2 KB)
-constexpr int kBar = 88064;      // 3 mbarriers, TMEM slot, abort flag
-constexpr int kAttnSmem = 1024 + kBar + 64;
+constexpr int kHeads = 6;
+constexpr int kAttnThreads = 352;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;  // TMEM allocator; issues tile 0's MMAs, warp 10 tile 1's
 constexpr int kValidKeys = kTokens;  // 201
 constexpr int kSKeys = 208;          // S columns computed (201 rounded up to 16)
-constexpr int kTmemCols = 256;
+constexpr int kKvBox = kSKeys;       // K, V token rows loaded per item
+constexpr int kOutBox = 32;          // token rows per output store (one warp's rows)
+constexpr int kQBytes = 128 * 128;   // 128 rows x 64 f16
+constexpr int kKvBytes = kKvBox * 128;
+// One stage: Q tile 0 | Q tile 1 | K | V, each 1024-byte aligned (8-row swizzle atoms).
+constexpr int kStageQ0 = 0;
+constexpr int kStageQ1 = kQBytes;
+constexpr int kStageK = 2 * kQBytes;
+constexpr int kStageV = kStageK + kKvBytes;
+constexpr int kStageBytes = kStageV + kKvBytes;
+constexpr uint32_t kLoadBytes = 2 * kQBytes + 2 * kKvBytes;
+constexpr int kStages = 2;
+constexpr int kStagingOff = kStages * kStageBytes;  // 8 warps x 32 rows x 128 B
+constexpr int kStagingBytes = kOutBox * 128;
+constexpr int kBarOff = kStagingOff + 8 * kStagingBytes;
+// 14 mbarriers: load_full[2], load_empty[2], s_full[2], p_full[2], o_full[2], tmem_empty[2],
+// drain[2]; then the TMEM slot and the abort flag.
+constexpr int kAttnSmem = 1024 + kBarOff + 128;
+constexpr int kTmemCols = 512;
+constexpr int kTileCols = 256;  // TMEM columns per query tile
+constexpr int kOCol = 128;      // O_t within the tile's columns
+static_assert(kStageV % 1024 == 0 && kStageBytes % 1024 == 0 && kStagingOff % 1024 == 0,
+              "swizzle atoms");
+static_assert(kAttnSmem <= 227 * 1024, "shared memory budget");
 
-// K-major 32-byte-swizzled tile descriptor: 32-byte rows (16 f16), 8-row groups 256 bytes apart,
-// layout type 6 (32-byte swizzle).
-__device__ __forceinline__ uint64_t sw32_desc(uint32_t smem_addr) {
-  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) |
-         (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46) | (6ull << 61);
+constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// w = 2^(s c - mc) for one pair of keys, summed into `sum`, returned as packed f16.
+__device__ __forceinline__ uint32_t exp_pair(uint32_t s0, uint32_t s1, float mc, float &sum,
+                                             bool v0 = true, bool v1 = true) {
+  const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s0), kScaleLog2, -mc)) : 0.f;
+  const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s1), kScaleLog2, -mc)) : 0.f;
+  sum += p0 + p1;
+  return pack_half2(p0, p1);
+}
+
+// Softmax of one query row whose S sits in TMEM columns tl..tl+207 (this thread's lane): stores
+// P over columns tl..tl+103 and returns the f32 sum of the weights. Both passes walk S in
+// 32-column chunks and load chunk c+1 while computing on chunk c. Each P store lands on S
+// columns that this thread has already read.
+__device__ __forceinline__ float softmax_row(uint32_t tl) {
+  uint32_t x[32], y[32];
+  float m0 = -INFINITY, m1 = -INFINITY;
+  auto max_chunk = [&](uint32_t (&v)[32], int n) {
+#pragma unroll
+    for (int i = 0; i + 1 < n; i += 4) {
+      m0 = max3(m0, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+      if (i + 3 < n) m1 = max3(m1, __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+      else if (i + 2 < n) m1 = fmaxf(m1, __uint_as_float(v[i + 2]));
+    }
+    if (n % 2) m0 = fmaxf(m0, __uint_as_float(v[n - 1]));
+  };
+  // Pass 1: chunks 0..5 (32 keys each) and keys 192..200 of chunk 6.
+  tmem_load32(tl, x);
+#pragma unroll
+  for (int c = 0; c < 6; c += 2) {
+    tmem_ld32(tl + (c + 1) * 32, y);
+    max_chunk(x, 32);
+    tmem_wait_ld(y);
+    tmem_ld32(tl + (c + 2) * 32, x);  // c + 2 == 6: columns 192..223 (only 192..200 are used)
+    max_chunk(y, 32);
+    tmem_wait_ld(x);
+  }
+  max_chunk(x, kValidKeys - 192);
+  const float mc = fmaxf(m0, m1) * kScaleLog2;
+
+  // Pass 2: keys 32c .. 32c+31 -> P columns 16c .. 16c+15.
+  float sum = 0.f;
+  auto exp_chunk = [&](uint32_t (&v)[32], int c) {
+    uint32_t p[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) p[j] = exp_pair(v[2 * j], v[2 * j + 1], mc, sum);
+    tmem_st16(tl + c * 16, p);
+  };
+  tmem_load32(tl, x);
+#pragma unroll
+  for (int c = 0; c < 6; c += 2) {
+    tmem_ld32(tl + (c + 1) * 32, y);
+    exp_chunk(x, c);
+    tmem_wait_ld(y);
+    if (c + 2 < 6) {
+      tmem_ld32(tl + (c + 2) * 32, x);
+      exp_chunk(y, c + 1);
+      tmem_wait_ld(x);
+    } else {
+      exp_chunk(y, c + 1);
+    }
+  }
+  uint32_t e[16];
+  tmem_ld16(tl + 192, e);  // keys 192..207 -> P columns 96..103
+  tmem_ld_wait();
+  tmem_regs_ready16(e);
+  uint32_t pe[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    pe[j] = exp_pair(e[2 * j], e[2 * j + 1], mc, sum, 192 + 2 * j < kValidKeys,
+                     192 + 2 * j + 1 < kValidKeys);
+  tmem_st8(tl + 96, pe);
+  return sum;
+}
+
+__device__ __forceinline__ uint32_t scaled_pair(uint32_t a, uint32_t b, float inv) {
+  return pack_half2(__uint_as_float(a) * inv, __uint_as_float(b) * inv);
 }
 }  // namespace
 
-__global__ void __launch_bounds__(kAttnThreads, 2)
-    attention_kernel(const __grid_constant__ CUtensorMap tm, int rows, __half *out,
-                     uint32_t *status) {
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tmq,
+                     const __grid_constant__ CUtensorMap tmkv,
+                     const __grid_constant__ CUtensorMap tmo, int n_items, uint32_t *status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t *smem = smem_raw + pad;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBar);  // 0 loads, 1 S ready, 2 O ready
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3);
+  uint64_t *load_full = reinterpret_cast<uint64_t *>(smem + kBarOff);
+  uint64_t *load_empty = load_full + 2;
+  uint64_t *s_full = load_full + 4;
+  uint64_t *p_full = load_full + 6;
+  uint64_t *o_full = load_full + 8;
+  uint64_t *tmem_empty = load_full + 10;
+  uint64_t *drain = load_full + 12;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(load_full + 14);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  float *red_max = reinterpret_cast<float *>(smem + kRed);
-  float *red_sum = red_max + 256;
-
-  const int qt = blockIdx.x, head = blockIdx.y, img = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int quarter = warp & 3, half = warp >> 2;
-  const int tok0 = img * kTokens;
+  // Items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int count = static_cast<int>(blockIdx.x) < n_items
+                        ? (n_items - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                        : 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&load_full[i], 1);
+      mbar_init(&load_empty[i], 2);  // one commit per tile's issuer
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&tmem_empty[i], 128);
+    }
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_map(&tm);
   }
-  if (warp == 0) {
+  if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_map(&tmq);
+    tma_prefetch_map(&tmkv);
+    tma_prefetch_map(&tmo);
+  }
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -80,153 +215,149 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   pdl_wait();  // the QKV rows of the previous kernel are complete from here on
   pdl_trigger();
 
-  // Thread 0 drives the pipeline and alone polls the mbarriers (bounded waits); the other warps
-  // sleep in __syncthreads, leaving issue slots to the co-resident CTA.
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&bars[0], 5 * 16384);
-    const int qx = head * 64, kx = kHidden + head * 64, vx = 2 * kHidden + head * 64;
-    tma_load_2d(smem + kQ, &tm, &bars[0], qx, tok0 + qt * 128);
-    tma_load_2d(smem + kK, &tm, &bars[0], kx, tok0);
-    tma_load_2d(smem + kK + 16384, &tm, &bars[0], kx, tok0 + 128);
-    tma_load_2d(smem + kV, &tm, &bars[0], vx, tok0);
-    tma_load_2d(smem + kV + 16384, &tm, &bars[0], vx, tok0 + 128);
-    bool ok = mbar_wait(&bars[0], 0, abort_flag);
-    if (ok) {
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      uint32_t armed = 0, last_parity = 0;  // per stage: armed at least once, parity of the last
+      for (int k = 0; k < count; ++k) {
+        const int s = k & 1;
+        const uint32_t ph = (k >> 1) & 1;
+        if (!mbar_wait(&load_empty[s], ph ^ 1u, abort_flag)) {
+          report(status, kErrAttentionWait);
+          *abort_flag = 1;
+          break;
+        }
+        const int item = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+        const int img = item / kHeads, head = item % kHeads;
+        uint8_t *st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&load_full[s], kLoadBytes);
+        tma_load_3d(st + kStageQ0, &tmq, &load_full[s], head * 64, 0, img);
+        tma_load_3d(st + kStageQ1, &tmq, &load_full[s], head * 64, 128, img);
+        tma_load_3d(st + kStageK, &tmkv, &load_full[s], kHidden + head * 64, 0, img);
+        tma_load_3d(st + kStageV, &tmkv, &load_full[s], 2 * kHidden + head * 64, 0, img);
+        armed |= 1u << s;
+        last_parity = (last_parity & ~(1u << s)) | (ph << s);
+      }
+      // Copies still in flight (only after an abort) land before shared memory is released.
+      for (int s = 0; s < kStages; ++s)
+        if ((armed >> s) & 1u) mbar_drain(&load_full[s], (last_parity >> s) & 1u);
+    }
+  } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+    // One issuer thread per tile, so neither tile's MMAs wait behind the other's issue.
+    if (lane == 0) {
+      const int t = warp - kMmaWarp;
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, kSKeys, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(128, 64, true);
+      const uint32_t d_s = tmem + t * kTileCols, d_o = d_s + kOCol;
+      bool ok = true;
+      for (int k = 0; ok && k < count; ++k) {
+        const uint32_t par = k & 1;
+        const uint8_t *st = smem + (k & 1) * kStageBytes;
+        // Tile 1 starts once tile 0's first P is written: from then on one tile's softmax
+        // overlaps the other tile's MMAs and output instead of both competing for the exp2 unit.
+        ok = mbar_wait(&load_full[k & 1], (k >> 1) & 1, abort_flag) &&
+             mbar_wait(&tmem_empty[t], par ^ 1u, abort_flag) &&
+             (t == 0 || k > 0 || mbar_wait(&p_full[0], 0, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t qd = sw128_desc(smem_u32(st + (t ? kStageQ1 : kStageQ0)));
+        const uint64_t kd = sw128_desc(smem_u32(st + kStageK));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_f16(d_s, qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0);
+        umma_commit(&s_full[t]);
+        ok = mbar_wait(&p_full[t], par, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t vb = smem_u32(st + kStageV);
+#pragma unroll
+        for (int kk = 0; kk < kSKeys / 16; ++kk)
+          umma_f16_ts(d_o, d_s + 8 * kk, sw128_desc(vb + kk * 2048), idesc_o, kk > 0);
+        umma_commit(&o_full[t]);
+        umma_commit(&load_empty[k & 1]);  // this tile is done with the item's stage
+      }
+      if (!ok) {
+        report(status, kErrAttentionWait);
+        *abort_flag = 1;
+      }
+      umma_commit(&drain[t]);  // every MMA this thread issued has completed before TMEM is freed
+      mbar_drain(&drain[t], 0);
+    }
+  } else {
+    const int t = warp >> 2, q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + t * kTileCols;
+    const bool active = !(t == 1 && q == 3);  // warp-uniform
+    uint8_t *stg = smem + kStagingOff + warp * kStagingBytes;
+    uint8_t *stg_row = stg + r % 32 * 128;
+    for (int k = 0; k < count; ++k) {
+      const uint32_t par = k & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], par, abort_flag))) {
+        if (lane == 0) {
+          report(status, kErrAttentionWait);
+          *abort_flag = 1;
+        }
+        break;
+      }
       tc_fence_after();
-      const uint64_t qd = sw128_desc(smem_u32(smem + kQ));
-      const uint64_t kd = sw128_desc(smem_u32(smem + kK));
-      constexpr uint32_t idesc = idesc_f16_f32(128, kSKeys, false);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) umma_f16(tmem, qd + 2 * k, kd + 2 * k, idesc, k > 0);
-      umma_commit(&bars[1]);
-      ok = mbar_wait(&bars[1], 0, abort_flag);
-    }
-    if (!ok) {
-      report(status, kErrAttentionWait);
-      *abort_flag = 1;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();  // S is in TMEM (or the kernel is unwinding)
-  tc_fence_after();
-
-  const int r = quarter * 32 + lane;  // query row in the tile == TMEM lane
-  const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-  // Key chunks of 32 owned by this half: 0..3 (keys 0..127) or 4..6 (keys 128..223, of which
-  // 128..207 exist in S and 128..200 are valid).
-  const int c_begin = half ? 4 : 0, c_end = half ? 7 : 4;
-  const bool ok = !*abort_flag;
-  if (ok) {
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; ++c) {
-      uint32_t v[32];
-      tmem_load32(trow + c * 32, v);
-      if (c < 6) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
-      } else {  // keys 192..223: only 192..200 are valid
-#pragma unroll
-        for (int i = 0; i < kValidKeys - 192; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+      float sum = 1.f;
+      if (active) sum = softmax_row(tl);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[t], par, abort_flag))) {
+        if (lane == 0) {
+          report(status, kErrAttentionWait);
+          *abort_flag = 1;
+        }
+        break;
       }
-    }
-    red_max[half * 128 + r] = mx;
-  }
-  __syncthreads();
-  float sum = 0.f;
-  if (ok) {
-    // w = exp(0.125 s - 0.125 max) = 2^(s c - max c), c = 0.125 log2(e)
-    constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
-    const float mxc = fmaxf(red_max[r], red_max[128 + r]) * kScaleLog2;
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; ++c) {
-      uint32_t v[32];
-      tmem_load32(trow + c * 32, v);
-      float p[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int key = c * 32 + i;
-        p[i] = key < kValidKeys ? ex2_approx(fmaf(__uint_as_float(v[i]), kScaleLog2, -mxc)) : 0.f;
-        sum += p[i];
-      }
-      if (c < 6) {  // keys c*32 .. c*32+31 into 128-byte-swizzled block c/2 (over Q and K)
-        uint8_t *blk = smem + (c / 2) * 16384 + (r / 8) * 1024 + (r % 8) * 128;
-        const int chunk0 = (c % 2) * 4;
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      if (active) tmem_load32x2(tl + kOCol, o0, tl + kOCol + 32, o1);
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[t]);
+      if (active) {
+        const float inv = 1.0f / sum;
+        if (lane == 0) bulk_wait_read<0>();  // the previous store has read the staging tile
+        __syncwarp();
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint4 val = make_uint4(pack_half2(p[8 * j + 0], p[8 * j + 1]),
-                                       pack_half2(p[8 * j + 2], p[8 * j + 3]),
-                                       pack_half2(p[8 * j + 4], p[8 * j + 5]),
-                                       pack_half2(p[8 * j + 6], p[8 * j + 7]));
-          *reinterpret_cast<uint4 *>(blk + (((chunk0 + j) ^ (r % 8)) * 16)) = val;
+          *reinterpret_cast<uint4 *>(stg_row + ((j ^ (lane & 7)) * 16)) =
+              make_uint4(scaled_pair(o0[8 * j], o0[8 * j + 1], inv),
+                         scaled_pair(o0[8 * j + 2], o0[8 * j + 3], inv),
+                         scaled_pair(o0[8 * j + 4], o0[8 * j + 5], inv),
+                         scaled_pair(o0[8 * j + 6], o0[8 * j + 7], inv));
+          *reinterpret_cast<uint4 *>(stg_row + (((4 + j) ^ (lane & 7)) * 16)) =
+              make_uint4(scaled_pair(o1[8 * j], o1[8 * j + 1], inv),
+                         scaled_pair(o1[8 * j + 2], o1[8 * j + 3], inv),
+                         scaled_pair(o1[8 * j + 4], o1[8 * j + 5], inv),
+                         scaled_pair(o1[8 * j + 6], o1[8 * j + 7], inv));
         }
-      } else {  // keys 192..207 into the 32-byte-swizzled tail block
-        uint8_t *rowp = smem + kPTail + (r / 8) * 256 + (r % 8) * 32;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const uint4 val = make_uint4(pack_half2(p[8 * j + 0], p[8 * j + 1]),
-                                       pack_half2(p[8 * j + 2], p[8 * j + 3]),
-                                       pack_half2(p[8 * j + 4], p[8 * j + 5]),
-                                       pack_half2(p[8 * j + 6], p[8 * j + 7]));
-          *reinterpret_cast<uint4 *>(rowp + ((j ^ ((r % 8) >> 2)) * 16)) = val;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int item = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+          tma_store_3d(&tmo, stg, (item % kHeads) * 64, t * 128 + q * 32, item / kHeads);
+          bulk_commit();
         }
       }
     }
-    red_sum[half * 128 + r] = sum;
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-
-  if (threadIdx.x == 0 && !*abort_flag) {
-    tc_fence_after();
-    const uint32_t pbase = smem_u32(smem);
-    const uint32_t vbase = smem_u32(smem + kV);
-    constexpr uint32_t idesc = idesc_f16_f32(128, 64, true);
-#pragma unroll
-    for (int kk = 0; kk < 12; ++kk) {
-      const uint64_t pd = sw128_desc(pbase + (kk / 4) * 16384 + (kk % 4) * 32);
-      umma_f16(tmem, pd, sw128_desc(vbase + kk * 2048), idesc, kk > 0);
-    }
-    umma_f16(tmem, sw32_desc(smem_u32(smem + kPTail)), sw128_desc(vbase + 12 * 2048), idesc, 1);
-    umma_commit(&bars[2]);
-    if (!mbar_wait(&bars[2], 0, abort_flag)) {
-      report(status, kErrAttentionWait);
-      *abort_flag = 1;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();  // O is in TMEM (or the kernel is unwinding)
-  tc_fence_after();
-
-  if (!*abort_flag) {
-    uint32_t o[32];
-    tmem_load32(trow + half * 32, o);
-    const int q_local = qt * 128 + r;
-    const int token = tok0 + q_local;
-    if (q_local < kValidKeys && token < rows) {
-      const float inv = 1.0f / (red_sum[r] + red_sum[128 + r]);
-      uint4 *dst =
-          reinterpret_cast<uint4 *>(out + static_cast<size_t>(token) * kHidden + head * 64 + half * 32);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        dst[j] = make_uint4(pack_half2(__uint_as_float(o[8 * j + 0]) * inv, __uint_as_float(o[8 * j + 1]) * inv),
-                            pack_half2(__uint_as_float(o[8 * j + 2]) * inv, __uint_as_float(o[8 * j + 3]) * inv),
-                            pack_half2(__uint_as_float(o[8 * j + 4]) * inv, __uint_as_float(o[8 * j + 5]) * inv),
-                            pack_half2(__uint_as_float(o[8 * j + 6]) * inv, __uint_as_float(o[8 * j + 7]) * inv));
-    }
+    if (lane == 0) bulk_wait<0>();  // output stores complete before the CTA retires
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
 }
 
-bool make_attention_map(const void *qkv, uint32_t rows, CUtensorMap *map, std::string *err) {
-  return encode_map_f16(map, qkv, kQkv, rows, 64, 128, err);
+bool make_attention_map(const void *qkv, const void *out, uint32_t rows, AttentionMaps *maps,
+                        std::string *err) {
+  const uint32_t n_images = rows / kTokens;
+  return encode_map_f16_images(&maps->q, qkv, kQkv, n_images, 128, err) &&
+         encode_map_f16_images(&maps->kv, qkv, kQkv, n_images, kKvBox, err) &&
+         encode_map_f16_images(&maps->out, out, kHidden, n_images, kOutBox, err);
 }
 
 cudaError_t configure_attention_kernel() {
@@ -234,7 +365,7 @@ cudaError_t configure_attention_kernel() {
                               kAttnSmem);
 }
 
-cudaError_t launch_attention(const CUtensorMap &map, uint32_t rows, __half *out, uint32_t *status,
+cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
                              cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
   static bool configured[64] = {};
@@ -245,9 +376,10 @@ cudaError_t launch_attention(const CUtensorMap &map, uint32_t rows, __half *out,
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const dim3 grid(2, 6, rows / kTokens);
-  return launch_pdl(attention_kernel, grid, dim3(kAttnThreads), kAttnSmem, stream, map,
-                    static_cast<int>(rows), out, status);
+  const int n_items = static_cast<int>(rows / kTokens) * kHeads;
+  const int grid = n_items < sm_count(dev) ? n_items : sm_count(dev);
+  return launch_pdl(attention_kernel, dim3(grid), dim3(kAttnThreads), kAttnSmem, stream, maps.q,
+                    maps.kv, maps.out, n_items, status);
 }
 
 }  // namespace dv3

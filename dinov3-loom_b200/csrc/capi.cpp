@@ -253,11 +253,10 @@ int dv3k_attention(const uint16_t *qkv, uint32_t rows, uint16_t *out, uint32_t *
   if (rows == 0) return DV3_OK;
   if (!all_aligned(qkv, out)) return bad_args("pointers must be 16-byte aligned");
   if (rows % dv3::kTokens != 0) return bad_args("rows must be a multiple of 201");
-  CUtensorMap map;
+  dv3::AttentionMaps map;
   std::string err;
-  if (!dv3::make_attention_map(qkv, rows, &map, &err)) return bad_args(err.c_str());
-  return launch_status(dv3::launch_attention(map, rows, reinterpret_cast<__half *>(out), status,
-                                             static_cast<cudaStream_t>(stream)),
+  if (!dv3::make_attention_map(qkv, out, rows, &map, &err)) return bad_args(err.c_str());
+  return launch_status(dv3::launch_attention(map, rows, status, static_cast<cudaStream_t>(stream)),
                        "attention");
 }
 

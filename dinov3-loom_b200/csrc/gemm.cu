@@ -38,6 +38,16 @@ constexpr int kGemmThreads = 64 + kEpilogueThreads;  // 320
 // weight tile arrives as two TMA boxes of BN/2 rows, and one accumulator fills TMEM.
 // Shared memory: [stages x (A 16 KB | B BN*128 B)] [TMA-store staging: 8 warps x 2 x 2 KB]
 // [mbarriers, TMEM slot, abort flag] [epilogue vectors]. As many stages as fit (at most 6).
+// Whether an epilogue loads input blocks by TMA (EpiResid): Epi::kTmaInput when it exists.
+template <class Epi, class = void>
+struct TmaInput {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct TmaInput<Epi, decltype(void(Epi::kTmaInput))> {
+  static constexpr bool value = Epi::kTmaInput;
+};
+
 template <int BN, class Epi>
 struct GemmCfg {
   static constexpr int kSplit = BN > 256 ? 2 : 1;    // MMAs (and B boxes) per K step
@@ -47,7 +57,8 @@ struct GemmCfg {
   static constexpr int kB = BN * BK * 2;
   static constexpr int kStage = kA + kB;
   static constexpr int kStaging = Epi::kTmaStore ? kEpilogueWarps * 2 * kStageBlockBytes : 0;
-  static constexpr int kBarBytes = 256;
+  static constexpr bool kInput = TmaInput<Epi>::value;
+  static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
   static constexpr int kFixed = 1024 + kStaging + kBarBytes + ((Epi::kSmem + 127) / 128) * 128;
   static constexpr int kFit = (227 * 1024 - kFixed) / kStage;
   static constexpr int kStages = kFit < 6 ? kFit : 6;
@@ -58,7 +69,9 @@ struct GemmCfg {
   static constexpr int kTmemCols = kAccBufs * BN <= 256 ? 256 : 512;
   static constexpr int kSmemBytes = 1024 + kExtraOffset + Epi::kSmem;
   static_assert(kMmaN % 16 == 0 && kMmaN <= 256, "tcgen05.mma N for M=128");
-  static_assert((2 * kStages + 2 * kAccBufs) * 8 + 8 <= kBarBytes, "barrier region");
+  static_assert((2 * kStages + 2 * kAccBufs + (kInput ? 2 * kEpilogueWarps : 0)) * 8 + 8 <=
+                    kBarBytes,
+                "barrier region");
   static_assert(kStages >= 2 && kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -84,7 +97,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *empty = full + C::kStages;
   uint64_t *tfull = empty + C::kStages;
   uint64_t *tempty = tfull + C::kAccBufs;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + C::kAccBufs);
+  uint64_t *in_bars = tempty + C::kAccBufs;  // 2 per epilogue warp (kInput only)
+  uint32_t *tmem_slot =
+      reinterpret_cast<uint32_t *>(in_bars + (C::kInput ? 2 * kEpilogueWarps : 0));
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   uint8_t *extra = smem + C::kExtraOffset;
 
@@ -100,6 +115,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 32 * kEpilogueWarps);
     }
+    if (C::kInput)
+      for (int i = 0; i < 2 * kEpilogueWarps; ++i) mbar_init(&in_bars[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_map(&tmA);
@@ -211,14 +228,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ctx.staging = smem + C::kStagingOffset + (warp - 2) * 2 * kStageBlockBytes;
     ctx.buf = 0;
     ctx.out_map = &tmC;
+    ctx.in_bar = in_bars + 2 * (warp - 2);
+    ctx.iter = 0;
+    ctx.abort_flag = abort_flag;
+    ctx.failed = false;
     int acc = 0;
     uint32_t acc_phase = 0;
+    bool in_pending = false;  // input blocks requested for a tile not yet processed
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = (tile / n_tiles_n) * BM;
       const int n0 = (tile % n_tiles_n) * BN + half * kCols;
       ctx.row = m0 + row_in_tile;
       ctx.row0 = m0 + q * 32;
       typename Epi::Pre pre = epi.prefetch(n0, ctx);
+      in_pending = C::kInput;
       const bool waited = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) {
@@ -230,6 +253,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       epi.template run<kCols>(
           tmem_base + lane_base + static_cast<uint32_t>(acc * BN + half * kCols), n0, ctx, pre);
+      if (ctx.failed) {
+        if (lane == 0) {
+          report(status, kErrEpilogueWait);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      in_pending = false;
+      ++ctx.iter;
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == C::kAccBufs) {
@@ -238,6 +270,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     if (Epi::kTmaStore && lane == 0) bulk_wait<0>();  // stores done before the CTA retires
+    // Input blocks requested for a tile that was never processed (after an abort) land before
+    // shared memory is released.
+    if (C::kInput && lane == 0 && in_pending)
+      for (int j = 0; j < 2; ++j) mbar_drain(&ctx.in_bar[j], ctx.iter & 1u);
   }
 
   tc_fence_before();
@@ -352,7 +388,7 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
                              EpiQkvRope{args.bias, args.rope_cos, args.rope_sin}, status, stream);
     case GemmOp::Resid384:
     case GemmOp::Resid1536:
-      return launch_one<128>(maps, rows, s.n, s.k, EpiResid{args.bias, args.lambda, args.out},
+      return launch_one<128>(maps, rows, s.n, s.k, EpiResid{args.bias, args.lambda},
                              status, stream);
     case GemmOp::SwiGLU:
       return launch_one<256>(maps, rows, s.n, s.k, EpiSwiGLU{args.bias}, status, stream);

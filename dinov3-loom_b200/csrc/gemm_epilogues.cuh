@@ -10,6 +10,8 @@
 //   struct Pre; Pre prefetch(int n0, const EpiCtx &ctx)
 //       called before the wait for the tile's accumulator: loads that do not depend on the
 //       MMAs (the residual row) start here and overlap the wait
+//   static constexpr bool kTmaInput;   (optional) prefetch() loads the tile's input blocks by TMA
+//       into the warp's staging blocks, one mbarrier per block (ctx.in_bar)
 //   template <int COLS> void run(uint32_t taddr, int n0, EpiCtx &ctx, Pre &pre)
 //       processes COLS accumulator columns starting at TMEM address `taddr` (this warp's lane
 //       quarter) that belong to output columns n0..n0+COLS-1 of output row ctx.row. ctx.row may
@@ -45,6 +47,10 @@ struct EpiCtx {
   uint8_t *staging;    // this warp's two staging blocks
   int buf;             // staging block to use next
   const CUtensorMap *out_map;
+  uint64_t *in_bar;    // kTmaInput epilogues: this warp's two input-block mbarriers
+  uint32_t iter;       // tiles this warp has processed (input-block barrier parity)
+  volatile int *abort_flag;
+  bool failed;         // a bounded wait expired inside run()
 };
 
 struct NoPre {};
@@ -222,22 +228,29 @@ struct EpiQkvRope {
 
 // ---------------------------------------------------------------------------------------------
 // Residual update with LayerScale: x[row][n] = f16(x + lambda[n] (acc + b[n])), in place. The
-// residual row is read one 32-column chunk ahead of its use; the result leaves by TMA store.
+// warp's residual block (its 32 rows x 64 columns) arrives by TMA in the warp's two staging
+// blocks, requested before the accumulator wait (prefetch). Each thread then rewrites its row of
+// a block in shared memory and the block leaves by TMA store, so x is read and written in whole
+// lines instead of one 16-byte piece per row and warp instruction.
 // ---------------------------------------------------------------------------------------------
 struct EpiResid {
   const float *bias;
   const float *lambda;
-  const __half *x;
   static constexpr int kSmem = 2 * kHidden * 4;
   static constexpr bool kTmaStore = true;
-  struct Pre {
-    uint4 q[4];
-  };
-  // The first 32 columns of the residual row, before the accumulator wait.
+  static constexpr bool kTmaInput = true;
+  using Pre = NoPre;
   __device__ Pre prefetch(int n0, const EpiCtx &c) const {
-    Pre p{};
-    if (c.row < c.M) ldg_half32(x + static_cast<size_t>(c.row) * kHidden + n0, p.q);
-    return p;
+    if (c.lane == 0) {
+      bulk_wait_read<0>();  // the previous tile's stores have read both blocks
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        mbar_arrive_expect_tx(&c.in_bar[j], kStageBlockBytes);
+        tma_load_2d(c.staging + j * kStageBlockBytes, c.out_map, &c.in_bar[j], n0 + 32 * j,
+                    c.row0);
+      }
+    }
+    return {};
   }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     float *s = reinterpret_cast<float *>(smem);
@@ -245,28 +258,39 @@ struct EpiResid {
     stage_floats(s + kHidden, lambda, kHidden, tid, n);
   }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
+    static_assert(COLS == 64, "one 32-column block per staging buffer");
     const float *sb = reinterpret_cast<const float *>(c.smem);
     const float *sl = sb + kHidden;
-    const bool ok = c.row < c.M;
-    const __half *xr = x + static_cast<size_t>(c.row) * kHidden + n0;
-    uint4 cur[4], nxt[4] = {};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) cur[j] = pre.q[j];
+    const int sw = (c.lane >> 1) & 3;
 #pragma unroll 1
-    for (int k = 0; k < COLS; k += 32) {
-      if (ok && k + 32 < COLS) ldg_half32(xr + k + 32, nxt);
+    for (int j = 0; j < 2; ++j) {
       uint32_t r[32];
-      tmem_load32(taddr + k, r);
+      tmem_ld32(taddr + 32 * j, r);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&c.in_bar[j], c.iter & 1u, c.abort_flag));
+      tmem_wait_ld(r);
+      if (!ok) {
+        c.failed = true;
+        return;
+      }
+      uint8_t *rowp = c.staging + j * kStageBlockBytes + c.lane * 64;
+      uint4 q[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q[k] = *reinterpret_cast<const uint4 *>(rowp + ((k ^ sw) << 4));
       float v[32], b[32], l[32];
-      unpack_half32(cur, v);
-      lds32(sb + n0 + k, b);
-      lds32(sl + n0 + k, l);
+      unpack_half32(q, v);
+      lds32(sb + n0 + 32 * j, b);
+      lds32(sl + n0 + 32 * j, l);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] += l[i] * (u2f(r[i]) + b[i]);
-      tma_emit32(c, v, n0 + k);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+      for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) = pack8(v, k);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (c.lane == 0) {
+        tma_store_2d(c.out_map, c.staging + j * kStageBlockBytes, n0 + 32 * j, c.row0);
+        bulk_commit();
+      }
     }
   }
 };

@@ -31,6 +31,12 @@ bool encode_map_f16_swizzled(CUtensorMap *map, const void *base, uint64_t cols, 
                              uint32_t box_cols, uint32_t box_rows, uint32_t swizzle_bytes,
                              std::string *err);
 
+// 3D f16 view [n_images][201 tokens][cols] of token rows, box = 64 columns x box_rows tokens x 1
+// image, 128-byte swizzle. Tokens past 201 fall outside the image: loads read zeros, stores
+// are clipped.
+bool encode_map_f16_images(CUtensorMap *map, const void *base, uint64_t cols, uint64_t n_images,
+                           uint32_t box_rows, std::string *err);
+
 // ---- GEMM operations (gemm.cu) ----
 // Resid*: x += lambda (A W^T + b) on 128-column tiles. ResidLN*: the same on full 384-column
 // rows, followed in the same kernel by the LayerNorm of the updated row into ln_out (f16) or
@@ -71,8 +77,16 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
 const char *gemm_name(GemmOp op);
 
 // ---- attention (attention.cu) ----
-bool make_attention_map(const void *qkv, uint32_t rows, CUtensorMap *map, std::string *err);
-cudaError_t launch_attention(const CUtensorMap &map, uint32_t rows, __half *out, uint32_t *status,
+// Per-image tensor maps: q (128-token boxes) and kv (208-token boxes) over the fused QKV rows,
+// out (32-token boxes) over the attention output.
+struct AttentionMaps {
+  CUtensorMap q;
+  CUtensorMap kv;
+  CUtensorMap out;
+};
+bool make_attention_map(const void *qkv, const void *out, uint32_t rows, AttentionMaps *maps,
+                        std::string *err);
+cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
                              cudaStream_t stream);
 
 // ---- bandwidth kernels (elementwise.cu) ----

@@ -206,8 +206,8 @@ Plan &Model::prepare(size_t b) {
 
   GemmMaps patch_maps;
   need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, x, &patch_maps, &err));
-  CUtensorMap attn_map;
-  need(make_attention_map(qkv, r, &attn_map, &err));
+  AttentionMaps attn_map;
+  need(make_attention_map(qkv, attn, r, &attn_map, &err));
 
   add("patchify", [=](cudaStream_t s) {
     return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s);
@@ -239,7 +239,7 @@ Plan &Model::prepare(size_t b) {
       g.out = qkv;
       return launch_gemm(GemmOp::QkvRope, qkv_maps, r, g, st, s);
     });
-    add("attention", [=](cudaStream_t s) { return launch_attention(attn_map, r, attn, st, s); });
+    add("attention", [=](cudaStream_t s) { return launch_attention(attn_map, r, st, s); });
     // o-proj + LayerScale 1 + residual, and LN2 of this layer (fused or separate): x -> x, h
     add(gemm_name(o_op), [=](cudaStream_t s) {
       GemmArgs g;

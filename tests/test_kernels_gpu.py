@@ -185,7 +185,8 @@ def attention_ref(qkv, b):
     return out
 
 
-@pytest.mark.parametrize("b", [1, 3, 8])
+# 50 and 64 images give 300 and 384 (image, head) items: each persistent CTA walks 2 or 3 of them.
+@pytest.mark.parametrize("b", [1, 3, 8, 50, 64])
 def test_attention(b):
     rng = np.random.default_rng(40 + b)
     r = rows_of(b)
