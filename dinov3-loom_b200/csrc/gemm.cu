@@ -48,6 +48,18 @@ struct TmaInput<Epi, decltype(void(Epi::kTmaInput))> {
   static constexpr bool value = Epi::kTmaInput;
 };
 
+// Whether an epilogue stages through the mainloop's tile buffers instead of a region of its own
+// (EpiResidWide): Epi::kStagingInTiles when it exists. Such an epilogue runs only when every CTA
+// has at most one tile, so the buffers are idle once the tile's accumulator is complete.
+template <class Epi, class = void>
+struct StagingInTiles {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct StagingInTiles<Epi, decltype(void(Epi::kStagingInTiles))> {
+  static constexpr bool value = Epi::kStagingInTiles;
+};
+
 template <int BN, class Epi>
 struct GemmCfg {
   static constexpr int kSplit = BN > 256 ? 2 : 1;    // MMAs (and B boxes) per K step
@@ -56,7 +68,8 @@ struct GemmCfg {
   static constexpr int kA = BM * BK * 2;  // 16 KB
   static constexpr int kB = BN * BK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kStaging = Epi::kTmaStore ? kEpilogueWarps * 2 * kStageBlockBytes : 0;
+  static constexpr bool kInTiles = StagingInTiles<Epi>::value;
+  static constexpr int kStaging = Epi::kTmaStore && !kInTiles ? kEpilogueWarps * 2 * kStageBlockBytes : 0;
   static constexpr bool kInput = TmaInput<Epi>::value;
   static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
   static constexpr int kFixed = 1024 + kStaging + kBarBytes + ((Epi::kSmem + 127) / 128) * 128;
@@ -135,6 +148,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = ((M + BM - 1) / BM) * n_tiles_n;
+  if (C::kInTiles && num_tiles > static_cast<int>(gridDim.x)) {  // the host never launches this
+    if (threadIdx.x == 0) report(status, kErrEpilogueWait);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+    return;
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -225,7 +248,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ctx.r = row_in_tile;
     ctx.lane = lane;
     ctx.smem = extra;
-    ctx.staging = smem + C::kStagingOffset + (warp - 2) * 2 * kStageBlockBytes;
+    if constexpr (C::kInTiles) {
+      static_assert(kEpilogueWarps * Epi::kWarpStaging <= C::kTiles, "staging in tile buffers");
+      ctx.staging = tiles + (warp - 2) * Epi::kWarpStaging;
+    } else
+      ctx.staging = smem + C::kStagingOffset + (warp - 2) * 2 * kStageBlockBytes;
     ctx.buf = 0;
     ctx.out_map = &tmC;
     ctx.in_bar = in_bars + 2 * (warp - 2);
@@ -241,7 +268,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ctx.row = m0 + row_in_tile;
       ctx.row0 = m0 + q * 32;
       typename Epi::Pre pre = epi.prefetch(n0, ctx);
-      in_pending = C::kInput;
+      in_pending = C::kInput && !C::kInTiles;  // kInTiles epilogues load inside run()
       const bool waited = mbar_wait(&tfull[acc], acc_phase, abort_flag);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) {
@@ -251,6 +278,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
+      if (C::kInTiles) in_pending = true;
       epi.template run<kCols>(
           tmem_base + lane_base + static_cast<uint32_t>(acc * BN + half * kCols), n0, ctx, pre);
       if (ctx.failed) {
@@ -282,6 +310,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
   }
+}
+
+// The residual GEMMs run on full 384-wide rows (one tile per CTA, A read once) while all M tiles
+// fit in one wave of CTAs, else on 128-wide tiles.
+static bool resid_wide(uint32_t rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return (rows + BM - 1) / BM <= static_cast<uint32_t>(sm_count(dev));
+}
+
+GemmShape gemm_shape(GemmOp op, uint32_t rows) {
+  if ((op == GemmOp::Resid384 || op == GemmOp::Resid1536) && resid_wide(rows)) {
+    GemmShape s = gemm_shape(op);
+    s.bn = 384;
+    return s;
+  }
+  return gemm_shape(op);
 }
 
 GemmShape gemm_shape(GemmOp op) {
@@ -323,7 +368,7 @@ static uint32_t tma_store_cols(GemmOp op) {
 
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
                     GemmMaps *maps, std::string *err) {
-  const GemmShape s = gemm_shape(op);
+  const GemmShape s = gemm_shape(op, rows);
   const uint32_t b_rows = s.bn > 256 ? s.bn / 2 : s.bn;  // one TMA box per MMA of the K step
   if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err) ||
       !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))
@@ -368,6 +413,7 @@ cudaError_t configure_gemm_kernels() {
   if ((e = configure_one<128, EpiPatch>()) != cudaSuccess) return e;
   if ((e = configure_one<256, EpiQkvRope>()) != cudaSuccess) return e;
   if ((e = configure_one<128, EpiResid>()) != cudaSuccess) return e;
+  if ((e = configure_one<384, EpiResidWide>()) != cudaSuccess) return e;
   if ((e = configure_one<256, EpiSwiGLU>()) != cudaSuccess) return e;
   if ((e = configure_one<384, EpiResidLN>()) != cudaSuccess) return e;
   int dev = 0;
@@ -388,6 +434,9 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
                              EpiQkvRope{args.bias, args.rope_cos, args.rope_sin}, status, stream);
     case GemmOp::Resid384:
     case GemmOp::Resid1536:
+      if (resid_wide(rows))
+        return launch_one<384>(maps, rows, s.n, s.k, EpiResidWide{args.bias, args.lambda}, status,
+                               stream);
       return launch_one<128>(maps, rows, s.n, s.k, EpiResid{args.bias, args.lambda},
                              status, stream);
     case GemmOp::SwiGLU:

@@ -296,6 +296,70 @@ struct EpiResid {
 };
 
 // ---------------------------------------------------------------------------------------------
+// The same residual update on full 384-wide rows (a 128 x 384 tile per CTA, one tile per CTA).
+// Once the tile's accumulator is complete the mainloop's tile buffers are idle: each warp loads
+// its residual block (32 rows x 192 columns, six 32-column TMA blocks) into its part of them with
+// one mbarrier, rewrites it row by row and stores the six blocks by TMA.
+// ---------------------------------------------------------------------------------------------
+struct EpiResidWide {
+  const float *bias;
+  const float *lambda;
+  static constexpr int kSmem = 2 * kHidden * 4;
+  static constexpr bool kTmaStore = true;
+  static constexpr bool kTmaInput = true;
+  static constexpr bool kStagingInTiles = true;
+  static constexpr int kBlocks = 6;  // 32-column blocks per warp (192 columns)
+  static constexpr int kWarpStaging = kBlocks * kStageBlockBytes;
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    float *s = reinterpret_cast<float *>(smem);
+    stage_floats(s, bias, kHidden, tid, n);
+    stage_floats(s + kHidden, lambda, kHidden, tid, n);
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
+    static_assert(COLS == 32 * kBlocks, "six 32-column blocks per warp");
+    if (c.lane == 0) {
+      mbar_arrive_expect_tx(&c.in_bar[0], kBlocks * kStageBlockBytes);
+#pragma unroll
+      for (int j = 0; j < kBlocks; ++j)
+        tma_load_2d(c.staging + j * kStageBlockBytes, c.out_map, &c.in_bar[0], n0 + 32 * j, c.row0);
+    }
+    const float *sb = reinterpret_cast<const float *>(c.smem);
+    const float *sl = sb + kHidden;
+    const int sw = (c.lane >> 1) & 3;
+    if (!__all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag))) {
+      c.failed = true;
+      return;
+    }
+#pragma unroll 1
+    for (int j = 0; j < kBlocks; ++j) {
+      uint32_t r[32];
+      tmem_load32(taddr + 32 * j, r);
+      uint8_t *rowp = c.staging + j * kStageBlockBytes + c.lane * 64;
+      uint4 q[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q[k] = *reinterpret_cast<const uint4 *>(rowp + ((k ^ sw) << 4));
+      float v[32], b[32], l[32];
+      unpack_half32(q, v);
+      lds32(sb + n0 + 32 * j, b);
+      lds32(sl + n0 + 32 * j, l);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += l[i] * (u2f(r[i]) + b[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) = pack8(v, k);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (c.lane == 0) {
+        tma_store_2d(c.out_map, c.staging + j * kStageBlockBytes, n0 + 32 * j, c.row0);
+        bulk_commit();
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
 // Gate/up with SwiGLU: the weight rows are packed 64 gate rows, the matching 64 up rows, ...;
 // act[row][j] = f16(silu(g + bg) (u + bu)), silu through the hardware tanh (one MUFU op).
 // ---------------------------------------------------------------------------------------------

@@ -49,6 +49,9 @@ struct GemmShape {
   int k;       // reduction length
 };
 GemmShape gemm_shape(GemmOp op);
+// The shape a launch over `rows` rows uses (the residual GEMMs widen to 384 columns when their M
+// tiles fit one wave).
+GemmShape gemm_shape(GemmOp op, uint32_t rows);
 
 // Tensor maps of one GEMM launch: A = activations [rows][k], B = weights [n][k].
 struct GemmMaps {
