@@ -186,12 +186,23 @@ bool all_aligned(P... p) {
 
 int bad_args(const char *what) { return fail(DV3_INVALID_ARGUMENT, what); }
 
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
 int gemm_entry(dv3::GemmOp op, const void *a, uint32_t rows, const void *w,
                const dv3::GemmArgs &args, uint32_t *status, void *stream) {
   if (rows == 0) return DV3_OK;
   dv3::GemmMaps maps;
   std::string err;
-  if (!dv3::make_gemm_maps(op, a, rows, w, args.out, &maps, &err)) return bad_args(err.c_str());
+  const bool ln = op == dv3::GemmOp::ResidLN384 || op == dv3::GemmOp::ResidLN1536;
+  const void *ln_out = args.ln_out_f32 ? static_cast<const void *>(args.ln_out_f32)
+                                       : static_cast<const void *>(args.ln_out);
+  if (!dv3::make_gemm_maps(op, a, rows, w, args.out, &maps, &err, ln ? ln_out : nullptr,
+                           args.ln_out_f32 != nullptr))
+    return bad_args(err.c_str());
   return launch_status(dv3::launch_gemm(op, maps, rows, args, status, static_cast<cudaStream_t>(stream)),
                        dv3::gemm_name(op));
 }
@@ -281,6 +292,8 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
     return bad_args("pointers must be 16-byte aligned");
   if (k != 384 && k != 1536) return bad_args("k must be 384 or 1536");
   if ((h == nullptr) == (out_f32 == nullptr)) return bad_args("exactly one of h and out_f32");
+  if (rows > 128u * static_cast<uint32_t>(dv3::sm_count(current_device())))
+    return bad_args("rows must fit one 128-row tile per SM");
   dv3::GemmArgs g;
   g.bias = bias;
   g.lambda = lambda;

@@ -23,6 +23,8 @@
 // Tiles are walked m-major with the N tile fastest (tile t -> m = t / n_tiles, n = t % n_tiles)
 // by a grid of min(tiles, SMs) persistent CTAs, so the CTAs working at one time share A rows
 // through L2.
+#include <type_traits>
+
 #include "gemm_epilogues.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -99,8 +101,8 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
 template <int BN, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, int M, int n_tiles_n, int k_blocks,
-                Epi epi, uint32_t *status) {
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                int M, int n_tiles_n, int k_blocks, Epi epi, uint32_t *status) {
   using C = GemmCfg<BN, Epi>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -135,6 +137,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
     if (Epi::kTmaStore) tma_prefetch_map(&tmC);
+    if (std::is_same<Epi, EpiResidLN>::value) tma_prefetch_map(&tmD);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -255,6 +258,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ctx.staging = smem + C::kStagingOffset + (warp - 2) * 2 * kStageBlockBytes;
     ctx.buf = 0;
     ctx.out_map = &tmC;
+    ctx.ln_map = &tmD;
     ctx.in_bar = in_bars + 2 * (warp - 2);
     ctx.iter = 0;
     ctx.abort_flag = abort_flag;
@@ -312,12 +316,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// The residual GEMMs run on full 384-wide rows (one tile per CTA, A read once) while all M tiles
-// fit in one wave of CTAs, else on 128-wide tiles.
-static bool resid_wide(uint32_t rows) {
+// The residual GEMMs run on full 384-wide rows (one tile per CTA, A read once: about 0.56 us per
+// 64-deep k-block for three 128-column tiles' worth of MMAs, against 0.31 us per k-block for one
+// 128-wide tile) once 128-wide tiles would need more than one wave of CTAs, as long as all the
+// full-row tiles fit one wave. Below that the 128-wide tiles keep three times as many SMs busy.
+bool resid_wide(uint32_t rows) {
   int dev = 0;
   cudaGetDevice(&dev);
-  return (rows + BM - 1) / BM <= static_cast<uint32_t>(sm_count(dev));
+  const uint32_t m_tiles = (rows + BM - 1) / BM, sms = static_cast<uint32_t>(sm_count(dev));
+  return 3 * m_tiles > sms && m_tiles <= sms;
 }
 
 GemmShape gemm_shape(GemmOp op, uint32_t rows) {
@@ -361,24 +368,36 @@ static uint32_t tma_store_cols(GemmOp op) {
     case GemmOp::QkvRope: return kQkv;
     case GemmOp::SwiGLU: return kMlp;
     case GemmOp::Resid384:
-    case GemmOp::Resid1536: return kHidden;
+    case GemmOp::Resid1536:
+    case GemmOp::ResidLN384:
+    case GemmOp::ResidLN1536: return kHidden;
     default: return 0;
   }
 }
 
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
-                    GemmMaps *maps, std::string *err) {
+                    GemmMaps *maps, std::string *err, const void *ln_out, bool ln_f32) {
   const GemmShape s = gemm_shape(op, rows);
   const uint32_t b_rows = s.bn > 256 ? s.bn / 2 : s.bn;  // one TMA box per MMA of the K step
   if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err) ||
       !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))
     return false;
+  maps->d = maps->a;  // unused unless the epilogue writes a LayerNorm output
   const uint32_t c_cols = tma_store_cols(op);
   if (c_cols == 0) {
     maps->c = maps->a;  // unused by this epilogue
     return true;
   }
-  return encode_map_f16_swizzled(&maps->c, out, c_cols, rows, 32, 32, 64, err);
+  if (!encode_map_f16_swizzled(&maps->c, out, c_cols, rows, 32, 32, 64, err)) return false;
+  if (op == GemmOp::ResidLN384 || op == GemmOp::ResidLN1536) {
+    if (ln_out == nullptr) {
+      if (err) *err = "the fused LayerNorm needs an output tensor";
+      return false;
+    }
+    return ln_f32 ? encode_map_f32(&maps->d, ln_out, kHidden, rows, 32, 32, err)
+                  : encode_map_f16_swizzled(&maps->d, ln_out, kHidden, rows, 32, 32, 64, err);
+  }
+  return true;
 }
 
 template <int BN, class Epi>
@@ -402,7 +421,7 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
   const int tiles = static_cast<int>((rows + BM - 1) / BM) * n_tiles_n;
   const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
-                    gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c,
+                    gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,
                     static_cast<int>(rows), n_tiles_n, k / BK, epi, status);
 }
 
@@ -444,8 +463,8 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
     case GemmOp::ResidLN384:
     case GemmOp::ResidLN1536:
       return launch_one<384>(maps, rows, s.n, s.k,
-                             EpiResidLN{args.bias, args.lambda, args.out, args.gamma, args.beta,
-                                        args.ln_out, args.ln_out_f32},
+                             EpiResidLN{args.bias, args.lambda, args.gamma, args.beta,
+                                        args.ln_out_f32 != nullptr},
                              status, stream);
   }
   return cudaErrorInvalidValue;

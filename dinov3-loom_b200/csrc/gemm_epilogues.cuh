@@ -47,6 +47,7 @@ struct EpiCtx {
   uint8_t *staging;    // this warp's two staging blocks
   int buf;             // staging block to use next
   const CUtensorMap *out_map;
+  const CUtensorMap *ln_map;  // EpiResidLN: the LayerNorm output
   uint64_t *in_bar;    // kTmaInput epilogues: this warp's two input-block mbarriers
   uint32_t iter;       // tiles this warp has processed (input-block barrier parity)
   volatile int *abort_flag;
@@ -394,25 +395,32 @@ struct EpiSwiGLU {
 };
 
 // ---------------------------------------------------------------------------------------------
-// Residual update fused with the following LayerNorm, for full-row tiles (BN = 384):
+// Residual update fused with the following LayerNorm, on full-row tiles (BN = 384, one tile per
+// CTA, staged in the idle mainloop buffers like EpiResidWide):
 //   x[row] = f16(x + lambda (acc + b))                        (matmul_resid_f16_wmma.loom)
 //   h[row] = f16(LN(x[row]))  or  out[row] = LN(x[row]) f32   (layernorm_rowwave_*.loom)
-// The two threads that own a row (one per column half) each hold 192 columns: pass 1 writes x
-// and puts the f16-rounded x back into TMEM (over the accumulator) while summing it; the halves
-// meet in shared memory for the mean; pass 2 sums squared deviations (same exchange); pass 3
-// normalises. eps 1e-5, f32 arithmetic, biased variance. Rows are written directly.
+// Each warp owns 32 rows x 192 columns (its lane quarter, its column half). Its x blocks come in
+// by TMA, are updated in place in shared memory and leave by TMA; the LayerNorm then reads the
+// stored f16 values back from shared memory, as the separate kernel reads them from memory. The
+// two warps of a row meet in shared memory for the row sum, then for the sum of squared
+// deviations (two-pass centred variance, eps 1e-5, f32). The normalised blocks are staged in the
+// second half of the tile buffers and leave by TMA: six f16 32x32 blocks, or (f32 output) two
+// rounds of three 32x32 f32 blocks.
 // ---------------------------------------------------------------------------------------------
 struct EpiResidLN {
   const float *bias;
   const float *lambda;
-  __half *x;
   const float *gamma;
   const float *beta;
-  __half *h;       // f16 LayerNorm output, or
-  float *out_f32;  // f32 LayerNorm output (the final norm) when non-null
-  static constexpr int kRed = 4 * kHidden * 4;            // after bias, lambda, gamma, beta
-  static constexpr int kSmem = kRed + 4 * 128 * 4;         // + [sum | sq][half][row]
-  static constexpr bool kTmaStore = false;
+  bool f32_out;
+  static constexpr int kVecs = 4 * kHidden;  // bias, lambda, gamma, beta
+  static constexpr int kSmem = kVecs * 4 + 4 * 128 * 4;  // + [2 halves][128 rows] sum, squares
+  static constexpr bool kTmaStore = true;
+  static constexpr bool kTmaInput = true;
+  static constexpr bool kStagingInTiles = true;
+  static constexpr int kBlocks = 6;  // 32-column blocks per warp (192 columns)
+  static constexpr int kWarpStaging = kBlocks * kStageBlockBytes;
+  static constexpr int kF32Block = 32 * 128;  // 32 rows x 32 f32 columns
   using Pre = NoPre;
   __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
@@ -422,94 +430,114 @@ struct EpiResidLN {
     stage_floats(s + 2 * kHidden, gamma, kHidden, tid, n);
     stage_floats(s + 3 * kHidden, beta, kHidden, tid, n);
   }
+  // Row lane of a 32x32 f16 block (64-byte swizzle): its four 16-byte chunks.
+  __device__ static void load_row(const uint8_t *rowp, int sw, float (&v)[32]) {
+    uint4 q[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) q[k] = *reinterpret_cast<const uint4 *>(rowp + ((k ^ sw) << 4));
+    unpack_half32(q, v);
+  }
   template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
-    const float *sb = reinterpret_cast<const float *>(c.smem);
-    const float *sl = sb + kHidden, *sg = sb + 2 * kHidden, *sbe = sb + 3 * kHidden;
-    float *red = reinterpret_cast<float *>(c.smem + kRed);
-    const int row = c.row, half = c.half, r = c.r;
-    const bool ok = row < c.M;
-    __half *xr = x + static_cast<size_t>(row) * kHidden + n0;
-    uint4 cur[4] = {}, nxt[4] = {};
-    if (ok) ldg_half32(xr, cur);
-    float s = 0.f;
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
+    static_assert(COLS == 32 * kBlocks, "six 32-column blocks per warp");
+    if (c.lane == 0) {
+      mbar_arrive_expect_tx(&c.in_bar[0], kBlocks * kStageBlockBytes);
+#pragma unroll
+      for (int j = 0; j < kBlocks; ++j)
+        tma_load_2d(c.staging + j * kStageBlockBytes, c.out_map, &c.in_bar[0], n0 + 32 * j, c.row0);
+    }
+    const float *sv = reinterpret_cast<const float *>(c.smem);
+    float *red = const_cast<float *>(sv) + kVecs;  // [0..255] sums, [256..511] squares
+    const int sw = (c.lane >> 1) & 3;
+    if (!__all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag))) {
+      c.failed = true;
+      return;
+    }
+    // x = f16(x + lambda (acc + b)), in place, out by TMA; sum of the stored values
+    float sum = 0.f;
 #pragma unroll 1
-    for (int k = 0; k < COLS; k += 32) {
-      if (ok && k + 32 < COLS) ldg_half32(xr + k + 32, nxt);
-      uint32_t acc[32];
-      tmem_load32(taddr + k, acc);
+    for (int j = 0; j < kBlocks; ++j) {
+      uint32_t r[32];
+      tmem_load32(taddr + 32 * j, r);
+      uint8_t *rowp = c.staging + j * kStageBlockBytes + c.lane * 64;
+      float v[32], b[32], l[32];
+      load_row(rowp, sw, v);
+      lds32(sv + n0 + 32 * j, b);
+      lds32(sv + kHidden + n0 + 32 * j, l);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += l[i] * (u2f(r[i]) + b[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 p = pack8(v, k);
+        *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) = p;
+        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_half2(w[e]);
+          sum += f.x + f.y;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (c.lane == 0) {
+        tma_store_2d(c.out_map, c.staging + j * kStageBlockBytes, n0 + 32 * j, c.row0);
+        bulk_commit();
+      }
+    }
+    red[c.half * 128 + c.r] = sum;
+    named_barrier(1, kEpilogueThreads);
+    const float mean = (red[c.r] + red[128 + c.r]) * (1.0f / kHidden);
+    float sq = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < kBlocks; ++j) {
       float v[32];
-      if (ok) {
-        float b[32], l[32];
-        unpack_half32(cur, v);
-        lds32(sb + n0 + k, b);
-        lds32(sl + n0 + k, l);
-        uint4 *dst = reinterpret_cast<uint4 *>(xr + k);
+      load_row(c.staging + j * kStageBlockBytes + c.lane * 64, sw, v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t pk[4];
+      for (int i = 0; i < 32; ++i) sq += (v[i] - mean) * (v[i] - mean);
+    }
+    red[256 + c.half * 128 + c.r] = sq;
+    named_barrier(1, kEpilogueThreads);
+    const float rstd = rsqrtf((red[256 + c.r] + red[384 + c.r]) * (1.0f / kHidden) + 1e-5f);
+    uint8_t *out_stage = c.staging + kEpilogueWarps * kWarpStaging;  // second half of the buffers
+#pragma unroll 1
+    for (int j = 0; j < kBlocks; ++j) {
+      float v[32], g[32], bt[32];
+      load_row(c.staging + j * kStageBlockBytes + c.lane * 64, sw, v);
+      lds32(sv + 2 * kHidden + n0 + 32 * j, g);
+      lds32(sv + 3 * kHidden + n0 + 32 * j, bt);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 8 * j + 2 * e;
-            pk[e] = pack_half2(v[i] + l[i] * (u2f(acc[i]) + b[i]),
-                               v[i + 1] + l[i + 1] * (u2f(acc[i + 1]) + b[i + 1]));
-            const float2 rounded = unpack_half2(pk[e]);  // the LayerNorm reads the stored f16
-            v[i] = rounded.x;
-            v[i + 1] = rounded.y;
-          }
-          dst[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * rstd * g[i] + bt[i];
+      if (!f32_out) {
+        uint8_t *rowp = out_stage + j * kStageBlockBytes + c.lane * 64;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) = pack8(v, k);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (c.lane == 0) {
+          tma_store_2d(c.ln_map, out_stage + j * kStageBlockBytes, n0 + 32 * j, c.row0);
+          bulk_commit();
         }
       } else {
+        // f32: 128-byte rows, 128-byte swizzle; three blocks fit the warp's space at a time
+        const int slot = j % 3;
+        if (j == 3) {
+          if (c.lane == 0) bulk_wait_read<0>();  // the first round's stores have read their blocks
+          __syncwarp();
+        }
+        uint8_t *blk = out_stage + slot * kF32Block;
+        uint8_t *rowp = blk + c.lane * 128;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s += v[i];
-        acc[i] = __float_as_uint(v[i]);
-      }
-      tmem_st32(taddr + k, acc);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
-    }
-    tmem_st_wait();
-    red[half * 128 + r] = s;
-    named_barrier(1, kEpilogueThreads);
-    const float mean = (red[r] + red[128 + r]) * (1.0f / kHidden);
-    float d = 0.f;
-#pragma unroll 1
-    for (int k = 0; k < COLS; k += 32) {
-      uint32_t v[32];
-      tmem_load32(taddr + k, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float t = u2f(v[i]) - mean;
-        d += t * t;
-      }
-    }
-    red[256 + half * 128 + r] = d;
-    named_barrier(1, kEpilogueThreads);
-    const float rstd = rsqrtf((red[256 + r] + red[384 + r]) * (1.0f / kHidden) + 1e-5f);
-#pragma unroll 1
-    for (int k = 0; k < COLS; k += 32) {
-      uint32_t v[32];
-      tmem_load32(taddr + k, v);
-      float g[32], b[32], y[32];
-      lds32(sg + n0 + k, g);
-      lds32(sbe + n0 + k, b);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) y[i] = (u2f(v[i]) - mean) * rstd * g[i] + b[i];
-      if (ok) {
-        if (out_f32) {
-          float4 *o = reinterpret_cast<float4 *>(out_f32 + static_cast<size_t>(row) * kHidden + n0 + k);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-        } else {
-          store_half32(h + static_cast<size_t>(row) * kHidden + n0 + k, y);
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4 *>(rowp + ((k ^ (c.lane & 7)) << 4)) =
+              make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (c.lane == 0) {
+          tma_store_2d(c.ln_map, blk, n0 + 32 * j, c.row0);
+          bulk_commit();
         }
       }
     }
-    named_barrier(1, kEpilogueThreads);  // `red` is reused by the next tile
   }
 };
 

@@ -31,6 +31,10 @@ bool encode_map_f16_swizzled(CUtensorMap *map, const void *base, uint64_t cols, 
                              uint32_t box_cols, uint32_t box_rows, uint32_t swizzle_bytes,
                              std::string *err);
 
+// 2D f32 tensor [rows][cols], box = 32 columns (128 bytes) x box_rows, 128-byte swizzle.
+bool encode_map_f32(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                    uint32_t box_cols, uint32_t box_rows, std::string *err);
+
 // 3D f16 view [n_images][201 tokens][cols] of token rows, box = 64 columns x box_rows tokens x 1
 // image, 128-byte swizzle. Tokens past 201 fall outside the image: loads read zeros, stores
 // are clipped.
@@ -52,16 +56,22 @@ GemmShape gemm_shape(GemmOp op);
 // The shape a launch over `rows` rows uses (the residual GEMMs widen to 384 columns when their M
 // tiles fit one wave).
 GemmShape gemm_shape(GemmOp op, uint32_t rows);
+// Whether the residual GEMMs over `rows` rows run on full 384-wide rows (the ResidLN* ops always
+// do; they need every 128-row tile in one wave of CTAs).
+bool resid_wide(uint32_t rows);
 
 // Tensor maps of one GEMM launch: A = activations [rows][k], B = weights [n][k].
 struct GemmMaps {
   CUtensorMap a;
   CUtensorMap b;
   CUtensorMap c;  // the epilogue's output, for epilogues that store through TMA
+  CUtensorMap d;  // ResidLN*: the LayerNorm output (f16 h, or the f32 final output)
 };
-// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch and ResidLN*).
+// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch). ResidLN* also takes
+// the LayerNorm output: `ln_out` f16 [rows][384], or f32 when `ln_f32`.
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
-                    GemmMaps *maps, std::string *err);
+                    GemmMaps *maps, std::string *err, const void *ln_out = nullptr,
+                    bool ln_f32 = false);
 
 struct GemmArgs {
   const float *bias = nullptr;

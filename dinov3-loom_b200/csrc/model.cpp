@@ -174,13 +174,14 @@ void Model::release() {
 // embed scatter), LN1 of layer 0, then per layer QKV+RoPE, attention, o-proj+LS1+residual+LN2,
 // gate/up+SwiGLU, and down-proj+LS2+residual+(LN1 of the next layer | final LN). The reference
 // launches each LayerNorm separately (87 launches at b > 1); here each one after layer 0's
-// first rides in the epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches).
-// Full-row tiles give ceil(201b/128) CTAs, too few for small batches, which therefore keep the
-// 128-column residual GEMMs and separate LayerNorm launches (3 + 12*7 = 87 launches).
-// DV3_FUSE_LAYERNORM=0/1 in the environment overrides the choice (for measurement).
+// first rides in the epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches),
+// whenever the residual GEMMs run on full rows (large batches; see resid_wide); small batches
+// keep 128-wide residual tiles and separate LayerNorm launches (3 + 12*7 = 87).
+// DV3_FUSE_LAYERNORM=0 in the environment restores the separate LayerNorm launches (3 + 12*7 =
+// 87, the reference's plan) for comparison; =1 forces fusion.
 bool Model::fuse_layernorm(size_t b) const {
   if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
-  return b >= kFuseLayerNormMinBatch;
+  return resid_wide(static_cast<uint32_t>(kTokens * b));
 }
 
 Plan &Model::prepare(size_t b) {
@@ -228,9 +229,11 @@ Plan &Model::prepare(size_t b) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
     need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, qkv, &qkv_maps, &err));
-    need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err));
+    need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err, h));
     need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, act, &gu_maps, &err));
-    need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err));
+    need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err,
+                        i == 11 ? static_cast<const void *>(out) : static_cast<const void *>(h),
+                        i == 11));
     add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;

@@ -47,10 +47,6 @@ struct Plan {
   size_t kernels = 0;
 };
 
-// Smallest batch whose plan fuses each LayerNorm into the residual GEMM before it. Measured on
-// B200, the full-row tiles that fusion needs lose to the 128-wide tiles plus a separate
-// LayerNorm at every batch size up to 64, so no resident batch fuses by default.
-constexpr size_t kFuseLayerNormMinBatch = DV3_MAX_BATCH_LIMIT + 1;
 
 class Model {
  public:

@@ -66,6 +66,33 @@ bool encode_map_f16_swizzled(CUtensorMap *map, const void *base, uint64_t cols, 
   return true;
 }
 
+bool encode_map_f32(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                    uint32_t box_cols, uint32_t box_rows, std::string *err) {
+  auto fn = encode_fn(err);
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 4) % 16 != 0 || rows == 0 ||
+      box_cols * 4 != 128 || box_rows == 0 || box_rows > 256) {
+    if (err) *err = "tensor map: base must be 16-byte aligned, rows of whole 16-byte units";
+    return false;
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 4};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides,
+                  box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) {
+      char buf[128];
+      std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+      *err = buf;
+    }
+    return false;
+  }
+  return true;
+}
+
 bool encode_map_f16_images(CUtensorMap *map, const void *base, uint64_t cols, uint64_t n_images,
                            uint32_t box_rows, std::string *err) {
   auto fn = encode_fn(err);

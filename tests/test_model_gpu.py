@@ -176,6 +176,9 @@ def test_full_size_batch_properties(models, oracles):
     two images match the oracle, and repeats are bitwise identical."""
     model = models("baseline", max_batch=64)
     images = synth.images(2024, 64)
+    # batch 64 fuses the LayerNorms into the residual GEMMs; single images use the split plan
+    assert model.launches_per_forward(64) == 3 + 12 * 5
+    assert model.launches_per_forward(1) == 3 + 12 * 7
     out = model.forward(images)
     assert np.isfinite(out).all()
     for i in (0, 17, 63):
@@ -204,9 +207,10 @@ def test_benchmark_and_profile(models):
 
 
 def test_fused_layernorm_plan(weights_file, monkeypatch):
-    """The plan variant that rides each LayerNorm after the first in the preceding residual GEMM
-    (3 + 12*5 launches; DV3_FUSE_LAYERNORM=1, read when a batch size's graph is built) gives the
-    same result as the default plan within f16 rounding."""
+    """Large batches ride each LayerNorm after the first in the preceding residual GEMM
+    (3 + 12*5 launches); small ones keep separate LayerNorm launches (3 + 12*7, the reference's
+    plan). At 16 images the default is the split plan; DV3_FUSE_LAYERNORM=1 (read when a batch
+    size's graph is built) forces fusion, which gives the same result within f16 rounding."""
     path = weights_file(1, "stress")
     images = synth.images(31, 16)
     with dv.DINOv3.load(path, dv.Options(0, 16)) as model:
