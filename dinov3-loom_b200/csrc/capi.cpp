@@ -72,38 +72,12 @@ int dv3_forward(dv3_model *m, const float *pixels, size_t n, float *out, size_t 
 
 int dv3_cls(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
   if (int rc = check_model(m)) return rc;
-  return guarded([&] {
-    if (n % DV3_IMAGE_ELEMENTS != 0)
-      throw dv3::Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
-    const size_t batch = n / DV3_IMAGE_ELEMENTS;
-    if (out_n < batch * DV3_HIDDEN)
-      throw dv3::Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * DV3_HIDDEN) + " floats");
-    std::vector<float> full(batch * DV3_TOKENS * DV3_HIDDEN);
-    m->impl.forward(pixels, n, full.data(), full.size());
-    for (size_t i = 0; i < batch; ++i)
-      std::memcpy(out + i * DV3_HIDDEN, full.data() + i * DV3_TOKENS * DV3_HIDDEN, DV3_HIDDEN * sizeof(float));
-  });
+  return guarded([&] { m->impl.forward(pixels, n, out, out_n, dv3::Model::Readout::Cls); });
 }
 
 int dv3_patch_mean(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
   if (int rc = check_model(m)) return rc;
-  return guarded([&] {
-    if (n % DV3_IMAGE_ELEMENTS != 0)
-      throw dv3::Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
-    const size_t batch = n / DV3_IMAGE_ELEMENTS;
-    if (out_n < batch * DV3_HIDDEN)
-      throw dv3::Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * DV3_HIDDEN) + " floats");
-    std::vector<float> full(batch * DV3_TOKENS * DV3_HIDDEN);
-    m->impl.forward(pixels, n, full.data(), full.size());
-    // src/lib.rs:134-148: f32 accumulation of row / 196, rows 5..200 in order.
-    for (size_t i = 0; i < batch; ++i) {
-      float acc[DV3_HIDDEN] = {};
-      const float *img = full.data() + i * DV3_TOKENS * DV3_HIDDEN;
-      for (int t = 5; t < DV3_TOKENS; ++t)
-        for (int c = 0; c < DV3_HIDDEN; ++c) acc[c] += img[t * DV3_HIDDEN + c] / 196.0f;
-      std::memcpy(out + i * DV3_HIDDEN, acc, sizeof acc);
-    }
-  });
+  return guarded([&] { m->impl.forward(pixels, n, out, out_n, dv3::Model::Readout::PatchMean); });
 }
 
 int dv3_benchmark(dv3_model *m, const float *pixels, size_t n, size_t samples, dv3_timings *out) {

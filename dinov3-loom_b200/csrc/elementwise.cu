@@ -171,6 +171,29 @@ cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *ga
                     static_cast<int>(rows), gamma, beta, static_cast<void *>(out));
 }
 
+// patch_mean (src/lib.rs:134-148) on the device: one thread per (image, channel) adds
+// row / 196 over the patch rows 5..200 in order, in f32 with correctly rounded division, so the
+// result equals the reference's host loop bit for bit. Reads are coalesced across channels.
+__global__ void __launch_bounds__(128)
+    patch_mean_kernel(const float *__restrict__ out, int n_images, float *__restrict__ dst) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;  // channel
+  const int img = blockIdx.y;
+  if (c >= kHidden || img >= n_images) return;
+  const float *src = out + static_cast<size_t>(img) * kTokens * kHidden + c;
+  float acc = 0.f;
+#pragma unroll 4
+  for (int t = kPrefix; t < kTokens; ++t) acc = __fadd_rn(acc, __fdiv_rn(src[t * kHidden], 196.0f));
+  dst[static_cast<size_t>(img) * kHidden + c] = acc;
+}
+
+cudaError_t launch_patch_mean(const float *out, uint32_t n_images, float *dst,
+                              cudaStream_t stream) {
+  if (n_images == 0) return cudaSuccess;
+  patch_mean_kernel<<<dim3(kHidden / 128, n_images), 128, 0, stream>>>(
+      out, static_cast<int>(n_images), dst);
+  return cudaGetLastError();
+}
+
 int sm_count(int device) {
   static int cache[64] = {};
   if (device < 0 || device >= 64) return 148;

@@ -110,6 +110,10 @@ cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *ga
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, float *out, cudaStream_t stream);
 
+// Mean of each image's 196 patch rows of the f32 output (the reference's f32 order), n x 384.
+cudaError_t launch_patch_mean(const float *out, uint32_t n_images, float *dst,
+                              cudaStream_t stream);
+
 // Packed gate/up row order: 64 gate rows, the matching 64 up rows, then the next 64 of each.
 inline uint32_t gateup_source_row(uint32_t packed) {
   const uint32_t block = packed / 128, within = packed % 128;

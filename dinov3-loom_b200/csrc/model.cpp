@@ -13,6 +13,7 @@
 //   act     f16 [201B][1536]       SwiGLU output
 //   out     f32 [201B][384]        final LayerNorm output
 //   status  u32 [2]                device failure bits, non-finite input flag (sticky until read)
+//   pmean   f32 [B][384]           patch-token means (patch_mean readout)
 // The QKV buffer needs no headroom rows: attention reads through TMA, whose out-of-bounds rows
 // are zero.
 #include "model.h"
@@ -123,11 +124,12 @@ Model::Model(const std::string &path, dv3_options options)
 
     // Activations for max_batch images.
     const size_t B = max_batch_, R = kTokens * B, P = kPatches * B;
-    const size_t sizes[9] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
-                             R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
-                             R * kMlp * 2,           R * kHidden * 4, 256};
-    size_t at[9], act_total = 0;
-    for (int i = 0; i < 9; ++i) {
+    const size_t sizes[10] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
+                              R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
+                              R * kMlp * 2,           R * kHidden * 4, 256,
+                              B * kHidden * 4};
+    size_t at[10], act_total = 0;
+    for (int i = 0; i < 10; ++i) {
       at[i] = act_total;
       act_total += align256(sizes[i]);
     }
@@ -142,6 +144,7 @@ Model::Model(const std::string &path, dv3_options options)
     act_ = reinterpret_cast<__half *>(a + at[6]);
     out_ = reinterpret_cast<float *>(a + at[7]);
     status_ = reinterpret_cast<uint32_t *>(a + at[8]);
+    pmean_ = reinterpret_cast<float *>(a + at[9]);
     cuda(cudaMemset(status_, 0, 256), "clear status");
     cuda(cudaMallocHost(reinterpret_cast<void **>(&status_host_), 2 * sizeof(uint32_t)),
          "allocate pinned status");
@@ -329,11 +332,13 @@ void Model::check_status() {
   if (nonfinite) throw Error(DV3_INVALID_ARGUMENT, "input must be finite");
 }
 
-void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out_floats) {
+void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out_floats,
+                    Readout readout) {
   if (n_floats % kImageElements != 0)
     throw Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
   const size_t batch = n_floats / kImageElements;
-  const size_t per = static_cast<size_t>(kTokens) * kHidden;
+  const size_t tokens = static_cast<size_t>(kTokens) * kHidden;  // floats per image on the device
+  const size_t per = readout == Readout::Full ? tokens : kHidden;  // floats per image returned
   if (out_floats < batch * per)
     throw Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(batch * per) + " floats");
   if (batch && (!pixels || !out)) throw Error(DV3_INVALID_ARGUMENT, "null buffer");
@@ -346,8 +351,20 @@ void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out
                          cudaMemcpyHostToDevice, stream_),
          "upload input");
     cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
-    cuda(cudaMemcpyAsync(out + i * per, out_, b * per * sizeof(float), cudaMemcpyDeviceToHost, stream_),
-         "read output");
+    if (readout == Readout::Full) {
+      cuda(cudaMemcpyAsync(out + i * per, out_, b * per * sizeof(float), cudaMemcpyDeviceToHost,
+                           stream_),
+           "read output");
+    } else if (readout == Readout::Cls) {  // row 0 of each image: one strided copy
+      cuda(cudaMemcpy2DAsync(out + i * per, kHidden * sizeof(float), out_, tokens * sizeof(float),
+                             kHidden * sizeof(float), b, cudaMemcpyDeviceToHost, stream_),
+           "read CLS rows");
+    } else {
+      cuda(launch_patch_mean(out_, static_cast<uint32_t>(b), pmean_, stream_), "patch mean");
+      cuda(cudaMemcpyAsync(out + i * per, pmean_, b * per * sizeof(float), cudaMemcpyDeviceToHost,
+                           stream_),
+           "read patch means");
+    }
     status_pending_ = true;
     check_status();
   }

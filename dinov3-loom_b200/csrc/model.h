@@ -55,7 +55,12 @@ class Model {
   Model(const Model &) = delete;
   Model &operator=(const Model &) = delete;
 
-  void forward(const float *pixels, size_t n_floats, float *out, size_t out_floats);
+  // What a forward returns to the host: every token (b x 201 x 384), the CLS token of each image
+  // (b x 384; only those rows are read back), or the mean of the patch tokens (b x 384, reduced
+  // on the device, only the means read back).
+  enum class Readout { Full, Cls, PatchMean };
+  void forward(const float *pixels, size_t n_floats, float *out, size_t out_floats,
+               Readout readout = Readout::Full);
   void forward_device(const float *pixels, size_t n_floats, float *out, size_t out_floats);
   void run(size_t batch);
   void synchronize();
@@ -86,7 +91,7 @@ class Model {
   DeviceWeights w_{};
   __half *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *act_ = nullptr,
          *patches_ = nullptr;
-  float *image_ = nullptr, *out_ = nullptr;
+  float *image_ = nullptr, *out_ = nullptr, *pmean_ = nullptr;
   uint32_t *status_ = nullptr;       // device: [0] failure bits, [1] non-finite input
   uint32_t *status_host_ = nullptr;  // pinned mirror
   bool status_pending_ = false;      // work enqueued since the last status check

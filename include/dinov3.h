@@ -80,10 +80,14 @@ int dv3_load(const char *safetensors_path, dv3_options options, dv3_model **out)
  * Host buffers may be pageable; pinned buffers transfer faster. */
 int dv3_forward(dv3_model *m, const float *pixels, size_t n_floats, float *out, size_t out_floats);
 
-/* DINOv3::cls (src/lib.rs:126-132): the CLS token of each image, k*384 floats. */
+/* DINOv3::cls (src/lib.rs:126-132): the CLS token of each image, k*384 floats. Only those
+ * rows are copied back from the device. */
 int dv3_cls(dv3_model *m, const float *pixels, size_t n_floats, float *out, size_t out_floats);
 
-/* DINOv3::patch_mean (src/lib.rs:134-148): mean of the 196 patch tokens, k*384 floats. */
+/* DINOv3::patch_mean (src/lib.rs:134-148): mean of the 196 patch tokens, k*384 floats,
+ * reduced on the device in the reference's f32 order (row / 196 added for rows 5..200), so it
+ * equals the reference's host loop over the full output bit for bit; only the means are copied
+ * back. */
 int dv3_patch_mean(dv3_model *m, const float *pixels, size_t n_floats, float *out,
                    size_t out_floats);
 
