@@ -358,11 +358,19 @@ def run_ours(args):
     model.close()
 
     cpu = None
+    cpu_single = None
     if rank == 0 and world == 1:
-        value_cpu, cores, n, dt, _, _ = cpu_oracle_throughput(images, args.cpu_budget_s)
+        value_cpu, cores, n, dt, model_cpu, sample = cpu_oracle_throughput(images, args.cpu_budget_s)
         cpu = {"value": value_cpu, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"{n} seeded 224x224 images of the batch-64 workload, float64 C oracle of "
                          f"tests/support/reference.rs, OpenMP over images, {dt:.1f} s"}
+        # The reference's own CPU path is single-threaded (matrixmultiply without its threading
+        # feature): the same oracle on one image with one thread.
+        t0 = time.perf_counter()
+        model_cpu.forward(np.ascontiguousarray(sample[:1]), threads=1)
+        dt1 = time.perf_counter() - t0
+        cpu_single = {"value": 1.0 / dt1, "unit": UNIT, "cores": 1, "kind": "port",
+                      "sample": f"1 seeded 224x224 image, float64 C oracle, 1 thread, {dt1:.2f} s"}
 
     if rank == 0:
         line = {
@@ -383,6 +391,7 @@ def run_ours(args):
                          "traffic": committed_traffic("gemm_gateup_swiglu"),
                          "algorithmic_bytes": GATEUP_BYTES_B64, "avg_launch_ms": gate_ms},
             "cpu_baseline": cpu,
+            "cpu_baseline_single": cpu_single,
             "p50_batch1_latency_ms": {"device": statistics.median(lat_dev), "e2e": statistics.median(lat_e2e)},
             "tflops_whole_forward": value / world * GFLOP_PER_IMAGE / 1000.0,
             "kernel_time_share": kernel_share,
