@@ -58,6 +58,11 @@ def parse_args():
     ap.add_argument("--forward-only", action="store_true",
                     help="profiling driver: load, stage one batch, replay warmup+steps forwards, exit")
     ap.add_argument("--batch", type=int, default=BATCH, help="images per forward (--forward-only)")
+    ap.add_argument("--serve", action="store_true",
+                    help="serving measurement (BASELINE config 4): calls of seeded random size "
+                         "1..64 from pinned host memory, synchronous and two-deep pipelined")
+    ap.add_argument("--serve-images", type=int, default=8192,
+                    help="images over all GPUs in the serving measurement")
     return ap.parse_args()
 
 
@@ -272,6 +277,10 @@ def run_ours(args):
     staged.copy_(torch.from_numpy(images).reshape(-1))
     torch.cuda.synchronize()
 
+    if args.serve:
+        run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist)
+        return
+
     if args.forward_only:
         b = max(1, min(args.batch, BATCH))
         for _ in range(args.warmup + args.steps):
@@ -399,6 +408,73 @@ def run_ours(args):
             "wall_s_timed_region": wall,
         }
         print(json.dumps(line), flush=True)
+    if dist is not None:
+        barrier()
+        dist.destroy_process_group()
+
+
+def run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist):
+    """each rank serves its share of `--serve-images` images in calls of seeded
+    uniform random size 1..64, from pinned host memory into pinned host memory, timed on the
+    host clock per call. Two passes: synchronous dv3_forward per call, then dv3_submit with two
+    calls in flight (a call is submitted, the call two before it is waited). Rank 0 prints one
+    JSON line: aggregate images/s over all ranks (images / max wall time) and per-call p50/p99."""
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(4 + rank)
+    share = args.serve_images // world
+    sizes = []
+    while sum(sizes) < share:
+        sizes.append(int(min(rng.integers(1, BATCH + 1), share - sum(sizes))))
+    pin_in = torch.from_numpy(images).pin_memory()
+    outs = [torch.empty((BATCH, 201, 384), dtype=torch.float32).pin_memory() for _ in range(3)]
+    # warm the CUDA graphs of every batch size used, for both serving slots
+    for k in sorted(set(sizes)):
+        model.forward(pin_in[:k], out=outs[0][:k])
+        for slot in range(2):
+            model.wait(model.submit(pin_in[:k], outs[slot][:k]))
+
+    def percentile(v, q):
+        return float(np.percentile(np.asarray(v), q))
+
+    results = {}
+    for mode in ("sync", "pipelined"):
+        lat = []
+        barrier()
+        t_start = time.perf_counter()
+        if mode == "sync":
+            for k in sizes:
+                t0 = time.perf_counter()
+                model.forward(pin_in[:k], out=outs[0][:k])
+                lat.append((time.perf_counter() - t0) * 1000)
+        else:
+            pending = []  # (ticket, submit time)
+            for i, k in enumerate(sizes):
+                if len(pending) == 2:
+                    tk, ts = pending.pop(0)
+                    model.wait(tk)
+                    lat.append((time.perf_counter() - ts) * 1000)
+                ts = time.perf_counter()
+                pending.append((model.submit(pin_in[:k], outs[i % 3][:k]), ts))
+            for tk, ts in pending:
+                model.wait(tk)
+                lat.append((time.perf_counter() - ts) * 1000)
+        wall = time.perf_counter() - t_start
+        wall_max = max_over_ranks(wall)
+        results[mode] = {"images_per_s": share * world / wall_max,
+                         "p50_ms": percentile(lat, 50), "p99_ms": percentile(lat, 99),
+                         "calls_per_gpu": len(sizes), "wall_s": wall_max}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "serving: aggregate images/s and per-call latency, calls of 1..64 images (config 4)",
+            "value": results["pipelined"]["images_per_s"], "unit": UNIT, "n_gpus": world,
+            "higher_is_better": True, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 4: seeded uniform call sizes 1..64, pinned host "
+                                   "buffers in and out, every call's full output read back",
+                       "images": share * world, "parallelism": f"replicas{world}"},
+            "sync": results["sync"], "pipelined": results["pipelined"]}), flush=True)
+    model.close()
     if dist is not None:
         barrier()
         dist.destroy_process_group()

@@ -104,6 +104,19 @@ int dv3_synchronize(dv3_model *m) {
   return guarded([&] { m->impl.synchronize(); });
 }
 
+int dv3_submit(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n,
+               uint64_t *ticket) {
+  if (int rc = check_model(m)) return rc;
+  if (!ticket) return fail(DV3_INVALID_ARGUMENT, "null ticket");
+  return guarded([&] { *ticket = m->impl.submit(pixels, n, out, out_n); });
+}
+
+int dv3_wait(dv3_model *m, uint64_t ticket) {
+  if (!m) return fail(DV3_INVALID_ARGUMENT, "null model");
+  // a poisoned model still reports each ticket's own status, then DV3_POISONED afterwards
+  return guarded([&] { m->impl.wait(ticket); });
+}
+
 int dv3_forward_device(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
   if (int rc = check_model(m)) return rc;
   return guarded([&] { m->impl.forward_device(pixels, n, out, out_n); });

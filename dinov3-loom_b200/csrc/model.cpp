@@ -14,6 +14,8 @@
 //   out     f32 [201B][384]        final LayerNorm output
 //   status  u32 [2]                device failure bits, non-finite input flag (sticky until read)
 //   pmean   f32 [B][384]           patch-token means (patch_mean readout)
+//   image1, out1                   the second serving slot's input and output (slot 0 uses
+//                                  image and out)
 // The QKV buffer needs no headroom rows: attention reads through TMA, whose out-of-bounds rows
 // are zero.
 #include "model.h"
@@ -76,6 +78,13 @@ Model::Model(const std::string &path, dv3_options options)
   activate();
   try {
     cuda(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "create stream");
+    cuda(cudaStreamCreateWithFlags(&h2d_stream_, cudaStreamNonBlocking), "create stream");
+    cuda(cudaStreamCreateWithFlags(&d2h_stream_, cudaStreamNonBlocking), "create stream");
+    for (int i = 0; i < 2; ++i) {
+      cuda(cudaEventCreateWithFlags(&ev_in_[i], cudaEventDisableTiming), "create event");
+      cuda(cudaEventCreateWithFlags(&ev_done_[i], cudaEventDisableTiming), "create event");
+      cuda(cudaEventCreateWithFlags(&ev_out_[i], cudaEventDisableTiming), "create event");
+    }
     cuda(configure_gemm_kernels(), "configure GEMM kernels");
     cuda(configure_attention_kernel(), "configure attention kernel");
 
@@ -124,12 +133,12 @@ Model::Model(const std::string &path, dv3_options options)
 
     // Activations for max_batch images.
     const size_t B = max_batch_, R = kTokens * B, P = kPatches * B;
-    const size_t sizes[10] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
+    const size_t sizes[12] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
                               R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
                               R * kMlp * 2,           R * kHidden * 4, 256,
-                              B * kHidden * 4};
-    size_t at[10], act_total = 0;
-    for (int i = 0; i < 10; ++i) {
+                              B * kHidden * 4,        B * kImageElements * 4, R * kHidden * 4};
+    size_t at[12], act_total = 0;
+    for (int i = 0; i < 12; ++i) {
       at[i] = act_total;
       act_total += align256(sizes[i]);
     }
@@ -145,6 +154,13 @@ Model::Model(const std::string &path, dv3_options options)
     out_ = reinterpret_cast<float *>(a + at[7]);
     status_ = reinterpret_cast<uint32_t *>(a + at[8]);
     pmean_ = reinterpret_cast<float *>(a + at[9]);
+    image_slot_[0] = image_;
+    out_slot_[0] = out_;
+    image_slot_[1] = reinterpret_cast<float *>(a + at[10]);
+    out_slot_[1] = reinterpret_cast<float *>(a + at[11]);
+    cuda(cudaMallocHost(reinterpret_cast<void **>(&slot_status_host_), 4 * sizeof(uint32_t)),
+         "allocate pinned status");
+    for (int i = 0; i < 4; ++i) slot_status_host_[i] = 0;
     cuda(cudaMemset(status_, 0, 256), "clear status");
     cuda(cudaMallocHost(reinterpret_cast<void **>(&status_host_), 2 * sizeof(uint32_t)),
          "allocate pinned status");
@@ -163,6 +179,19 @@ void Model::release() {
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   plans_.clear();
   if (stream_) cudaStreamSynchronize(stream_);
+  if (h2d_stream_) cudaStreamSynchronize(h2d_stream_);
+  if (d2h_stream_) cudaStreamSynchronize(d2h_stream_);
+  for (int i = 0; i < 2; ++i) {
+    if (ev_in_[i]) cudaEventDestroy(ev_in_[i]);
+    if (ev_done_[i]) cudaEventDestroy(ev_done_[i]);
+    if (ev_out_[i]) cudaEventDestroy(ev_out_[i]);
+    ev_in_[i] = ev_done_[i] = ev_out_[i] = nullptr;
+  }
+  if (h2d_stream_) cudaStreamDestroy(h2d_stream_);
+  if (d2h_stream_) cudaStreamDestroy(d2h_stream_);
+  h2d_stream_ = d2h_stream_ = nullptr;
+  if (slot_status_host_) cudaFreeHost(slot_status_host_);
+  slot_status_host_ = nullptr;
   if (status_host_) cudaFreeHost(status_host_);
   if (act_blob_) cudaFree(act_blob_);
   if (weight_blob_) cudaFree(weight_blob_);
@@ -187,8 +216,8 @@ bool Model::fuse_layernorm(size_t b) const {
   return resid_wide(static_cast<uint32_t>(kTokens * b));
 }
 
-Plan &Model::prepare(size_t b) {
-  auto it = plans_.find(b);
+Plan &Model::prepare(size_t b, int slot) {
+  auto it = plans_.find({b, slot});
   if (it != plans_.end()) return it->second;
   const uint32_t r = static_cast<uint32_t>(kTokens * b), p = static_cast<uint32_t>(kPatches * b);
   std::string err;
@@ -205,7 +234,7 @@ Plan &Model::prepare(size_t b) {
   };
   uint32_t *st = status_;
   const DeviceWeights w = w_;
-  float *image = image_, *out = out_;
+  float *image = image_slot_[slot], *out = out_slot_[slot];
   __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
 
   GemmMaps patch_maps;
@@ -310,7 +339,7 @@ Plan &Model::prepare(size_t b) {
   cudaError_t e = cudaGraphInstantiate(&plan.exec, graph, 0);
   cudaGraphDestroy(graph);
   cuda(e, "instantiate graph");
-  return plans_.emplace(b, std::move(plan)).first->second;
+  return plans_.emplace(std::make_pair(b, slot), std::move(plan)).first->second;
 }
 
 void Model::check_status() {
@@ -334,6 +363,7 @@ void Model::check_status() {
 
 void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out_floats,
                     Readout readout) {
+  drain();
   if (n_floats % kImageElements != 0)
     throw Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
   const size_t batch = n_floats / kImageElements;
@@ -371,6 +401,7 @@ void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out
 }
 
 void Model::forward_device(const float *pixels, size_t n_floats, float *out, size_t out_floats) {
+  drain();
   if (n_floats % kImageElements != 0)
     throw Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
   const size_t batch = n_floats / kImageElements;
@@ -394,7 +425,87 @@ void Model::forward_device(const float *pixels, size_t n_floats, float *out, siz
   if (batch) check_status();
 }
 
+// ---- serving path ----
+// Per submission: upload on h2d_stream_ (after the slot's previous forward consumed its input),
+// forward on stream_ (after the upload and after the slot's previous download read its output),
+// with the status words cleared before and copied to the slot's pinned words after, and the
+// download on d2h_stream_. Two slots, so consecutive submissions overlap; a third submission
+// first completes the one occupying its slot (its status is kept for its own wait).
+uint64_t Model::submit(const float *pixels, size_t n_floats, float *out, size_t out_floats) {
+  check_usable();
+  if (n_floats == 0 || n_floats % kImageElements != 0)
+    throw Error(DV3_INVALID_ARGUMENT, "input must contain complete 3×224×224 images");
+  const size_t b = n_floats / kImageElements;
+  if (b > max_batch_) throw Error(DV3_INVALID_ARGUMENT, "a submission holds at most max_batch images");
+  const size_t per = static_cast<size_t>(kTokens) * kHidden;
+  if (out_floats < b * per)
+    throw Error(DV3_INVALID_ARGUMENT, "output must hold " + std::to_string(b * per) + " floats");
+  if (!pixels || !out) throw Error(DV3_INVALID_ARGUMENT, "null buffer");
+  activate();
+  const uint64_t ticket = next_ticket_;
+  const int slot = static_cast<int>(ticket & 1);
+  if (submitted_[slot]) retire(slot);
+  Plan &plan = prepare(b, slot);
+  ++next_ticket_;
+  cuda(cudaStreamWaitEvent(h2d_stream_, ev_done_[slot], 0), "order upload");
+  cuda(cudaMemcpyAsync(image_slot_[slot], pixels, b * kImageElements * sizeof(float),
+                       cudaMemcpyHostToDevice, h2d_stream_),
+       "upload input");
+  cuda(cudaEventRecord(ev_in_[slot], h2d_stream_), "record upload");
+  cuda(cudaStreamWaitEvent(stream_, ev_in_[slot], 0), "order forward");
+  cuda(cudaStreamWaitEvent(stream_, ev_out_[slot], 0), "order forward");
+  cuda(cudaMemsetAsync(status_, 0, 2 * sizeof(uint32_t), stream_), "clear status");
+  cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+  cuda(cudaMemcpyAsync(slot_status_host_ + 2 * slot, status_, 2 * sizeof(uint32_t),
+                       cudaMemcpyDeviceToHost, stream_),
+       "read status");
+  cuda(cudaEventRecord(ev_done_[slot], stream_), "record forward");
+  cuda(cudaStreamWaitEvent(d2h_stream_, ev_done_[slot], 0), "order download");
+  cuda(cudaMemcpyAsync(out, out_slot_[slot], b * per * sizeof(float), cudaMemcpyDeviceToHost,
+                       d2h_stream_),
+       "read output");
+  cuda(cudaEventRecord(ev_out_[slot], d2h_stream_), "record download");
+  submitted_[slot] = true;
+  slot_ticket_[slot] = ticket;
+  return ticket;
+}
+
+void Model::retire(int slot) {
+  cuda(cudaEventSynchronize(ev_out_[slot]), "finish submission");
+  const uint32_t fault = slot_status_host_[2 * slot], nonfinite = slot_status_host_[2 * slot + 1];
+  finished_[slot_ticket_[slot]] = {fault, nonfinite};
+  submitted_[slot] = false;
+  if (fault) failed_ = true;  // the session is poisoned whether or not that ticket is waited
+}
+
+void Model::wait(uint64_t ticket) {
+  if (ticket >= next_ticket_) throw Error(DV3_INVALID_ARGUMENT, "unknown ticket");
+  const int slot = static_cast<int>(ticket & 1);
+  auto it = finished_.find(ticket);
+  if (it == finished_.end()) {
+    if (!submitted_[slot] || slot_ticket_[slot] != ticket)
+      throw Error(DV3_INVALID_ARGUMENT, "ticket already waited");
+    activate();
+    retire(slot);
+    it = finished_.find(ticket);
+  }
+  const auto [fault, nonfinite] = it->second;
+  finished_.erase(it);
+  if (fault) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "a kernel wait expired (device status 0x%x)", fault);
+    throw Error(DV3_POISONED, std::string(buf) + "; session is unusable after a GPU failure");
+  }
+  if (nonfinite) throw Error(DV3_INVALID_ARGUMENT, "input must be finite");
+}
+
+void Model::drain() {
+  for (int slot = 0; slot < 2; ++slot)
+    if (submitted_[slot]) retire(slot);
+}
+
 void Model::run(size_t batch) {
+  drain();
   check_usable();
   if (batch < 1 || batch > max_batch_)
     throw Error(DV3_INVALID_ARGUMENT, "batch must be 1..=max_batch");
@@ -419,6 +530,7 @@ size_t Model::launches_per_forward(size_t batch) {
 }
 
 dv3_timings Model::benchmark(const float *pixels, size_t n_floats, size_t samples) {
+  drain();
   if (n_floats == 0 || n_floats > max_batch_ * kImageElements)
     throw Error(DV3_INVALID_ARGUMENT, "benchmark requires one nonempty batch");
   std::vector<float> first(n_floats / kImageElements * kTokens * kHidden);
@@ -464,6 +576,7 @@ dv3_timings Model::benchmark(const float *pixels, size_t n_floats, size_t sample
 // residual GEMMs update x in place, so x holds garbage afterwards; the next forward rebuilds it.
 std::vector<std::pair<const char *, double>> Model::profile_launches(size_t batch,
                                                                      size_t iterations) {
+  drain();
   check_usable();
   if (batch < 1 || batch > max_batch_)
     throw Error(DV3_INVALID_ARGUMENT, "batch must be 1..=max_batch");

@@ -64,6 +64,12 @@ class Model {
   void forward_device(const float *pixels, size_t n_floats, float *out, size_t out_floats);
   void run(size_t batch);
   void synchronize();
+  // Serving path (no reference counterpart): enqueue upload, forward and download of one batch
+  // of 1..=max_batch images without waiting, into one of two buffer slots, so that the upload
+  // of one submission overlaps the forward of the previous one and the download of the one
+  // before. `wait` blocks until that submission's output is in `out` and reports its errors.
+  uint64_t submit(const float *pixels, size_t n_floats, float *out, size_t out_floats);
+  void wait(uint64_t ticket);
   dv3_timings benchmark(const float *pixels, size_t n_floats, size_t samples);
   size_t launches_per_forward(size_t batch);
   std::vector<std::pair<const char *, double>> profile_launches(size_t batch, size_t iterations);
@@ -76,7 +82,8 @@ class Model {
  private:
   void check_usable() const;
   void cuda(cudaError_t e, const char *what);  // poisons and throws on failure
-  Plan &prepare(size_t batch);                  // build + capture once per batch size
+  Plan &prepare(size_t batch, int slot = 0);    // build + capture once per batch size and slot
+  void drain();                                  // finish every outstanding submission
   bool fuse_layernorm(size_t batch) const;      // plan variant for this batch size
   void check_status();                          // read the device status words (synchronous)
   void activate() const;
@@ -85,17 +92,28 @@ class Model {
   int device_;
   size_t max_batch_;
   bool failed_ = false;
-  cudaStream_t stream_ = nullptr;
+  cudaStream_t stream_ = nullptr;      // the forward (compute) stream
+  cudaStream_t h2d_stream_ = nullptr;  // serving uploads
+  cudaStream_t d2h_stream_ = nullptr;  // serving downloads
   void *weight_blob_ = nullptr;
   void *act_blob_ = nullptr;
   DeviceWeights w_{};
   __half *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *act_ = nullptr,
          *patches_ = nullptr;
   float *image_ = nullptr, *out_ = nullptr, *pmean_ = nullptr;
+  float *image_slot_[2] = {}, *out_slot_[2] = {};  // slot 0 aliases image_ / out_
+  // Per slot: upload done, forward done (input consumed, output ready), download done.
+  cudaEvent_t ev_in_[2] = {}, ev_done_[2] = {}, ev_out_[2] = {};
+  uint32_t *slot_status_host_ = nullptr;  // pinned [2][2]: each submission's status words
+  uint64_t next_ticket_ = 0;
+  bool submitted_[2] = {};     // the slot holds a submission nobody has waited for yet
+  uint64_t slot_ticket_[2] = {};
+  std::map<uint64_t, std::pair<uint32_t, uint32_t>> finished_;  // completed, not yet waited
+  void retire(int slot);       // complete the slot's submission and keep its status words
   uint32_t *status_ = nullptr;       // device: [0] failure bits, [1] non-finite input
   uint32_t *status_host_ = nullptr;  // pinned mirror
   bool status_pending_ = false;      // work enqueued since the last status check
-  std::map<size_t, Plan> plans_;
+  std::map<std::pair<size_t, int>, Plan> plans_;
 };
 
 }  // namespace dv3

@@ -67,6 +67,7 @@ class DINOv3:
 
     def __init__(self, handle: int):
         self._h = ctypes.c_void_p(handle)
+        self._inflight = {}  # ticket -> buffers kept alive until wait()
 
     # -- construction -------------------------------------------------------------------------
     @classmethod
@@ -141,6 +142,28 @@ class DINOv3:
         _check(_lib.load().dv3_benchmark(self._h, ptr, n, samples, ctypes.byref(t)))
         del keep
         return t
+
+    # -- serving path (asynchronous) ----------------------------------------------------------
+    def submit(self, pixels, out) -> int:
+        """Enqueue upload, forward and download of 1..max_batch images; returns a ticket at once.
+
+        `pixels` and `out` (n*201*384 float32) are host buffers (pinned CPU torch tensors overlap
+        best) that must stay alive and unchanged until wait(ticket) returns; the model keeps a
+        reference to both until then.
+        """
+        ptr, n, keep = _host_floats(pixels)
+        optr = out.data_ptr() if _is_torch(out) else out.ctypes.data
+        onum = out.numel() if _is_torch(out) else out.size
+        t = ctypes.c_uint64()
+        _check(_lib.load().dv3_submit(self._h, ptr, n, optr, onum, ctypes.byref(t)))
+        self._inflight[t.value] = (keep, pixels, out)
+        return t.value
+
+    def wait(self, ticket: int):
+        """Block until submission `ticket` is done; returns its output buffer."""
+        held = self._inflight.pop(ticket, None)
+        _check(_lib.load().dv3_wait(self._h, ticket))
+        return held[2] if held else None
 
     # -- device-resident path -----------------------------------------------------------------
     def forward_device(self, pixels, out=None):

@@ -66,6 +66,8 @@ SIGNATURES = {
     "dv3_run": ([_P, _SZ], _I),
     "dv3_synchronize": ([_P], _I),
     "dv3_forward_device": ([_P, _P, _SZ, _P, _SZ], _I),
+    "dv3_submit": ([_P, _P, _SZ, _P, _SZ, ctypes.POINTER(ctypes.c_uint64)], _I),
+    "dv3_wait": ([_P, ctypes.c_uint64], _I),
     "dv3_launches_per_forward": ([_P, _SZ, ctypes.POINTER(_SZ)], _I),
     "dv3_profile_launches": ([_P, _SZ, _SZ, _P, _P, _SZ, ctypes.POINTER(_SZ)], _I),
     "dv3_pack_f16": ([ctypes.c_char_p, _P, _SZ, _P, ctypes.POINTER(_SZ)], _I),

@@ -127,6 +127,23 @@ int dv3_run(dv3_model *m, size_t batch);
  * check (DV3_INVALID_ARGUMENT for non-finite input; DV3_POISONED for a device fault). */
 int dv3_synchronize(dv3_model *m);
 
+/* Serving path (no reference counterpart; the reference's forward is synchronous). Enqueue the
+ * upload of k = n_floats/DV3_IMAGE_ELEMENTS images (1 <= k <= max_batch) from `pixels`, one
+ * forward and the download of its k*201*384 floats into `out`, and return at once with a ticket.
+ * Submissions alternate between two device buffer slots on three streams, so the upload of one
+ * overlaps the forward of the previous and the download of the one before; a third outstanding
+ * submission first completes the oldest (keeping its status for its own dv3_wait). The caller
+ * keeps `pixels` and `out` valid and unchanged until dv3_wait(ticket) returns; pinned host memory
+ * lets the copies overlap (pageable memory is staged synchronously by the CUDA driver).
+ * Synchronous calls on the model (dv3_forward, dv3_run, ...) first complete every submission. */
+int dv3_submit(dv3_model *m, const float *pixels, size_t n_floats, float *out, size_t out_floats,
+               uint64_t *ticket);
+
+/* Wait for one submission: 0 when its output is in `out`; DV3_INVALID_ARGUMENT for non-finite
+ * input (`out` unspecified) or an unknown / already waited ticket; DV3_POISONED after a device
+ * fault in that submission (the model is then unusable). */
+int dv3_wait(dv3_model *m, uint64_t ticket);
+
 /* dv3_forward on device pointers (same device as the model): copies each chunk into the input
  * buffer, runs it and copies its output out, all on the model's stream, then synchronises. */
 int dv3_forward_device(dv3_model *m, const float *device_pixels, size_t n_floats,

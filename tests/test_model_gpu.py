@@ -226,3 +226,42 @@ def test_fused_layernorm_plan(weights_file, monkeypatch):
     assert [n for n, _ in prof].count("gemm_down_resid_layernorm") == 12
     for i in range(16):
         assert cos(fused[i], split[i]) > 0.99999
+
+
+def test_submit_wait_serving_path(models):
+    """Serving path (dv3_submit / dv3_wait): submissions of changing size, two in flight and a
+    third that first completes the oldest, waited out of order, give exactly the synchronous
+    forward's outputs; a non-finite submission reports its own error and leaves the model and
+    the other submissions usable; a waited ticket cannot be waited again."""
+    import torch
+
+    model = models("stress", max_batch=4)
+    sizes = [3, 1, 4, 2, 4]
+    imgs = [synth.images(100 + i, k) for i, k in enumerate(sizes)]
+    want = [model.forward(x) for x in imgs]
+    ins = [torch.from_numpy(x).pin_memory() for x in imgs]
+    outs = [torch.empty((k, 201, 384), dtype=torch.float32).pin_memory() for k in sizes]
+    t = [model.submit(ins[i], outs[i]) for i in range(3)]
+    model.wait(t[1])
+    model.wait(t[0])
+    model.wait(t[2])
+    t3 = model.submit(ins[3], outs[3])
+    t4 = model.submit(ins[4], outs[4])
+    model.wait(t3)
+    model.wait(t4)
+    for o, w in zip(outs, want):
+        np.testing.assert_array_equal(o.numpy(), w)
+    with pytest.raises(dv.DINOv3Error):
+        model.wait(t4)
+    bad = imgs[0].copy()
+    bad[1, 2, 3, 4] = np.nan
+    bad_out = torch.empty((3, 201, 384), dtype=torch.float32).pin_memory()
+    tb = model.submit(torch.from_numpy(bad).pin_memory(), bad_out)
+    outs[1].zero_()
+    tg = model.submit(ins[1], outs[1])
+    with pytest.raises(dv.DINOv3Error, match="finite"):
+        model.wait(tb)
+    model.wait(tg)
+    np.testing.assert_array_equal(outs[1].numpy(), want[1])
+    # synchronous calls after asynchronous ones
+    np.testing.assert_array_equal(model.forward(imgs[2]), want[2])
