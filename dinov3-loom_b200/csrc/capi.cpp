@@ -198,6 +198,14 @@ int gemm_entry(dv3::GemmOp op, const void *a, uint32_t rows, const void *w,
 
 extern "C" {
 
+int dv3k_bounded_wait_selftest(uint64_t wait_ns, uint32_t *status, void *stream) {
+  if (!status) return bad_args("null status");
+  if (wait_ns == 0 || wait_ns > 1000000000ull) return bad_args("wait_ns must be 1..1e9");
+  return launch_status(dv3::launch_bounded_wait_selftest(wait_ns, status,
+                                                         static_cast<cudaStream_t>(stream)),
+                       "bounded wait self-test");
+}
+
 int dv3k_patchify(const float *images, uint32_t n_images, const float *prefix, uint16_t *patches,
                   uint16_t *x, uint32_t *status, void *stream) {
   if (n_images == 0) return DV3_OK;

@@ -194,6 +194,45 @@ cudaError_t launch_patch_mean(const float *out, uint32_t n_images, float *dst,
   return cudaGetLastError();
 }
 
+// Self-test of the failure path every kernel uses (no reference counterpart): two mbarriers
+// that nothing ever arrives at. Warp 0 waits on the first with a short limit; when it expires it
+// records kErrSelfTestWait and raises the CTA's abort flag, as a kernel role does. Warp 1 waits
+// on the second with a limit a thousand times longer and must leave on the abort flag, recording
+// kErrSelfTestAbort. The kernel then returns normally: no trap, no fault, the context stays
+// usable, and the host reads the status word.
+__global__ void __launch_bounds__(64) bounded_wait_selftest_kernel(uint64_t short_ns,
+                                                                   uint32_t *status) {
+  __shared__ uint64_t bars[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int *abort = &abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    if (warp == 0) {
+      if (!mbar_wait(&bars[0], 0, abort, short_ns)) {
+        report(status, kErrSelfTestWait);
+        *abort = 1;
+      }
+    } else {
+      if (!mbar_wait(&bars[1], 0, abort, short_ns * 1000) && *abort)
+        report(status, kErrSelfTestAbort);
+    }
+  }
+  __syncthreads();
+}
+
+cudaError_t launch_bounded_wait_selftest(uint64_t short_ns, uint32_t *status,
+                                         cudaStream_t stream) {
+  bounded_wait_selftest_kernel<<<1, 64, 0, stream>>>(short_ns, status);
+  return cudaGetLastError();
+}
+
 int sm_count(int device) {
   static int cache[64] = {};
   if (device < 0 || device >= 64) return 148;

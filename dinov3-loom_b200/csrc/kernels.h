@@ -120,6 +120,10 @@ inline uint32_t gateup_source_row(uint32_t packed) {
   return within < 64 ? block * 64 + within : kMlp + block * 64 + (within - 64);
 }
 
+// Failure-path self-test: an mbarrier wait that expires after `short_ns` and a second role that
+// unwinds on the abort flag; reports through status[0] (bits 4 and 5).
+cudaError_t launch_bounded_wait_selftest(uint64_t short_ns, uint32_t *status, cudaStream_t stream);
+
 int sm_count(int device);
 
 // Launch `kernel` with programmatic stream serialization (see pdl_wait in sm100.cuh), so its

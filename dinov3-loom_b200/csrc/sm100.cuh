@@ -20,6 +20,8 @@ constexpr uint32_t kErrProducerWait = 1u << 0;
 constexpr uint32_t kErrMmaWait = 1u << 1;
 constexpr uint32_t kErrEpilogueWait = 1u << 2;
 constexpr uint32_t kErrAttentionWait = 1u << 3;
+constexpr uint32_t kErrSelfTestWait = 1u << 4;   // the bounded-wait self-test's expired wait
+constexpr uint32_t kErrSelfTestAbort = 1u << 5;  // the self-test's second role unwound on abort
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -99,8 +101,9 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed. Returns false if the wait expired
-// or another role raised `abort`.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+// (after `timeout_ns` of %globaltimer time) or another role raised `abort`.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -109,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     for (int i = 0; i < 16; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+    if (globaltimer() - t0 > timeout_ns) return false;
   }
 }
 

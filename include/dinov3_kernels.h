@@ -117,6 +117,13 @@ int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_
  * that packed row `packed_row` (< 3072) of gateup_w holds. Host function. */
 uint32_t dv3k_gateup_source_row(uint32_t packed_row);
 
+/* Self-test of the kernels' failure path (no reference counterpart): one CTA whose first role
+ * waits on an mbarrier that nothing arrives at, with a limit of `wait_ns` nanoseconds, then
+ * records bit 4 in status[0] and raises the CTA's abort flag; a second role waiting (with a
+ * thousand-fold limit) on another such barrier leaves on that flag and records bit 5. The kernel
+ * returns normally, so the context stays usable; every kernel above unwinds the same way. */
+int dv3k_bounded_wait_selftest(uint64_t wait_ns, uint32_t *status, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -273,3 +273,30 @@ def test_matmul_swiglu(b):
                                       ptr(act), ptr(status()), stream()))
     torch.cuda.synchronize()
     assert_close16(act, ref)
+
+
+def test_bounded_wait_expires_and_context_survives():
+    """The failure path every kernel uses, made to run out on the device without a fault: a wait
+    on an mbarrier that nothing arrives at expires after its limit and records its bit, the
+    second role leaves on the abort flag (well before its own, thousand-fold limit) and records
+    its bit, the kernel returns, and the context keeps running kernels."""
+    import time
+
+    st = status()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    check_rc(lib().dv3k_bounded_wait_selftest(20_000_000, ptr(st), stream()))  # 20 ms
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert st.cpu().tolist() == [(1 << 4) | (1 << 5), 0]
+    assert 0.015 < elapsed < 2.0  # the second role's own limit would be 20 s
+    # the context is intact: a regular kernel still runs and its status stays clean
+    rng = np.random.default_rng(3)
+    r = rows_of(1)
+    qkv = f16(rng.standard_normal((r, 1152)))
+    out = torch.empty((r, 384), dtype=torch.float16, device=DEV)
+    st2 = status()
+    check_rc(lib().dv3k_attention(ptr(t16(qkv)), r, ptr(out), ptr(st2), stream()))
+    torch.cuda.synchronize()
+    assert st2.cpu().tolist() == [0, 0]
+    assert_close16(out, attention_ref(qkv, 1))
