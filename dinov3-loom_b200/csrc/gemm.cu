@@ -62,10 +62,36 @@ struct StagingInTiles<Epi, decltype(void(Epi::kStagingInTiles))> {
   static constexpr bool value = Epi::kStagingInTiles;
 };
 
+// Whether the TMA producer loads the epilogue's input blocks into the stage buffers that the last
+// k-blocks free first (EpiResidLN), so that the load overlaps the last MMAs: Epi::kEarlyInput.
+template <class Epi, class = void>
+struct EarlyInput {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct EarlyInput<Epi, decltype(void(Epi::kEarlyInput))> {
+  static constexpr bool value = Epi::kEarlyInput;
+};
+
+// Bytes of one epilogue warp's staging region in the tile buffers: Epi::kWarpStaging when it
+// exists.
+template <class Epi, class = void>
+struct EpiWarpStaging {
+  static constexpr int value = 0;
+};
+template <class Epi>
+struct EpiWarpStaging<Epi, decltype(void(Epi::kWarpStaging))> {
+  static constexpr int value = Epi::kWarpStaging;
+};
+
 template <int BN, class Epi>
 struct GemmCfg {
-  static constexpr int kSplit = BN > 256 ? 2 : 1;    // MMAs (and B boxes) per K step
+  static constexpr int kSplit = BN > 256 ? 2 : 1;    // MMAs per K step
   static constexpr int kMmaN = BN / kSplit;
+  // BN = 256: a unit of work may be a narrow BM x BN/2 tile (TileSched); the weight tile then
+  // arrives as BN/2-row boxes, two per K step for a full tile and one for a narrow one.
+  static constexpr bool kNarrow = BN == 256;
+  static constexpr int kBBox = kNarrow ? BN / 2 : kMmaN;  // rows of one weight box
   static constexpr int kAccBufs = 2 * BN <= 512 ? 2 : 1;
   static constexpr int kA = BM * BK * 2;  // 16 KB
   static constexpr int kB = BN * BK * 2;
@@ -73,6 +99,7 @@ struct GemmCfg {
   static constexpr bool kInTiles = StagingInTiles<Epi>::value;
   static constexpr int kStaging = Epi::kTmaStore && !kInTiles ? kEpilogueWarps * 2 * kStageBlockBytes : 0;
   static constexpr bool kInput = TmaInput<Epi>::value;
+  static constexpr bool kEarly = EarlyInput<Epi>::value;
   static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
   static constexpr int kFixed = 1024 + kStaging + kBarBytes + ((Epi::kSmem + 127) / 128) * 128;
   static constexpr int kFit = (227 * 1024 - kFixed) / kStage;
@@ -82,9 +109,18 @@ struct GemmCfg {
   static constexpr int kBarOffset = kStagingOffset + kStaging;
   static constexpr int kExtraOffset = kBarOffset + kBarBytes;
   static constexpr int kTmemCols = kAccBufs * BN <= 256 ? 256 : 512;
+  // kEarly: epilogue warps whose staging region lies in the first freed stage (the rest go to
+  // the second); each warp's region is Epi::kWarpStaging bytes.
+  static constexpr int kEarlyA =
+      kEarly ? (kStage / EpiWarpStaging<Epi>::value < kEpilogueWarps ? kStage / EpiWarpStaging<Epi>::value
+                                                                     : kEpilogueWarps)
+             : 0;
+  static_assert(!kEarly || (kStages >= 3 && kEarlyA > 0 &&
+                            (kEpilogueWarps - kEarlyA) * EpiWarpStaging<Epi>::value <= kStage),
+                "early epilogue input: two freed stages hold every warp's staging region");
   static constexpr int kSmemBytes = 1024 + kExtraOffset + Epi::kSmem;
   static_assert(kMmaN % 16 == 0 && kMmaN <= 256, "tcgen05.mma N for M=128");
-  static_assert((2 * kStages + 2 * kAccBufs + (kInput ? 2 * kEpilogueWarps : 0)) * 8 + 8 <=
+  static_assert((2 * kStages + 2 * kAccBufs + (kInput ? 2 * kEpilogueWarps : 0)) * 8 + 12 <=
                     kBarBytes,
                 "barrier region");
   static_assert(kStages >= 2 && kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -95,6 +131,42 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
   return GemmCfg<BN, Epi>::kSmemBytes;
 }
 
+// The units of work of one launch, dealt round-robin to the persistent CTAs (unit u to CTA
+// u % grid). Units [0, split_from) are full BM x BN tiles in m-major order with the N tile
+// fastest (full_n of them per M tile, so the CTAs working at one time share A rows through L2);
+// the rest are narrow BM x BN/2 units (BN = 256 only): first the two halves of each full tile
+// from split_from on, then, when N leaves half a tile over (N = full_n*BN + BN/2), the narrow
+// tile of each M tile at column full_n*BN. Narrow units at the end fill a partial last wave
+// with half-length work instead of whole tiles that leave most CTAs idle.
+struct TileSched {
+  int m_tiles;
+  int full_n;      // full-width tiles per M tile
+  int split_from;  // full tiles processed whole
+  int num_units;
+};
+
+template <int BN>
+__device__ __forceinline__ void unit_coords(const TileSched &s, int u, int &m0, int &n0,
+                                            bool &narrow) {
+  if (u < s.split_from) {
+    m0 = (u / s.full_n) * BM;
+    n0 = (u % s.full_n) * BN;
+    narrow = false;
+    return;
+  }
+  narrow = true;
+  const int v = u - s.split_from;
+  const int halves = 2 * (s.m_tiles * s.full_n - s.split_from);
+  if (v < halves) {
+    const int t = s.split_from + v / 2;
+    m0 = (t / s.full_n) * BM;
+    n0 = (t % s.full_n) * BN + (v & 1) * (BN / 2);
+  } else {
+    m0 = (v - halves) * BM;
+    n0 = s.full_n * BN;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
@@ -102,7 +174,7 @@ template <int BN, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
-                int M, int n_tiles_n, int k_blocks, Epi epi, uint32_t *status) {
+                int M, TileSched sched, int k_blocks, Epi epi, uint32_t *status) {
   using C = GemmCfg<BN, Epi>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -116,6 +188,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t *tmem_slot =
       reinterpret_cast<uint32_t *>(in_bars + (C::kInput ? 2 * kEpilogueWarps : 0));
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *in_armed = abort_flag + 1;  // kEarly: epilogue warps whose input the producer armed
   uint8_t *extra = smem + C::kExtraOffset;
 
   const int warp = threadIdx.x / 32;
@@ -133,6 +206,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (C::kInput)
       for (int i = 0; i < 2 * kEpilogueWarps; ++i) mbar_init(&in_bars[i], 1);
     *abort_flag = 0;
+    *in_armed = 0;
     fence_mbar_init();
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
@@ -150,7 +224,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   pdl_wait();  // activations of the previous kernel are complete from here on
   pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_tiles = ((M + BM - 1) / BM) * n_tiles_n;
+  const int num_tiles = sched.num_units;
   if (C::kInTiles && num_tiles > static_cast<int>(gridDim.x)) {  // the host never launches this
     if (threadIdx.x == 0) report(status, kErrEpilogueWait);
     tc_fence_before();
@@ -168,8 +242,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles_n) * BM;
-        const int n0 = (tile % n_tiles_n) * BN;
+        int m0, n0;
+        bool narrow;
+        unit_coords<BN>(sched, tile, m0, n0, narrow);
+        if constexpr (!C::kNarrow) narrow = false;
+        const int b_boxes = narrow ? 1 : BN / C::kBBox;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             report(status, kErrProducerWait);
@@ -178,22 +255,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           uint8_t *a = tiles + stage * C::kStage;
-          mbar_arrive_expect_tx(&full[stage], C::kStage);
+          mbar_arrive_expect_tx(&full[stage], C::kA + b_boxes * C::kBBox * BK * 2);
           tma_load_2d(a, &tmA, &full[stage], kb * BK, m0);
-#pragma unroll
-          for (int s = 0; s < C::kSplit; ++s)
-            tma_load_2d(a + C::kA + s * C::kMmaN * BK * 2, &tmB, &full[stage], kb * BK,
-                        n0 + s * C::kMmaN);
+          for (int s = 0; s < b_boxes; ++s)
+            tma_load_2d(a + C::kA + s * C::kBBox * BK * 2, &tmB, &full[stage], kb * BK,
+                        n0 + s * C::kBBox);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
+          }
+        }
+        if constexpr (C::kEarly) {
+          // The epilogue's x blocks go into the stages of the last-but-two and last-but-one
+          // k-blocks (one tile per CTA) once their MMAs have completed: epilogue warps 0..kEarlyA-1
+          // into the first, the others into the second (the staging pointers of the epilogue).
+          for (int part = 0; ok && part < 2; ++part) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+              report(status, kErrProducerWait);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            uint8_t *base = tiles + stage * C::kStage;
+            const int w0 = part == 0 ? 0 : C::kEarlyA, w1 = part == 0 ? C::kEarlyA : kEpilogueWarps;
+            *in_armed = w1;
+            for (int ew = w0; ew < w1; ++ew) {
+              uint64_t *bar = &in_bars[2 * ew];
+              mbar_arrive_expect_tx(bar, Epi::kWarpStaging);
+              const int row0 = m0 + 32 * ((ew + 2) & 3);  // the warp's TMEM lane quarter
+              const int col0 = n0 + (ew >> 2) * (BN / 2);  // its column half
+              for (int b = 0; b < Epi::kInBlocks; ++b)
+                tma_load_2d(base + (ew - w0) * Epi::kWarpStaging + b * Epi::kBlockBytes, &tmC, bar,
+                            col0 + 64 * b, row0);
+            }
+            if (++stage == C::kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(BM, C::kMmaN, false);
+      constexpr uint32_t idesc_full = idesc_f16_f32(BM, C::kMmaN, false);
+      constexpr uint32_t idesc_narrow = idesc_f16_f32(BM, C::kNarrow ? BN / 2 : C::kMmaN, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -206,6 +312,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
+        int m0_unused, n0_unused;
+        bool narrow;
+        unit_coords<BN>(sched, tile, m0_unused, n0_unused, narrow);
+        const uint32_t idesc = C::kNarrow && narrow ? idesc_narrow : idesc_full;
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
@@ -251,7 +361,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ctx.r = row_in_tile;
     ctx.lane = lane;
     ctx.smem = extra;
-    if constexpr (C::kInTiles) {
+    if constexpr (C::kEarly) {
+      const int ew = warp - 2;  // in the stage of k-block k_blocks-3 or k_blocks-2 (see producer)
+      const int st = (k_blocks + (ew < C::kEarlyA ? 0 : 1)) % C::kStages;
+      ctx.staging = tiles + st * C::kStage + (ew < C::kEarlyA ? ew : ew - C::kEarlyA) * Epi::kWarpStaging;
+    } else if constexpr (C::kInTiles) {
       static_assert(kEpilogueWarps * Epi::kWarpStaging <= C::kTiles, "staging in tile buffers");
       ctx.staging = tiles + (warp - 2) * Epi::kWarpStaging;
     } else
@@ -267,8 +381,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     bool in_pending = false;  // input blocks requested for a tile not yet processed
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = (tile / n_tiles_n) * BM;
-      const int n0 = (tile % n_tiles_n) * BN + half * kCols;
+      int m0, n0;
+      bool narrow;
+      unit_coords<BN>(sched, tile, m0, n0, narrow);
+      if constexpr (!C::kNarrow) narrow = false;
+      // a full tile: this warp's column half; a narrow unit: the epilogue splits it itself
+      const uint32_t col_off = narrow ? 0u : static_cast<uint32_t>(half * kCols);
+      if (!narrow) n0 += half * kCols;
+      ctx.narrow = narrow;
       ctx.row = m0 + row_in_tile;
       ctx.row0 = m0 + q * 32;
       typename Epi::Pre pre = epi.prefetch(n0, ctx);
@@ -282,9 +402,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      if (C::kInTiles) in_pending = true;
-      epi.template run<kCols>(
-          tmem_base + lane_base + static_cast<uint32_t>(acc * BN + half * kCols), n0, ctx, pre);
+      if (C::kInTiles && !C::kEarly) in_pending = true;  // run() requests its input blocks
+      epi.template run<kCols>(tmem_base + lane_base + static_cast<uint32_t>(acc * BN) + col_off,
+                              n0, ctx, pre);
       if (ctx.failed) {
         if (lane == 0) {
           report(status, kErrEpilogueWait);
@@ -305,11 +425,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // Input blocks requested for a tile that was never processed (after an abort) land before
     // shared memory is released.
     if (C::kInput && lane == 0 && in_pending)
-      for (int j = 0; j < 2; ++j) mbar_drain(&ctx.in_bar[j], ctx.iter & 1u);
+      for (int j = 0; j < (C::kInTiles ? 1 : 2); ++j) mbar_drain(&ctx.in_bar[j], ctx.iter & 1u);
   }
 
   tc_fence_before();
   __syncthreads();
+  // Input blocks the producer requested land before shared memory is released (immediate
+  // unless the epilogue unwound without consuming them).
+  if (C::kEarly && threadIdx.x == 0)
+    for (int ew = 0; ew < *in_armed; ++ew) mbar_drain(&in_bars[2 * ew], 0);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
@@ -378,7 +502,9 @@ static uint32_t tma_store_cols(GemmOp op) {
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
                     GemmMaps *maps, std::string *err, const void *ln_out, bool ln_f32) {
   const GemmShape s = gemm_shape(op, rows);
-  const uint32_t b_rows = s.bn > 256 ? s.bn / 2 : s.bn;  // one TMA box per MMA of the K step
+  // weight boxes: one per MMA of the K step (BN = 384: two of 192 rows), or BN/2 rows for the
+  // BN = 256 ops (two per full tile, one per narrow unit)
+  const uint32_t b_rows = s.bn >= 256 ? s.bn / 2 : s.bn;
   if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err) ||
       !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))
     return false;
@@ -388,14 +514,17 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
     maps->c = maps->a;  // unused by this epilogue
     return true;
   }
-  if (!encode_map_f16_swizzled(&maps->c, out, c_cols, rows, 32, 32, 64, err)) return false;
-  if (op == GemmOp::ResidLN384 || op == GemmOp::ResidLN1536) {
+  const bool ln = op == GemmOp::ResidLN384 || op == GemmOp::ResidLN1536;
+  // the LayerNorm epilogue moves 64-column blocks (128-byte rows), the others 32-column blocks
+  if (!encode_map_f16_swizzled(&maps->c, out, c_cols, rows, ln ? 64 : 32, 32, ln ? 128 : 64, err))
+    return false;
+  if (ln) {
     if (ln_out == nullptr) {
       if (err) *err = "the fused LayerNorm needs an output tensor";
       return false;
     }
     return ln_f32 ? encode_map_f32(&maps->d, ln_out, kHidden, rows, 32, 32, err)
-                  : encode_map_f16_swizzled(&maps->d, ln_out, kHidden, rows, 32, 32, 64, err);
+                  : encode_map_f16_swizzled(&maps->d, ln_out, kHidden, rows, 64, 32, 128, err);
   }
   return true;
 }
@@ -404,6 +533,27 @@ template <int BN, class Epi>
 static cudaError_t configure_one() {
   return cudaFuncSetAttribute(gemm_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               gemm_smem_bytes<BN, Epi>());
+}
+
+// The schedule of a launch (TileSched). BN = 256: N = full_n*256 (+ 128 for QKV's last
+// columns, one narrow unit per M tile, last); when a partial last wave of L full tiles would
+// hold at most half the CTAs, those L tiles run as 2L narrow units, so the last wave costs half
+// a tile instead of a whole one.
+template <int BN>
+static TileSched tile_sched(uint32_t rows, int n, int sms) {
+  TileSched t;
+  t.m_tiles = static_cast<int>((rows + BM - 1) / BM);
+  const bool narrow_ok = GemmCfg<BN, EpiSwiGLU>::kNarrow;
+  t.full_n = narrow_ok ? n / BN : (n + BN - 1) / BN;
+  const bool native_half = narrow_ok && n % BN != 0;  // n % BN == BN / 2 (QKV)
+  const int full = t.m_tiles * t.full_n;
+  t.split_from = full;
+  if (narrow_ok && !native_half && full > sms) {
+    const int left = full % sms;
+    if (left > 0 && 2 * left <= sms) t.split_from = full - left;
+  }
+  t.num_units = t.split_from + 2 * (full - t.split_from) + (native_half ? t.m_tiles : 0);
+  return t;
 }
 
 template <int BN, class Epi>
@@ -417,12 +567,11 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const int n_tiles_n = (n + BN - 1) / BN;
-  const int tiles = static_cast<int>((rows + BM - 1) / BM) * n_tiles_n;
-  const int grid = tiles < sm_count(dev) ? tiles : sm_count(dev);
+  const TileSched sched = tile_sched<BN>(rows, n, sm_count(dev));
+  const int grid = sched.num_units < sm_count(dev) ? sched.num_units : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
                     gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,
-                    static_cast<int>(rows), n_tiles_n, k / BK, epi, status);
+                    static_cast<int>(rows), sched, k / BK, epi, status);
 }
 
 // Set the shared-memory limits of every GEMM instance on the current device (done at load, so

@@ -46,6 +46,7 @@ struct EpiCtx {
   uint8_t *smem;       // epilogue's staged vectors
   uint8_t *staging;    // this warp's two staging blocks
   int buf;             // staging block to use next
+  bool narrow;         // BM x BN/2 unit: run() gets the whole unit and takes its part by `half`
   const CUtensorMap *out_map;
   const CUtensorMap *ln_map;  // EpiResidLN: the LayerNorm output
   uint64_t *in_bar;    // kTmaInput epilogues: this warp's two input-block mbarriers
@@ -211,8 +212,10 @@ struct EpiQkvRope {
     const float *sb = reinterpret_cast<const float *>(c.smem + kRopeBytes);
     const float *cy = tab + (p / 14) * kPad, *sy = tab + kTab + (p / 14) * kPad;
     const float *cx = tab + 2 * kTab + (p % 14) * kPad, *sx = tab + 3 * kTab + (p % 14) * kPad;
+    // a narrow unit (128 columns: two heads) gives each column half one head
+    const int h0 = c.narrow ? 64 * c.half : 0, h1 = c.narrow ? h0 + 64 : COLS;
 #pragma unroll 1
-    for (int h = 0; h < COLS; h += 64) {
+    for (int h = h0; h < h1; h += 64) {
       const int col = n0 + h;  // first column of this 64-wide head
       if (col >= kQkv) break;  // warp-uniform
       uint32_t ra[32], rb[32];
@@ -391,18 +394,21 @@ struct EpiSwiGLU {
   __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
     static_assert(COLS % 128 == 0, "a thread owns whole 64 gate + 64 up groups");
     const float *sb = bias;
+    // a narrow unit is one group: each column half takes 32 of its 64 outputs
+    const int g1 = c.narrow ? 128 : COLS;
+    const int s0 = c.narrow ? 32 * c.half : 0, s1 = c.narrow ? s0 + 32 : 64;
 #pragma unroll 1
-    for (int g = 0; g < COLS; g += 128) {
+    for (int g = 0; g < g1; g += 128) {
 #pragma unroll 1
-      for (int half = 0; half < 64; half += 32) {
+      for (int sub = s0; sub < s1; sub += 32) {
         uint32_t rg[32], ru[32];
-        tmem_load32x2(taddr + g + half, rg, taddr + g + 64 + half, ru);
+        tmem_load32x2(taddr + g + sub, rg, taddr + g + 64 + sub, ru);
         float gv[32], uv[32];
-        ldg32(sb + n0 + g + half, gv);
-        ldg32(sb + n0 + g + 64 + half, uv);
+        ldg32(sb + n0 + g + sub, gv);
+        ldg32(sb + n0 + g + 64 + sub, uv);
 #pragma unroll
         for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i] + u2f(rg[i])) * (uv[i] + u2f(ru[i]));
-        tma_emit32(c, gv, (n0 + g) / 2 + half);
+        tma_emit32(c, gv, (n0 + g) / 2 + sub);
       }
     }
   }
@@ -410,16 +416,22 @@ struct EpiSwiGLU {
 
 // ---------------------------------------------------------------------------------------------
 // Residual update fused with the following LayerNorm, on full-row tiles (BN = 384, one tile per
-// CTA, staged in the idle mainloop buffers like EpiResidWide):
+// CTA, staged in mainloop buffers that are idle by then):
 //   x[row] = f16(x + lambda (acc + b))                        (matmul_resid_f16_wmma.loom)
 //   h[row] = f16(LN(x[row]))  or  out[row] = LN(x[row]) f32   (layernorm_rowwave_*.loom)
-// Each warp owns 32 rows x 192 columns (its lane quarter, its column half). Its x blocks come in
-// by TMA, are updated in place in shared memory and leave by TMA; the LayerNorm then reads the
-// stored f16 values back from shared memory, as the separate kernel reads them from memory. The
-// two warps of a row meet in shared memory for the row sum, then for the sum of squared
-// deviations (two-pass centred variance, eps 1e-5, f32). The normalised blocks are staged in the
-// second half of the tile buffers and leave by TMA: six f16 32x32 blocks, or (f32 output) two
-// rounds of three 32x32 f32 blocks.
+// Each warp owns 32 rows x 192 columns (its lane quarter, its column half) and a 12 KB staging
+// region: three 32-row x 64-column f16 blocks in the 128-byte-swizzled layout of the TMA maps
+// (row r at r*128 bytes, its 16-byte chunk k at chunk k ^ (r & 7)). The TMA producer loads the
+// x blocks into these regions as soon as the mainloop has finished with the stage buffers that
+// hold them (kEarlyInput: the stages of the last-but-two and last-but-one k-blocks), so the load
+// overlaps the last MMAs. The updated blocks are written in place and leave by TMA one 64-column
+// block at a time; the stored f16 values also go back into TMEM over the accumulator columns
+// already consumed (16 packed columns per 32), which is where the LayerNorm reads them, as the
+// separate kernel reads x from memory. Statistics: each warp takes the mean and the centred sum
+// of squares of its 192 values, and the two warps of a row merge them through shared memory
+// (Chan et al.: M2 = M2a + M2b + d^2 n_a n_b / n), eps 1e-5, f32. The normalised blocks reuse
+// the staging region once the x stores have read it: three f16 blocks, or (f32 output) two
+// rounds of three 32-row x 32-column f32 blocks.
 // ---------------------------------------------------------------------------------------------
 struct EpiResidLN {
   const float *bias;
@@ -428,13 +440,16 @@ struct EpiResidLN {
   const float *beta;
   bool f32_out;
   static constexpr int kVecs = 4 * kHidden;  // bias, lambda, gamma, beta
-  static constexpr int kSmem = kVecs * 4 + 4 * 128 * 4;  // + [2 halves][128 rows] sum, squares
+  static constexpr int kSmem = kVecs * 4 + 4 * 128 * 4;  // + [mean|M2][2 halves][128 rows]
   static constexpr bool kTmaStore = true;
   static constexpr bool kTmaInput = true;
   static constexpr bool kStagingInTiles = true;
-  static constexpr int kBlocks = 6;  // 32-column blocks per warp (192 columns)
-  static constexpr int kWarpStaging = kBlocks * kStageBlockBytes;
-  static constexpr int kF32Block = 32 * 128;  // 32 rows x 32 f32 columns
+  static constexpr bool kEarlyInput = true;
+  static constexpr int kBlockBytes = 32 * 128;              // 32 rows x 64 f16 columns
+  static constexpr int kInBlocks = 3;                       // per warp (192 columns)
+  static constexpr int kWarpStaging = kInBlocks * kBlockBytes;
+  static constexpr int kSub = 6;                            // 32-column accumulator chunks
+  static constexpr int kF32Block = 32 * 128;                // 32 rows x 32 f32 columns
   using Pre = NoPre;
   __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
@@ -444,112 +459,156 @@ struct EpiResidLN {
     stage_floats(s + 2 * kHidden, gamma, kHidden, tid, n);
     stage_floats(s + 3 * kHidden, beta, kHidden, tid, n);
   }
-  // Row lane of a 32x32 f16 block (64-byte swizzle): its four 16-byte chunks.
-  __device__ static void load_row(const uint8_t *rowp, int sw, float (&v)[32]) {
-    uint4 q[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) q[k] = *reinterpret_cast<const uint4 *>(rowp + ((k ^ sw) << 4));
-    unpack_half32(q, v);
+  // Eight consecutive floats of a staged vector (a shared-memory broadcast).
+  __device__ static void lds8(const float *p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0];
+    const float4 b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
   template <int COLS>
   __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
-    static_assert(COLS == 32 * kBlocks, "six 32-column blocks per warp");
-    if (c.lane == 0) {
-      mbar_arrive_expect_tx(&c.in_bar[0], kBlocks * kStageBlockBytes);
-#pragma unroll
-      for (int j = 0; j < kBlocks; ++j)
-        tma_load_2d(c.staging + j * kStageBlockBytes, c.out_map, &c.in_bar[0], n0 + 32 * j, c.row0);
-    }
+    static_assert(COLS == 32 * kSub, "six 32-column accumulator chunks per warp");
     const float *sv = reinterpret_cast<const float *>(c.smem);
-    float *red = const_cast<float *>(sv) + kVecs;  // [0..255] sums, [256..511] squares
-    const int sw = (c.lane >> 1) & 3;
+    float *red = const_cast<float *>(sv) + kVecs;  // [0..255] means, [256..511] M2
+    const int sw = c.lane & 7;
+    uint8_t *const stage = c.staging;
     if (!__all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag))) {
       c.failed = true;
       return;
     }
-    // x = f16(x + lambda (acc + b)), in place, out by TMA; sum of the stored values
-    float sum = 0.f;
-#pragma unroll 1
-    for (int j = 0; j < kBlocks; ++j) {
-      uint32_t r[32];
-      tmem_load32(taddr + 32 * j, r);
-      uint8_t *rowp = c.staging + j * kStageBlockBytes + c.lane * 64;
-      float v[32], b[32], l[32];
-      load_row(rowp, sw, v);
-      lds32(sv + n0 + 32 * j, b);
-      lds32(sv + kHidden + n0 + 32 * j, l);
+    // x = f16(x + lambda (acc + b)) in place; back into TMEM as packed f16; out by TMA
+    float2 s2 = make_float2(0.f, 0.f);
+    uint32_t ra[32], rb[32];
+    tmem_ld32(taddr, ra);
+    tmem_wait_ld(ra);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += l[i] * (u2f(r[i]) + b[i]);
+    for (int j = 0; j < kSub; ++j) {
+      uint32_t(&r)[32] = (j & 1) ? rb : ra;
+      uint32_t(&rn)[32] = (j & 1) ? ra : rb;
+      if (j + 1 < kSub) tmem_ld32(taddr + 32 * (j + 1), rn);
+      uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
+      uint32_t o[16];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint4 p = pack8(v, k);
-        *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) = p;
-        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+        uint4 *qp = reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4));
+        const uint4 q = *qp;
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        float bb[8], ll[8];
+        lds8(sv + n0 + 32 * j + 8 * k, bb);
+        lds8(sv + kHidden + n0 + 32 * j + 8 * k, ll);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_half2(w[e]);
-          sum += f.x + f.y;
+        for (int p = 0; p < 4; ++p) {
+          const float2 a = make_float2(u2f(r[8 * k + 2 * p]), u2f(r[8 * k + 2 * p + 1]));
+          const float2 t = __fadd2_rn(a, make_float2(bb[2 * p], bb[2 * p + 1]));
+          const float2 v = __ffma2_rn(make_float2(ll[2 * p], ll[2 * p + 1]), t, unpack_half2(w[p]));
+          o[4 * k + p] = pack_half2(v.x, v.y);
+          s2 = __fadd2_rn(s2, unpack_half2(o[4 * k + p]));
         }
+        *qp = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (c.lane == 0) {
-        tma_store_2d(c.out_map, c.staging + j * kStageBlockBytes, n0 + 32 * j, c.row0);
-        bulk_commit();
-      }
-    }
-    red[c.half * 128 + c.r] = sum;
-    named_barrier(1, kEpilogueThreads);
-    const float mean = (red[c.r] + red[128 + c.r]) * (1.0f / kHidden);
-    float sq = 0.f;
-#pragma unroll 1
-    for (int j = 0; j < kBlocks; ++j) {
-      float v[32];
-      load_row(c.staging + j * kStageBlockBytes + c.lane * 64, sw, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) sq += (v[i] - mean) * (v[i] - mean);
-    }
-    red[256 + c.half * 128 + c.r] = sq;
-    named_barrier(1, kEpilogueThreads);
-    const float rstd = rsqrtf((red[256 + c.r] + red[384 + c.r]) * (1.0f / kHidden) + 1e-5f);
-    uint8_t *out_stage = c.staging + kEpilogueWarps * kWarpStaging;  // second half of the buffers
-#pragma unroll 1
-    for (int j = 0; j < kBlocks; ++j) {
-      float v[32], g[32], bt[32];
-      load_row(c.staging + j * kStageBlockBytes + c.lane * 64, sw, v);
-      lds32(sv + 2 * kHidden + n0 + 32 * j, g);
-      lds32(sv + 3 * kHidden + n0 + 32 * j, bt);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * rstd * g[i] + bt[i];
-      if (!f32_out) {
-        uint8_t *rowp = out_stage + j * kStageBlockBytes + c.lane * 64;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) = pack8(v, k);
+      tmem_st16(taddr + 32 * j, o);
+      if (j + 1 < kSub) tmem_wait_ld(rn);
+      if (j & 1) {  // a 64-column block is complete
         fence_proxy_async_smem();
         __syncwarp();
         if (c.lane == 0) {
-          tma_store_2d(c.ln_map, out_stage + j * kStageBlockBytes, n0 + 32 * j, c.row0);
+          tma_store_2d(c.out_map, stage + (j >> 1) * kBlockBytes, n0 + 64 * (j >> 1), c.row0);
           bulk_commit();
         }
+      }
+    }
+    tmem_st_wait();
+    // this warp's mean and centred sum of squares, merged with the other half of the row
+    const float mh = (s2.x + s2.y) * (1.0f / (kHidden / 2));
+    const float2 nmh = make_float2(-mh, -mh);
+    float2 q2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kSub; j += 2) {
+      uint32_t x0[16], x1[16];
+      tmem_ld16(taddr + 32 * j, x0);
+      tmem_ld16(taddr + 32 * (j + 1), x1);
+      tmem_ld_wait();
+      tmem_regs_ready16(x0);
+      tmem_regs_ready16(x1);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 d0 = __fadd2_rn(unpack_half2(x0[i]), nmh);
+        q2 = __ffma2_rn(d0, d0, q2);
+        const float2 d1 = __fadd2_rn(unpack_half2(x1[i]), nmh);
+        q2 = __ffma2_rn(d1, d1, q2);
+      }
+    }
+    red[c.half * 128 + c.r] = mh;
+    red[256 + c.half * 128 + c.r] = q2.x + q2.y;
+    named_barrier(1, kEpilogueThreads);
+    const float m0 = red[c.r], m1 = red[128 + c.r];
+    const float mean = 0.5f * (m0 + m1), d = m1 - m0;
+    const float m2 = red[256 + c.r] + red[384 + c.r] + d * d * (kHidden / 4);
+    const float rstd = rsqrtf(m2 * (1.0f / kHidden) + 1e-5f);
+    // h = (x - mean) rstd gamma + beta, staged where the x blocks were
+    if (c.lane == 0) bulk_wait_read<0>();  // the x stores have read the staging region
+    __syncwarp();
+    const float2 nm = make_float2(-mean, -mean), rs = make_float2(rstd, rstd);
+    uint32_t xa[16], xb[16];
+    tmem_ld16(taddr, xa);
+    tmem_ld_wait();
+    tmem_regs_ready16(xa);
+#pragma unroll
+    for (int j = 0; j < kSub; ++j) {
+      uint32_t(&xr)[16] = (j & 1) ? xb : xa;
+      uint32_t(&xn)[16] = (j & 1) ? xa : xb;
+      if (j + 1 < kSub) tmem_ld16(taddr + 32 * (j + 1), xn);
+      float y[32];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float gg[8], tt[8];
+        lds8(sv + 2 * kHidden + n0 + 32 * j + 8 * k, gg);
+        lds8(sv + 3 * kHidden + n0 + 32 * j + 8 * k, tt);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 z = __fmul2_rn(__fadd2_rn(unpack_half2(xr[4 * k + p]), nm), rs);
+          const float2 v = __ffma2_rn(z, make_float2(gg[2 * p], gg[2 * p + 1]),
+                                      make_float2(tt[2 * p], tt[2 * p + 1]));
+          y[8 * k + 2 * p] = v.x;
+          y[8 * k + 2 * p + 1] = v.y;
+        }
+      }
+      if (!f32_out) {
+        uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) = pack8(y, k);
+        if (j & 1) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (c.lane == 0) {
+            tma_store_2d(c.ln_map, stage + (j >> 1) * kBlockBytes, n0 + 64 * (j >> 1), c.row0);
+            bulk_commit();
+          }
+        }
       } else {
-        // f32: 128-byte rows, 128-byte swizzle; three blocks fit the warp's space at a time
-        const int slot = j % 3;
+        // f32: 32 columns (128-byte rows, 128-byte swizzle) per block, three blocks at a time
         if (j == 3) {
           if (c.lane == 0) bulk_wait_read<0>();  // the first round's stores have read their blocks
           __syncwarp();
         }
-        uint8_t *blk = out_stage + slot * kF32Block;
+        uint8_t *blk = stage + (j % 3) * kF32Block;
         uint8_t *rowp = blk + c.lane * 128;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<float4 *>(rowp + ((k ^ (c.lane & 7)) << 4)) =
-              make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          *reinterpret_cast<float4 *>(rowp + ((k ^ sw) << 4)) =
+              make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (c.lane == 0) {
           tma_store_2d(c.ln_map, blk, n0 + 32 * j, c.row0);
           bulk_commit();
         }
+      }
+      if (j + 1 < kSub) {
+        tmem_ld_wait();
+        tmem_regs_ready16(xn);
       }
     }
   }
