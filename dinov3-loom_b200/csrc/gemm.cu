@@ -73,6 +73,16 @@ struct EarlyInput<Epi, decltype(void(Epi::kEarlyInput))> {
   static constexpr bool value = Epi::kEarlyInput;
 };
 
+// TMA-store staging blocks per epilogue warp: Epi::kStagingBufs when it exists, else 2.
+template <class Epi, class = void>
+struct StagingBufs {
+  static constexpr int value = 2;
+};
+template <class Epi>
+struct StagingBufs<Epi, decltype(void(Epi::kStagingBufs))> {
+  static constexpr int value = Epi::kStagingBufs;
+};
+
 // Bytes of one epilogue warp's staging region in the tile buffers: Epi::kWarpStaging when it
 // exists.
 template <class Epi, class = void>
@@ -97,7 +107,8 @@ struct GemmCfg {
   static constexpr int kB = BN * BK * 2;
   static constexpr int kStage = kA + kB;
   static constexpr bool kInTiles = StagingInTiles<Epi>::value;
-  static constexpr int kStaging = Epi::kTmaStore && !kInTiles ? kEpilogueWarps * 2 * kStageBlockBytes : 0;
+  static constexpr int kStaging =
+      Epi::kTmaStore && !kInTiles ? kEpilogueWarps * StagingBufs<Epi>::value * kStageBlockBytes : 0;
   static constexpr bool kInput = TmaInput<Epi>::value;
   static constexpr bool kEarly = EarlyInput<Epi>::value;
   static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
@@ -369,8 +380,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       static_assert(kEpilogueWarps * Epi::kWarpStaging <= C::kTiles, "staging in tile buffers");
       ctx.staging = tiles + (warp - 2) * Epi::kWarpStaging;
     } else
-      ctx.staging = smem + C::kStagingOffset + (warp - 2) * 2 * kStageBlockBytes;
+      ctx.staging = smem + C::kStagingOffset + (warp - 2) * StagingBufs<Epi>::value * kStageBlockBytes;
     ctx.buf = 0;
+    ctx.nbuf = StagingBufs<Epi>::value;
     ctx.out_map = &tmC;
     ctx.ln_map = &tmD;
     ctx.in_bar = in_bars + 2 * (warp - 2);

@@ -46,6 +46,7 @@ struct EpiCtx {
   uint8_t *smem;       // epilogue's staged vectors
   uint8_t *staging;    // this warp's two staging blocks
   int buf;             // staging block to use next
+  int nbuf;            // staging blocks per warp (2: double-buffered; 1: Epi::kStagingBufs)
   bool narrow;         // BM x BN/2 unit: run() gets the whole unit and takes its part by `half`
   const CUtensorMap *out_map;
   const CUtensorMap *ln_map;  // EpiResidLN: the LayerNorm output
@@ -125,7 +126,10 @@ __device__ __forceinline__ void store_half32(__half *dst, const float (&v)[32]) 
 // through a staging block and a TMA store.
 __device__ __forceinline__ void tma_emit32(EpiCtx &c, const float (&v)[32], int col) {
   uint8_t *blk = c.staging + c.buf * kStageBlockBytes;
-  if (c.lane == 0) bulk_wait_read<1>();  // the store that last used this block has read it
+  if (c.lane == 0) {  // the store that last used this block has read it
+    if (c.nbuf == 2) bulk_wait_read<1>();
+    else bulk_wait_read<0>();
+  }
   __syncwarp();
   uint8_t *rowp = blk + c.lane * 64;
   const int sw = (c.lane >> 1) & 3;
@@ -137,7 +141,7 @@ __device__ __forceinline__ void tma_emit32(EpiCtx &c, const float (&v)[32], int 
     tma_store_2d(c.out_map, blk, col, c.row0);
     bulk_commit();
   }
-  c.buf ^= 1;
+  c.buf = c.nbuf == 2 ? c.buf ^ 1 : 0;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -190,6 +194,9 @@ struct EpiQkvRope {
   static constexpr int kRopeBytes = ((4 * kTab * 4 + 15) / 16) * 16;
   static constexpr int kSmem = kRopeBytes + kQkv * 4;       // + bias
   static constexpr bool kTmaStore = true;
+  // One staging block per warp: the 16 KB saved let a fourth 48 KB mainloop stage fit beside
+  // the RoPE tables and the bias (the epilogue has slack to wait for each store's read).
+  static constexpr int kStagingBufs = 1;
   using Pre = NoPre;
   __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
