@@ -9,8 +9,12 @@ barrier and the max-over-ranks of the timings).
   value   images/s over all ranks with the inputs already resident in HBM: K steps timed with CUDA
           events on the model's stream, the L2 flushed (256 MiB memset) between timed steps,
           value = N * 64 * K / max over ranks of the summed step time.
-  e2e     the same through the public API with host buffers: dv3_forward on a pinned host input,
-          writing a pinned host output, host<->device copies inside the timed region.
+  e2e     the same through the public API with host buffers, host<->device copies of every step
+          inside the timed region: the serving calls dv3_submit / dv3_wait with two steps in
+          flight (pinned host input and output per step; the library overlaps one step's upload
+          and another's download with the forward in between), host clock between device
+          synchronisations, max over ranks. `e2e_sync` beside it: one blocking dv3_forward per
+          step (upload, forward and download in series), CUDA events on the model's stream.
   roofline the dominant kernel (gate/up GEMM + SwiGLU, 46.5 % of the FLOPs): its algorithmic FLOPs
           per launch / its average launch time (CUDA event nodes between the launches of a graph
           replay of the forward on the model's stream, `--profile-iters` replays), against the
@@ -330,9 +334,41 @@ def run_ours(args):
         e.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev2))
-    e2e_value = world * BATCH * e2e_steps / (e2e_ms / 1000.0)
+    e2e_sync_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev2))
+    e2e_sync = world * BATCH * e2e_steps / (e2e_sync_ms / 1000.0)
     assert np.isfinite(pin_out.numpy()).all()
+
+    # ---- end to end, pipelined through the serving API (dv3_submit / dv3_wait) ----
+    # Two submissions in flight, each with its own pinned input and output: the upload of step
+    # i overlaps the forward of step i-1 and the download of step i-2 (three streams inside the
+    # library). Every step's host->device copy and device->host read are inside the timed
+    # region; the L2 is flushed on the compute stream before each step's forward (the flush
+    # time is included). Timed by the host clock between two device synchronisations, max over
+    # ranks.
+    pins_in = [pin_in, torch.from_numpy(images).pin_memory()]
+    pins_out = [pin_out, torch.empty((BATCH, 201, 384), dtype=torch.float32).pin_memory()]
+
+    def run_pipelined(steps: int) -> None:
+        tickets = []
+        for i in range(steps):
+            if len(tickets) == 2:
+                model.wait(tickets.pop(0))
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            tickets.append(model.submit(pins_in[i % 2], pins_out[i % 2]))
+        for t in tickets:
+            model.wait(t)
+
+    run_pipelined(4)
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    run_pipelined(e2e_steps)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0)
+    barrier()
+    e2e_value = world * BATCH * e2e_steps / (e2e_ms / 1000.0)
+    assert all(np.isfinite(o.numpy()).all() for o in pins_out)
 
     # ---- batch-1 latency (p50), device-resident and end to end ----
     lat_dev, lat_e2e = [], []
@@ -392,7 +428,13 @@ def run_ours(args):
                        "l2": "flushed between timed steps (256 MiB memset)"},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": BATCH * 3 * 224 * 224 * 4,
-                    "d2h_bytes_per_step": BATCH * 201 * 384 * 4 + 8},
+                    "d2h_bytes_per_step": BATCH * 201 * 384 * 4 + 8,
+                    "api": "dv3_submit/dv3_wait, two steps in flight (copies overlap the "
+                           "neighbouring steps' forwards), host clock, L2 flushed per step",
+                    "steps": e2e_steps},
+            "e2e_sync": {"value": e2e_sync, "unit": UNIT,
+                         "api": "dv3_forward, one blocking call per step (upload, forward, "
+                                "download in series), CUDA events on the model's stream"},
             "gpu_launches": steps_launches,
             "roofline": {"kernel": "gemm_gateup_swiglu", "bound": "tensor", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
