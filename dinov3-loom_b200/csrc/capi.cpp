@@ -266,6 +266,50 @@ int dv3k_attention(const uint16_t *qkv, uint32_t rows, uint16_t *out, uint32_t *
                        "attention");
 }
 
+int dv3k_matmul_splitk(const uint16_t *a, uint32_t rows, const uint16_t *w, uint32_t splits,
+                       float *partials, uint32_t *status, void *stream) {
+  if (!all_aligned(a, w, partials)) return bad_args("pointers must be 16-byte aligned");
+  if (splits == 0 || (dv3::kMlp / 64) % splits != 0)
+    return bad_args("splits must divide 24 (the 64-wide k-blocks of 1536)");
+  if (rows == 0) return DV3_OK;
+  dv3::GemmMaps maps;
+  std::string err;
+  if (!dv3::make_gemm_maps(dv3::GemmOp::SplitK1536, a, rows, w, partials, &maps, &err, nullptr,
+                           false, splits))
+    return bad_args(err.c_str());
+  dv3::GemmArgs g;
+  g.partials = partials;
+  g.splits = splits;
+  return launch_status(dv3::launch_gemm(dv3::GemmOp::SplitK1536, maps, rows, g, status,
+                                        static_cast<cudaStream_t>(stream)),
+                       dv3::gemm_name(dv3::GemmOp::SplitK1536));
+}
+
+int dv3k_splitk_reduce(const float *partials, uint32_t rows, uint32_t splits, const float *bias,
+                       const float *lambda, uint16_t *x, void *stream) {
+  if (!all_aligned(partials, bias, lambda, x)) return bad_args("pointers must be 16-byte aligned");
+  if (splits == 0 || splits > 24) return bad_args("splits must be 1..24");
+  return launch_status(dv3::launch_splitk_reduce(partials, rows, splits, bias, lambda,
+                                                 reinterpret_cast<__half *>(x), nullptr, nullptr,
+                                                 nullptr, nullptr, static_cast<cudaStream_t>(stream)),
+                       "splitk_reduce");
+}
+
+int dv3k_splitk_reduce_layernorm(const float *partials, uint32_t rows, uint32_t splits,
+                                 const float *bias, const float *lambda, uint16_t *x,
+                                 const float *gamma, const float *beta, uint16_t *h,
+                                 float *out_f32, void *stream) {
+  if (!all_aligned(partials, bias, lambda, x, gamma, beta, h, out_f32))
+    return bad_args("pointers must be 16-byte aligned");
+  if (splits == 0 || splits > 24) return bad_args("splits must be 1..24");
+  if ((h == nullptr) == (out_f32 == nullptr)) return bad_args("exactly one of h and out_f32");
+  return launch_status(dv3::launch_splitk_reduce(partials, rows, splits, bias, lambda,
+                                                 reinterpret_cast<__half *>(x), gamma, beta,
+                                                 reinterpret_cast<__half *>(h), out_f32,
+                                                 static_cast<cudaStream_t>(stream)),
+                       "splitk_reduce_layernorm");
+}
+
 int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
                       const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
                       void *stream) {

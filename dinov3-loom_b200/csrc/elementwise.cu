@@ -171,6 +171,121 @@ cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *ga
                     static_cast<int>(rows), gamma, beta, static_cast<void *>(out));
 }
 
+// Split-K completion (kernels/splitk_reduce_f16.loom): one warp per row, lane columns
+// 8*lane..8*lane+7 and 256+4*lane..+3 (coalesced f32 and f16 loads). The slabs are added in order
+// s = 0..splits-1 onto zero, then the bias, times lambda, onto the f16 residual, each step rounded
+// as the reference does it (no fused multiply-add). kLn: the LayerNorm of the stored f16 row
+// follows in registers, as layernorm_kernel computes it (two-pass centred variance, eps 1e-5),
+// into h (f16) or out (f32).
+template <int kLn>  // 0: reduce only, 1: + LayerNorm to f16 h, 2: + LayerNorm to f32 out
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float *__restrict__ partials, int rows, int splits,
+                         const float *__restrict__ bias, const float *__restrict__ lambda,
+                         __half *__restrict__ x, const float *__restrict__ gamma,
+                         const float *__restrict__ beta, void *__restrict__ out) {
+  pdl_wait();  // the partial slabs of the previous kernel are complete from here on
+  pdl_trigger();
+  const int row = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;  // whole warp leaves together
+  const int c0 = lane * 8, c1 = 256 + lane * 4;
+  auto load12 = [&](const float *base, float (&v)[12]) {
+    const float4 a0 = __ldg(reinterpret_cast<const float4 *>(base + c0));
+    const float4 a1 = __ldg(reinterpret_cast<const float4 *>(base + c0) + 1);
+    const float4 a2 = __ldg(reinterpret_cast<const float4 *>(base + c1));
+    const float t[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
+#pragma unroll
+    for (int e = 0; e < 12; ++e) v[e] = t[e];
+  };
+  float acc[12];
+#pragma unroll
+  for (int e = 0; e < 12; ++e) acc[e] = 0.f;
+  const size_t slab = static_cast<size_t>(rows) * kHidden;
+  const float *prow = partials + static_cast<size_t>(row) * kHidden;
+  // up to eight slabs' loads in flight at once, then added in slab order
+  for (int s0 = 0; s0 < splits; s0 += 8) {
+    float p[8][12];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < splits) load12(prow + (s0 + k) * slab, p[k]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < splits) {
+#pragma unroll
+        for (int e = 0; e < 12; ++e) acc[e] = __fadd_rn(acc[e], p[k][e]);
+      }
+  }
+  float b[12], l[12];
+  load12(bias, b);
+  load12(lambda, l);
+  __half *xr = x + static_cast<size_t>(row) * kHidden;
+  const uint4 xa = *reinterpret_cast<const uint4 *>(xr + c0);
+  const uint2 xb = *reinterpret_cast<const uint2 *>(xr + c1);
+  const uint32_t w[6] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y};
+  float v[12];
+  uint32_t o[6];
+#pragma unroll
+  for (int e = 0; e < 6; ++e) {
+    const float2 prior = unpack_half2(w[e]);
+    const float u0 = __fadd_rn(prior.x, __fmul_rn(__fadd_rn(acc[2 * e], b[2 * e]), l[2 * e]));
+    const float u1 =
+        __fadd_rn(prior.y, __fmul_rn(__fadd_rn(acc[2 * e + 1], b[2 * e + 1]), l[2 * e + 1]));
+    o[e] = pack_half2(u0, u1);
+    const float2 r = unpack_half2(o[e]);  // the LayerNorm reads the stored f16 values
+    v[2 * e] = r.x;
+    v[2 * e + 1] = r.y;
+  }
+  *reinterpret_cast<uint4 *>(xr + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint2 *>(xr + c1) = make_uint2(o[4], o[5]);
+  if constexpr (kLn != 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 12; ++e) s += v[e];
+    const float mean = warp_sum(s) * (1.0f / kHidden);
+    float d = 0.f;
+#pragma unroll
+    for (int e = 0; e < 12; ++e) {
+      v[e] -= mean;
+      d += v[e] * v[e];
+    }
+    const float rstd = rsqrtf(warp_sum(d) * (1.0f / kHidden) + 1e-5f);
+    float g[12], bt[12], y[12];
+    load12(gamma, g);
+    load12(beta, bt);
+#pragma unroll
+    for (int e = 0; e < 12; ++e) y[e] = v[e] * rstd * g[e] + bt[e];
+    if constexpr (kLn == 2) {
+      float *orow = static_cast<float *>(out) + static_cast<size_t>(row) * kHidden;
+      reinterpret_cast<float4 *>(orow + c0)[0] = make_float4(y[0], y[1], y[2], y[3]);
+      reinterpret_cast<float4 *>(orow + c0)[1] = make_float4(y[4], y[5], y[6], y[7]);
+      *reinterpret_cast<float4 *>(orow + c1) = make_float4(y[8], y[9], y[10], y[11]);
+    } else {
+      __half *hrow = static_cast<__half *>(out) + static_cast<size_t>(row) * kHidden;
+      *reinterpret_cast<uint4 *>(hrow + c0) =
+          make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]), pack_half2(y[4], y[5]),
+                     pack_half2(y[6], y[7]));
+      *reinterpret_cast<uint2 *>(hrow + c1) = make_uint2(pack_half2(y[8], y[9]), pack_half2(y[10], y[11]));
+    }
+  }
+}
+
+cudaError_t launch_splitk_reduce(const float *partials, uint32_t rows, uint32_t splits,
+                                 const float *bias, const float *lambda, __half *x,
+                                 const float *gamma, const float *beta, __half *h, float *out_f32,
+                                 cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  const dim3 grid((rows + 7) / 8), block(256);
+  const int r = static_cast<int>(rows), sp = static_cast<int>(splits);
+  if (gamma == nullptr)
+    return launch_pdl(splitk_reduce_kernel<0>, grid, block, 0, stream, partials, r, sp, bias,
+                      lambda, x, gamma, beta, static_cast<void *>(nullptr));
+  if (out_f32 != nullptr)
+    return launch_pdl(splitk_reduce_kernel<2>, grid, block, 0, stream, partials, r, sp, bias,
+                      lambda, x, gamma, beta, static_cast<void *>(out_f32));
+  return launch_pdl(splitk_reduce_kernel<1>, grid, block, 0, stream, partials, r, sp, bias, lambda,
+                    x, gamma, beta, static_cast<void *>(h));
+}
+
 // patch_mean (src/lib.rs:134-148) on the device: one thread per (image, channel) adds
 // row / 196 over the patch rows 5..200 in order, in f32 with correctly rounded division, so the
 // result equals the reference's host loop bit for bit. Reads are coalesced across channels.

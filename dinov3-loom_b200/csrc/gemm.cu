@@ -6,6 +6,7 @@
 //   Resid*    x = f16(x + lambda (A W^T + b))              kernels/matmul_resid_f16_wmma.loom
 //   ResidLN*  the same on full rows, then LayerNorm        + kernels/layernorm_rowwave_*.loom
 //   SwiGLU    act = f16(silu(A Wg^T + bg) (A Wu^T + bu))   kernels/matmul_swiglu_f16_wmma.loom
+//   SplitK    partials[s] = A[:, K_s] W[:, K_s]^T (f32)     kernels/matmul_splitk_f16_wmma.loom
 //
 // Layout: A [M][K] f16 activations and W [N][K] f16 weights, both K-major, are streamed by TMA
 // in 128-row x 64-column boxes with the 128-byte swizzle into a ring of shared-memory stages.
@@ -154,11 +155,18 @@ struct TileSched {
   int full_n;      // full-width tiles per M tile
   int split_from;  // full tiles processed whole
   int num_units;
+  int k_splits;    // split-K: the full tiles repeat for each K slice (slice-major); else 1
 };
 
 template <int BN>
 __device__ __forceinline__ void unit_coords(const TileSched &s, int u, int &m0, int &n0,
-                                            bool &narrow) {
+                                            bool &narrow, int &k_slice) {
+  k_slice = 0;
+  if (s.k_splits > 1) {  // split-K launches have full tiles only
+    const int per = s.m_tiles * s.full_n;
+    k_slice = u / per;
+    u -= k_slice * per;
+  }
   if (u < s.split_from) {
     m0 = (u / s.full_n) * BM;
     n0 = (u % s.full_n) * BN;
@@ -253,11 +261,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        int m0, n0;
+        int m0, n0, k_slice;
         bool narrow;
-        unit_coords<BN>(sched, tile, m0, n0, narrow);
+        unit_coords<BN>(sched, tile, m0, n0, narrow, k_slice);
         if constexpr (!C::kNarrow) narrow = false;
         const int b_boxes = narrow ? 1 : BN / C::kBBox;
+        const int kb0 = k_slice * k_blocks;  // split-K: this unit's slice of the k-blocks
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             report(status, kErrProducerWait);
@@ -267,9 +276,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint8_t *a = tiles + stage * C::kStage;
           mbar_arrive_expect_tx(&full[stage], C::kA + b_boxes * C::kBBox * BK * 2);
-          tma_load_2d(a, &tmA, &full[stage], kb * BK, m0);
+          tma_load_2d(a, &tmA, &full[stage], (kb0 + kb) * BK, m0);
           for (int s = 0; s < b_boxes; ++s)
-            tma_load_2d(a + C::kA + s * C::kBBox * BK * 2, &tmB, &full[stage], kb * BK,
+            tma_load_2d(a + C::kA + s * C::kBBox * BK * 2, &tmB, &full[stage], (kb0 + kb) * BK,
                         n0 + s * C::kBBox);
           if (++stage == C::kStages) {
             stage = 0;
@@ -323,9 +332,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
-        int m0_unused, n0_unused;
+        int m0_unused, n0_unused, k_slice_unused;
         bool narrow;
-        unit_coords<BN>(sched, tile, m0_unused, n0_unused, narrow);
+        unit_coords<BN>(sched, tile, m0_unused, n0_unused, narrow, k_slice_unused);
         const uint32_t idesc = C::kNarrow && narrow ? idesc_narrow : idesc_full;
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
@@ -393,10 +402,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     bool in_pending = false;  // input blocks requested for a tile not yet processed
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int m0, n0;
+      int m0, n0, k_slice;
       bool narrow;
-      unit_coords<BN>(sched, tile, m0, n0, narrow);
+      unit_coords<BN>(sched, tile, m0, n0, narrow, k_slice);
       if constexpr (!C::kNarrow) narrow = false;
+      ctx.split = k_slice;
       // a full tile: this warp's column half; a narrow unit: the epilogue splits it itself
       const uint32_t col_off = narrow ? 0u : static_cast<uint32_t>(half * kCols);
       if (!narrow) n0 += half * kCols;
@@ -463,6 +473,15 @@ bool resid_wide(uint32_t rows) {
   return 3 * m_tiles > sms && m_tiles <= sms;
 }
 
+uint32_t splitk_splits(uint32_t rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t tiles = 3 * ((rows + BM - 1) / BM), sms = static_cast<uint32_t>(sm_count(dev));
+  for (uint32_t s : {8u, 6u, 4u, 3u, 2u})
+    if (tiles * s <= sms) return s;
+  return 1;
+}
+
 GemmShape gemm_shape(GemmOp op, uint32_t rows) {
   if ((op == GemmOp::Resid384 || op == GemmOp::Resid1536) && resid_wide(rows)) {
     GemmShape s = gemm_shape(op);
@@ -481,6 +500,7 @@ GemmShape gemm_shape(GemmOp op) {
     case GemmOp::SwiGLU: return {256, kGateUp, kHidden};
     case GemmOp::ResidLN384: return {384, kHidden, kHidden};
     case GemmOp::ResidLN1536: return {384, kHidden, kMlp};
+    case GemmOp::SplitK1536: return {128, kHidden, kMlp};
   }
   return {0, 0, 0};
 }
@@ -494,6 +514,7 @@ const char *gemm_name(GemmOp op) {
     case GemmOp::SwiGLU: return "gemm_gateup_swiglu";
     case GemmOp::ResidLN384: return "gemm_o_resid_layernorm";
     case GemmOp::ResidLN1536: return "gemm_down_resid_layernorm";
+    case GemmOp::SplitK1536: return "gemm_down_splitk";
   }
   return "?";
 }
@@ -512,7 +533,8 @@ static uint32_t tma_store_cols(GemmOp op) {
 }
 
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
-                    GemmMaps *maps, std::string *err, const void *ln_out, bool ln_f32) {
+                    GemmMaps *maps, std::string *err, const void *ln_out, bool ln_f32,
+                    uint32_t splits) {
   const GemmShape s = gemm_shape(op, rows);
   // weight boxes: one per MMA of the K step (BN = 384: two of 192 rows), or BN/2 rows for the
   // BN = 256 ops (two per full tile, one per narrow unit)
@@ -521,6 +543,8 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
       !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))
     return false;
   maps->d = maps->a;  // unused unless the epilogue writes a LayerNorm output
+  if (op == GemmOp::SplitK1536)  // f32 partial slabs [splits][rows][384], 32x32 blocks
+    return encode_map_f32_slabs(&maps->c, out, kHidden, rows, splits, 32, err);
   const uint32_t c_cols = tma_store_cols(op);
   if (c_cols == 0) {
     maps->c = maps->a;  // unused by this epilogue
@@ -552,8 +576,9 @@ static cudaError_t configure_one() {
 // hold at most half the CTAs, those L tiles run as 2L narrow units, so the last wave costs half
 // a tile instead of a whole one.
 template <int BN>
-static TileSched tile_sched(uint32_t rows, int n, int sms) {
+static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
   TileSched t;
+  t.k_splits = k_splits;
   t.m_tiles = static_cast<int>((rows + BM - 1) / BM);
   const bool narrow_ok = GemmCfg<BN, EpiSwiGLU>::kNarrow;
   t.full_n = narrow_ok ? n / BN : (n + BN - 1) / BN;
@@ -565,12 +590,13 @@ static TileSched tile_sched(uint32_t rows, int n, int sms) {
     if (left > 0 && 2 * left <= sms) t.split_from = full - left;
   }
   t.num_units = t.split_from + 2 * (full - t.split_from) + (native_half ? t.m_tiles : 0);
+  if (k_splits > 1) t.num_units = full * k_splits;  // full tiles only, repeated per K slice
   return t;
 }
 
 template <int BN, class Epi>
 static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k, const Epi &epi,
-                              uint32_t *status, cudaStream_t stream) {
+                              uint32_t *status, cudaStream_t stream, int k_splits = 1) {
   static bool configured[64] = {};  // per template instance and device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -579,11 +605,11 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const TileSched sched = tile_sched<BN>(rows, n, sm_count(dev));
+  const TileSched sched = tile_sched<BN>(rows, n, sm_count(dev), k_splits);
   const int grid = sched.num_units < sm_count(dev) ? sched.num_units : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
                     gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,
-                    static_cast<int>(rows), sched, k / BK, epi, status);
+                    static_cast<int>(rows), sched, k / BK / k_splits, epi, status);
 }
 
 // Set the shared-memory limits of every GEMM instance on the current device (done at load, so
@@ -596,6 +622,7 @@ cudaError_t configure_gemm_kernels() {
   if ((e = configure_one<384, EpiResidWide>()) != cudaSuccess) return e;
   if ((e = configure_one<256, EpiSwiGLU>()) != cudaSuccess) return e;
   if ((e = configure_one<384, EpiResidLN>()) != cudaSuccess) return e;
+  if ((e = configure_one<128, EpiPartialF32>()) != cudaSuccess) return e;
   int dev = 0;
   cudaGetDevice(&dev);
   sm_count(dev);
@@ -627,6 +654,10 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
                              EpiResidLN{args.bias, args.lambda, args.gamma, args.beta,
                                         args.ln_out_f32 != nullptr},
                              status, stream);
+    case GemmOp::SplitK1536:
+      if (args.splits == 0 || (kMlp / BK) % args.splits != 0) return cudaErrorInvalidValue;
+      return launch_one<128>(maps, rows, s.n, s.k, EpiPartialF32{}, status, stream,
+                             static_cast<int>(args.splits));
   }
   return cudaErrorInvalidValue;
 }

@@ -48,6 +48,7 @@ struct EpiCtx {
   int buf;             // staging block to use next
   int nbuf;            // staging blocks per warp (2: double-buffered; 1: Epi::kStagingBufs)
   bool narrow;         // BM x BN/2 unit: run() gets the whole unit and takes its part by `half`
+  int split;           // split-K launches: the K slice (partial slab) of this unit
   const CUtensorMap *out_map;
   const CUtensorMap *ln_map;  // EpiResidLN: the LayerNorm output
   uint64_t *in_bar;    // kTmaInput epilogues: this warp's two input-block mbarriers
@@ -247,6 +248,46 @@ struct EpiQkvRope {
       }
       tma_emit32(c, lo, col);
       tma_emit32(c, hi, col + 32);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Split-K partial product (kernels/matmul_splitk_f16_wmma.loom): the f32 accumulator of this
+// unit's K slice, without the bias, into slab ctx.split of partials [splits][rows][384]. Each warp
+// emits 32-row x 32-column f32 blocks (128-byte rows, 128-byte swizzle: row r's 16-byte chunk k
+// at chunk k ^ (r & 7)) through two 4 KB staging blocks and TMA stores; the map clips rows past
+// the GEMM's rows inside each slab.
+// ---------------------------------------------------------------------------------------------
+struct EpiPartialF32 {
+  static constexpr int kSmem = 0;
+  static constexpr bool kTmaStore = true;
+  static constexpr int kStagingBufs = 4;  // 4 x 2 KB = two 4 KB f32 blocks per warp
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
+  __device__ void init(uint8_t *, int, int) const {}
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
+    const int sw = c.lane & 7;
+#pragma unroll 1
+    for (int j = 0; j < COLS; j += 32) {
+      uint32_t r[32];
+      tmem_load32(taddr + j, r);
+      uint8_t *blk = c.staging + c.buf * 4096;
+      if (c.lane == 0) bulk_wait_read<1>();  // the store that last used this block has read it
+      __syncwarp();
+      uint8_t *rowp = blk + c.lane * 128;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<uint4 *>(rowp + ((k ^ sw) << 4)) =
+            make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (c.lane == 0) {
+        tma_store_3d(c.out_map, blk, n0 + j, c.row0, c.split);
+        bulk_commit();
+      }
+      c.buf ^= 1;
     }
   }
 };

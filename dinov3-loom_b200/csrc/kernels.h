@@ -40,12 +40,18 @@ bool encode_map_f32(CUtensorMap *map, const void *base, uint64_t cols, uint64_t 
 // are clipped.
 bool encode_map_f16_images(CUtensorMap *map, const void *base, uint64_t cols, uint64_t n_images,
                            uint32_t box_rows, std::string *err);
+// 3D f32 view [slabs][rows][cols] (split-K partials), box = 32 columns x box_rows x 1 slab,
+// 128-byte swizzle; stores past `rows` are clipped inside each slab.
+bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                          uint64_t slabs, uint32_t box_rows, std::string *err);
 
 // ---- GEMM operations (gemm.cu) ----
 // Resid*: x += lambda (A W^T + b) on 128-column tiles. ResidLN*: the same on full 384-column
 // rows, followed in the same kernel by the LayerNorm of the updated row into ln_out (f16) or
-// ln_out_f32.
-enum class GemmOp { Patch, QkvRope, Resid384, Resid1536, SwiGLU, ResidLN384, ResidLN1536 };
+// ln_out_f32. SplitK1536: the down projection's K split into `splits` slices, each CTA writing
+// the f32 partial product of its slice (no bias) into slab s of partials [splits][rows][384]
+// (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it.
+enum class GemmOp { Patch, QkvRope, Resid384, Resid1536, SwiGLU, ResidLN384, ResidLN1536, SplitK1536 };
 
 struct GemmShape {
   int bn;      // tile width along N
@@ -69,9 +75,10 @@ struct GemmMaps {
 };
 // `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch). ResidLN* also takes
 // the LayerNorm output: `ln_out` f16 [rows][384], or f32 when `ln_f32`.
+// SplitK1536: `out` is the f32 partials [splits][rows][384].
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
                     GemmMaps *maps, std::string *err, const void *ln_out = nullptr,
-                    bool ln_f32 = false);
+                    bool ln_f32 = false, uint32_t splits = 1);
 
 struct GemmArgs {
   const float *bias = nullptr;
@@ -83,7 +90,15 @@ struct GemmArgs {
   const float *beta = nullptr;
   __half *ln_out = nullptr;      // ResidLN*: f16 LayerNorm output, or
   float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
+  float *partials = nullptr;     // SplitK1536: [splits][rows][384] f32
+  uint32_t splits = 1;           // SplitK1536: K slices (a divisor of 24, the 64-wide k-blocks)
 };
+
+// The K split of the down projection over `rows` rows in the model's plan: the most slices (at
+// most 8, a divisor of 24, so each CTA walks at least three 64-wide k-blocks) whose
+// 128x128 partial tiles still fit one wave of CTAs; 1 means no split (the unsplit residual
+// GEMM runs instead).
+uint32_t splitk_splits(uint32_t rows);
 
 cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const GemmArgs &args,
                         uint32_t *status, cudaStream_t stream);
@@ -109,6 +124,16 @@ cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *ga
                                  const float *beta, __half *out, cudaStream_t stream);
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, float *out, cudaStream_t stream);
+
+// Split-K completion (kernels/splitk_reduce_f16.loom): x[r][n] = f16(x + lambda[n] (sum over
+// s = 0..splits-1 in that order of partials[s][r][n] + b[n])), one warp per row. With gamma and
+// beta it also writes the LayerNorm of the updated f16 row, like the separate LayerNorm kernel
+// that follows the reduce in the reference's plan, into h (f16) or, when out_f32 is non-null,
+// out_f32.
+cudaError_t launch_splitk_reduce(const float *partials, uint32_t rows, uint32_t splits,
+                                 const float *bias, const float *lambda, __half *x,
+                                 const float *gamma, const float *beta, __half *h, float *out_f32,
+                                 cudaStream_t stream);
 
 // Mean of each image's 196 patch rows of the f32 output (the reference's f32 order), n x 384.
 cudaError_t launch_patch_mean(const float *out, uint32_t n_images, float *dst,

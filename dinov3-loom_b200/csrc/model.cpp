@@ -133,18 +133,26 @@ Model::Model(const std::string &path, dv3_options options)
 
     // Activations for max_batch images.
     const size_t B = max_batch_, R = kTokens * B, P = kPatches * B;
-    const size_t sizes[12] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
+    // split-K partial slabs of the down projection: the largest splits x rows of any batch size
+    size_t partial_floats = 0;
+    for (size_t b = 1; b <= B; ++b) {
+      const uint32_t r = static_cast<uint32_t>(kTokens * b);
+      partial_floats = std::max(partial_floats, static_cast<size_t>(splitk_splits(r)) * r * kHidden);
+    }
+    const size_t sizes[13] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
                               R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
                               R * kMlp * 2,           R * kHidden * 4, 256,
-                              B * kHidden * 4,        B * kImageElements * 4, R * kHidden * 4};
-    size_t at[12], act_total = 0;
-    for (int i = 0; i < 12; ++i) {
+                              B * kHidden * 4,        B * kImageElements * 4, R * kHidden * 4,
+                              partial_floats * 4};
+    size_t at[13], act_total = 0;
+    for (int i = 0; i < 13; ++i) {
       at[i] = act_total;
       act_total += align256(sizes[i]);
     }
     cuda(cudaMalloc(&act_blob_, act_total), "allocate activations");
     uint8_t *a = static_cast<uint8_t *>(act_blob_);
     image_ = reinterpret_cast<float *>(a + at[0]);
+    partials_ = reinterpret_cast<float *>(a + at[12]);
     patches_ = reinterpret_cast<__half *>(a + at[1]);
     x_ = reinterpret_cast<__half *>(a + at[2]);
     h_ = reinterpret_cast<__half *>(a + at[3]);
@@ -211,6 +219,14 @@ void Model::release() {
 // keep 128-wide residual tiles and separate LayerNorm launches (3 + 12*7 = 87).
 // DV3_FUSE_LAYERNORM=0 in the environment restores the separate LayerNorm launches (3 + 12*7 =
 // 87, the reference's plan) for comparison; =1 forces fusion.
+// K slices of the down projection at this batch size (1: unsplit). DV3_SPLITK=0 in the
+// environment turns the split off for comparison.
+uint32_t Model::down_splits(uint32_t rows) const {
+  if (const char *v = std::getenv("DV3_SPLITK"))
+    if (v[0] == '0') return 1;
+  return splitk_splits(rows);
+}
+
 bool Model::fuse_layernorm(size_t b) const {
   if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
   return resid_wide(static_cast<uint32_t>(kTokens * b));
@@ -257,15 +273,24 @@ Plan &Model::prepare(size_t b, int slot) {
   const bool fuse = fuse_layernorm(b);
   const GemmOp o_op = fuse ? GemmOp::ResidLN384 : GemmOp::Resid384;
   const GemmOp down_op = fuse ? GemmOp::ResidLN1536 : GemmOp::Resid1536;
+  // Small batches: the down projection splits K (its 6 to 39 128x128 tiles alone would leave most
+  // SMs idle for 24 k-blocks) and the reduce kernel also does the LayerNorm after it (the
+  // reference splits K at batch 1, src/lib.rs:218-226).
+  const uint32_t splits = fuse ? 1u : down_splits(r);
+  float *partials = partials_;
   for (int i = 0; i < 12; ++i) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
     need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, qkv, &qkv_maps, &err));
     need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err, h));
     need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, act, &gu_maps, &err));
-    need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err,
-                        i == 11 ? static_cast<const void *>(out) : static_cast<const void *>(h),
-                        i == 11));
+    if (splits > 1)
+      need(make_gemm_maps(GemmOp::SplitK1536, act, r, l.down_w, partials, &down_maps, &err,
+                          nullptr, false, splits));
+    else
+      need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err,
+                          i == 11 ? static_cast<const void *>(out) : static_cast<const void *>(h),
+                          i == 11));
     add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;
@@ -301,6 +326,19 @@ Plan &Model::prepare(size_t b, int slot) {
     const bool last = i == 11;
     const float *ng = last ? w.norm_w : w.layer[i + 1].norm1_w;
     const float *nb = last ? w.norm_b : w.layer[i + 1].norm1_b;
+    if (splits > 1) {
+      add(gemm_name(GemmOp::SplitK1536), [=](cudaStream_t s) {
+        GemmArgs g;
+        g.partials = partials;
+        g.splits = splits;
+        return launch_gemm(GemmOp::SplitK1536, down_maps, r, g, st, s);
+      });
+      add("splitk_reduce_layernorm", [=](cudaStream_t s) {
+        return launch_splitk_reduce(partials, r, splits, l.down_b, l.ls2, x, ng, nb,
+                                    last ? nullptr : h, last ? out : nullptr, s);
+      });
+      continue;
+    }
     add(gemm_name(down_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.down_b;

@@ -85,6 +85,7 @@ class Model {
   Plan &prepare(size_t batch, int slot = 0);    // build + capture once per batch size and slot
   void drain();                                  // finish every outstanding submission
   bool fuse_layernorm(size_t batch) const;      // plan variant for this batch size
+  uint32_t down_splits(uint32_t rows) const;    // split-K slices of the down projection
   void check_status();                          // read the device status words (synchronous)
   void activate() const;
   void release();  // free every device resource (idempotent)
@@ -101,6 +102,7 @@ class Model {
   __half *x_ = nullptr, *h_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *act_ = nullptr,
          *patches_ = nullptr;
   float *image_ = nullptr, *out_ = nullptr, *pmean_ = nullptr;
+  float *partials_ = nullptr;  // split-K partial slabs of the down projection
   float *image_slot_[2] = {}, *out_slot_[2] = {};  // slot 0 aliases image_ / out_
   // Per slot: upload done, forward done (input consumed, output ready), download done.
   cudaEvent_t ev_in_[2] = {}, ev_done_[2] = {}, ev_out_[2] = {};

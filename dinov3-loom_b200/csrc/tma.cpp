@@ -120,4 +120,33 @@ bool encode_map_f16_images(CUtensorMap *map, const void *base, uint64_t cols, ui
   return true;
 }
 
+// 3D f32 view [slabs][rows][cols] of split-K partial slabs, box = 32 columns (128 bytes) x
+// box_rows x 1 slab, 128-byte swizzle: stores past `rows` are clipped inside each slab.
+bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                          uint64_t slabs, uint32_t box_rows, std::string *err) {
+  auto fn = encode_fn(err);
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 4) % 16 != 0 || rows == 0 ||
+      slabs == 0 || box_rows == 0 || box_rows > 256) {
+    if (err) *err = "tensor map: base must be 16-byte aligned, rows of whole 16-byte units";
+    return false;
+  }
+  const cuuint64_t dims[3] = {cols, rows, slabs};
+  const cuuint64_t strides[2] = {cols * 4, cols * 4 * rows};
+  const cuuint32_t box[3] = {32, box_rows, 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base), dims,
+                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) {
+      char buf[128];
+      std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+      *err = buf;
+    }
+    return false;
+  }
+  return true;
+}
+
 }  // namespace dv3

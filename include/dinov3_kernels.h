@@ -89,8 +89,7 @@ int dv3k_attention(const uint16_t *qkv, uint32_t rows, uint16_t *out, uint32_t *
 
 /* Projection with LayerScale and residual: x[row][n] = f16(x + lambda[n] * (a @ w^T + bias)[n])
  * for n < 384, in place. k is 384 (attention output projection) or 1536 (MLP down projection).
- * Replaces kernels/matmul_resid_f16_wmma.loom (both specialisations) and, for batch 1, the
- * split-K pair kernels/matmul_splitk_f16_wmma.loom + kernels/splitk_reduce_f16.loom. */
+ * Replaces kernels/matmul_resid_f16_wmma.loom (both specialisations). */
 int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
                       const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
                       void *stream);
@@ -106,6 +105,29 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
                                 const float *bias, const float *lambda, uint16_t *x,
                                 const float *gamma, const float *beta, uint16_t *h,
                                 float *out_f32, uint32_t *status, void *stream);
+
+/* Down projection split over K (kernels/matmul_splitk_f16_wmma.loom, launched at batch 1 by
+ * src/lib.rs:218-224 with the specialisation of :297): for each slice s < splits of the 1536-long
+ * reduction, partials[s][row][n] = sum over k in slice s of a[row][k] * w[n][k], f32, no bias.
+ * a: [rows][1536] f16, w: [384][1536] f16, partials: [splits][rows][384] f32. splits divides 24
+ * (the 64-wide k-blocks): 1, 2, 3, 4, 6, 8, 12 or 24 (the reference fixes 4). */
+int dv3k_matmul_splitk(const uint16_t *a, uint32_t rows, const uint16_t *w, uint32_t splits,
+                       float *partials, uint32_t *status, void *stream);
+
+/* Split-K completion (kernels/splitk_reduce_f16.loom, src/lib.rs:225-226, :298): in place,
+ * x[row][n] = f16(x + lambda[n] * ((partials[0][row][n] + ... + partials[splits-1][row][n]) +
+ * bias[n])), the slabs summed in order onto zero, each step rounded as written. */
+int dv3k_splitk_reduce(const float *partials, uint32_t rows, uint32_t splits, const float *bias,
+                       const float *lambda, uint16_t *x, void *stream);
+
+/* dv3k_splitk_reduce followed in the same kernel by the LayerNorm that the reference launches
+ * after it (kernels/layernorm_rowwave_f16.loom, or _f32out for the final norm): h[row] =
+ * f16(LN(x[row]) * gamma + beta), or, when h is NULL, out_f32[row] = the same in f32. The
+ * LayerNorm reads the f16-rounded x, eps 1e-5. */
+int dv3k_splitk_reduce_layernorm(const float *partials, uint32_t rows, uint32_t splits,
+                                 const float *bias, const float *lambda, uint16_t *x,
+                                 const float *gamma, const float *beta, uint16_t *h,
+                                 float *out_f32, void *stream);
 
 /* Gate/up projection with SwiGLU: act[row][j] = f16(silu(g) * u), g = h@Wg^T+bg, u = h@Wu^T+bu,
  * j < 1536, from the interleaved gateup_w / gateup_b. Replaces

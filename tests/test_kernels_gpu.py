@@ -255,6 +255,85 @@ def test_matmul_resid_layernorm(k, b, f32_out):
         assert_close16(h, ref_ln)
 
 
+def splitk_reduce_ref(partials, bias, lam, x):
+    """kernels/splitk_reduce_f16.loom in float32 with its own rounding order: the slabs onto
+    zero in order, + bias, * lambda, + the f16 residual, rounded to f16."""
+    acc = np.zeros(partials.shape[1:], np.float32)
+    for p in partials.astype(np.float32):
+        acc = acc + p
+    u = x.astype(np.float32) + (acc + bias.astype(np.float32)) * lam.astype(np.float32)
+    return u.astype(np.float16)
+
+
+# The down projection's K split (the reference splits it in 4 at batch 1): every slab against
+# numpy; 3 and 8 images need clipped rows inside each slab (201 and 1608 rows, not multiples of
+# 128); the slabs of a row must not spill into the next slab.
+@pytest.mark.parametrize("splits", [1, 4, 8])
+@pytest.mark.parametrize("b", [1, 3, 8])
+def test_matmul_splitk(b, splits):
+    rng = np.random.default_rng(80 + b + splits)
+    r = rows_of(b)
+    a = f16(rng.standard_normal((r, 1536)))
+    w = f16(rng.standard_normal((384, 1536)) / np.sqrt(1536))
+    parts = torch.full((splits, r, 384), 7.0, dtype=torch.float32, device=DEV)
+    st = status()
+    check_rc(lib().dv3k_matmul_splitk(ptr(t16(a)), r, ptr(t16(w)), splits, ptr(parts), ptr(st), stream()))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist() == [0, 0]
+    got = parts.cpu().numpy().astype(np.float64)
+    ks = 1536 // splits
+    for s in range(splits):
+        ref = a[:, s * ks:(s + 1) * ks] @ w[:, s * ks:(s + 1) * ks].T
+        err = np.abs(got[s] - ref) / np.maximum(1.0, np.abs(ref))
+        assert err.max() < 1e-4, (s, err.max())
+    with pytest.raises(AssertionError):
+        check_rc(lib().dv3k_matmul_splitk(ptr(t16(a)), r, ptr(t16(w)), 5, ptr(parts), ptr(st), stream()))
+
+
+@pytest.mark.parametrize("splits", [1, 4, 8])
+@pytest.mark.parametrize("b", [1, 3])
+def test_splitk_reduce_bit_exact(b, splits):
+    """The reduce follows the reference's rounding order exactly: bitwise equal to float32 numpy."""
+    rng = np.random.default_rng(90 + b + splits)
+    r = rows_of(b)
+    partials = rng.standard_normal((splits, r, 384)).astype(np.float32)
+    bias = (rng.standard_normal(384) * 0.1).astype(np.float32)
+    lam = (rng.random(384) * 0.2 + 0.05).astype(np.float32)
+    x0 = rng.standard_normal((r, 384)).astype(np.float16)
+    x = torch.from_numpy(x0.copy()).to(DEV)
+    check_rc(lib().dv3k_splitk_reduce(ptr(t32(partials)), r, splits, ptr(t32(bias)), ptr(t32(lam)),
+                                      ptr(x), stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(x.cpu().numpy(), splitk_reduce_ref(partials, bias, lam, x0))
+
+
+@pytest.mark.parametrize("f32_out", [False, True])
+@pytest.mark.parametrize("b", [1, 5])
+def test_splitk_reduce_layernorm(b, f32_out):
+    rng = np.random.default_rng(95 + b + f32_out)
+    r, splits = rows_of(b), 8
+    partials = rng.standard_normal((splits, r, 384)).astype(np.float32)
+    bias = (rng.standard_normal(384) * 0.1).astype(np.float32)
+    lam = (rng.random(384) * 0.2 + 0.05).astype(np.float32)
+    x0 = (rng.standard_normal((r, 384)) + rng.standard_normal((r, 1))).astype(np.float16)
+    g = (rng.standard_normal(384) * 0.3 + 1).astype(np.float32)
+    be = (rng.standard_normal(384) * 0.1).astype(np.float32)
+    x = torch.from_numpy(x0.copy()).to(DEV)
+    h = None if f32_out else torch.empty((r, 384), dtype=torch.float16, device=DEV)
+    o = torch.empty((r, 384), dtype=torch.float32, device=DEV) if f32_out else None
+    check_rc(lib().dv3k_splitk_reduce_layernorm(ptr(t32(partials)), r, splits, ptr(t32(bias)),
+                                                ptr(t32(lam)), ptr(x), ptr(t32(g)), ptr(t32(be)),
+                                                ptr(h), ptr(o), stream()))
+    torch.cuda.synchronize()
+    want_x = splitk_reduce_ref(partials, bias, lam, x0)
+    np.testing.assert_array_equal(x.cpu().numpy(), want_x)
+    ref_ln = ref_numpy.norm(want_x.astype(np.float64), g, be)
+    if f32_out:
+        assert np.abs(o.cpu().numpy() - ref_ln).max() < 1e-4
+    else:
+        assert_close16(h, ref_ln)
+
+
 # 50 and 64 images leave a partial last wave of at most 74 tiles: those run as two 128-wide
 # units each (1008 and 1240 units of work over 148 CTAs).
 @pytest.mark.parametrize("b", [1, 3, 50, 64])

@@ -202,10 +202,13 @@ def test_benchmark_and_profile(models):
         model.benchmark(np.zeros(0, np.float32), 10)
     prof = model.profile_launches(2, 2)
     # small batches: patchify, patch GEMM, LN1 of layer 0, then per layer QKV, attention, o,
-    # LN2, gate/up, down, LN (the reference's plan, src/lib.rs:149-263, also has 87 at b > 1)
+    # LN2, gate/up, and the down projection as a split-K GEMM plus a reduce that also does the
+    # LayerNorm after it (the reference's plan, src/lib.rs:149-263, has 87 launches too)
     assert len(prof) == model.launches_per_forward(2) == 3 + 12 * 7
     assert all(ms > 0 for _, ms in prof)
-    assert sum(name.startswith("layernorm") for name, _ in prof) == 25
+    names = [name for name, _ in prof]
+    assert sum(n.startswith("layernorm") for n in names) == 1 + 12
+    assert names.count("gemm_down_splitk") == names.count("splitk_reduce_layernorm") == 12
 
 
 def test_fused_layernorm_plan(weights_file, monkeypatch):
@@ -226,6 +229,25 @@ def test_fused_layernorm_plan(weights_file, monkeypatch):
     assert [n for n, _ in prof].count("gemm_down_resid_layernorm") == 12
     for i in range(16):
         assert cos(fused[i], split[i]) > 0.99999
+
+
+def test_split_k_plan(weights_file, monkeypatch):
+    """Small batches split the down projection's K (and fuse the LayerNorm after it into the
+    reduce); DV3_SPLITK=0 (read when a batch size's graph is built) keeps the unsplit GEMM and a
+    separate LayerNorm. Both give the same result within f32 summation order and f16 rounding."""
+    path = weights_file(1, "stress")
+    images = synth.images(33, 3)
+    with dv.DINOv3.load(path, dv.Options(0, 4)) as model:
+        names = [n for n, _ in model.profile_launches(3, 1)]
+        assert names.count("gemm_down_splitk") == 12
+        split = model.forward(images)
+    monkeypatch.setenv("DV3_SPLITK", "0")
+    with dv.DINOv3.load(path, dv.Options(0, 4)) as model:
+        names = [n for n, _ in model.profile_launches(3, 1)]
+        assert names.count("gemm_down_resid") == 12 and "gemm_down_splitk" not in names
+        plain = model.forward(images)
+    for i in range(3):
+        assert cos(split[i], plain[i]) > 0.99999
 
 
 def test_submit_wait_serving_path(models):
