@@ -589,6 +589,9 @@ static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
     const int left = full % sms;
     if (left > 0 && 2 * left <= sms) t.split_from = full - left;
   }
+  // Small batches: when even the halves of every tile fit one wave, all of them run as narrow
+  // units, so twice as many SMs share the work and each epilogue has half as much.
+  if (narrow_ok && 2 * full <= sms) t.split_from = 0;
   t.num_units = t.split_from + 2 * (full - t.split_from) + (native_half ? t.m_tiles : 0);
   if (k_splits > 1) t.num_units = full * k_splits;  // full tiles only, repeated per K slice
   return t;
