@@ -254,9 +254,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint8_t *st = smem + (k & 1) * kStageBytes;
         // Tile 1 starts once tile 0's first P is written: from then on one tile's softmax
         // overlaps the other tile's MMAs and output instead of both competing for the exp2 unit.
+        // A CTA with a single item (small batches) has nothing to overlap and starts both.
         ok = mbar_wait(&load_full[k & 1], (k >> 1) & 1, abort_flag) &&
              mbar_wait(&tmem_empty[t], par ^ 1u, abort_flag) &&
-             (t == 0 || k > 0 || mbar_wait(&p_full[0], 0, abort_flag));
+             (t == 0 || k > 0 || count == 1 || mbar_wait(&p_full[0], 0, abort_flag));
         if (!ok) break;
         tc_fence_after();
         const uint64_t qd = sw128_desc(smem_u32(st + (t ? kStageQ1 : kStageQ0)));
