@@ -84,6 +84,17 @@ struct StagingBufs<Epi, decltype(void(Epi::kStagingBufs))> {
   static constexpr int value = Epi::kStagingBufs;
 };
 
+// Whether a BN = 128 epilogue takes narrow BM x 64 units (Epi::kNarrowOk; BN = 256 epilogues all
+// do).
+template <class Epi, class = void>
+struct NarrowOk {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct NarrowOk<Epi, decltype(void(Epi::kNarrowOk))> {
+  static constexpr bool value = Epi::kNarrowOk;
+};
+
 // Bytes of one epilogue warp's staging region in the tile buffers: Epi::kWarpStaging when it
 // exists.
 template <class Epi, class = void>
@@ -99,9 +110,10 @@ template <int BN, class Epi>
 struct GemmCfg {
   static constexpr int kSplit = BN > 256 ? 2 : 1;    // MMAs per K step
   static constexpr int kMmaN = BN / kSplit;
-  // BN = 256: a unit of work may be a narrow BM x BN/2 tile (TileSched); the weight tile then
-  // arrives as BN/2-row boxes, two per K step for a full tile and one for a narrow one.
-  static constexpr bool kNarrow = BN == 256;
+  // BN = 256 (and BN = 128 with a kNarrowOk epilogue): a unit of work may be a narrow BM x BN/2
+  // tile (TileSched); the weight tile then arrives as BN/2-row boxes, two per K step for a full
+  // tile and one for a narrow one.
+  static constexpr bool kNarrow = BN == 256 || (BN == 128 && NarrowOk<Epi>::value);
   static constexpr int kBBox = kNarrow ? BN / 2 : kMmaN;  // rows of one weight box
   static constexpr int kAccBufs = 2 * BN <= 512 ? 2 : 1;
   static constexpr int kA = BM * BK * 2;  // 16 KB
@@ -537,8 +549,10 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
                     uint32_t splits) {
   const GemmShape s = gemm_shape(op, rows);
   // weight boxes: one per MMA of the K step (BN = 384: two of 192 rows), or BN/2 rows for the
-  // BN = 256 ops (two per full tile, one per narrow unit)
-  const uint32_t b_rows = s.bn >= 256 ? s.bn / 2 : s.bn;
+  // ops that take narrow units (BN = 256, and the 128-wide residual GEMMs): two per full tile,
+  // one per narrow unit
+  const bool narrow_ops = s.bn == 256 || (s.bn == 128 && (op == GemmOp::Resid384 || op == GemmOp::Resid1536));
+  const uint32_t b_rows = s.bn >= 256 || narrow_ops ? s.bn / 2 : s.bn;
   if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err) ||
       !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))
     return false;
@@ -575,12 +589,12 @@ static cudaError_t configure_one() {
 // columns, one narrow unit per M tile, last); when a partial last wave of L full tiles would
 // hold at most half the CTAs, those L tiles run as 2L narrow units, so the last wave costs half
 // a tile instead of a whole one.
-template <int BN>
+template <int BN, class Epi>
 static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
   TileSched t;
   t.k_splits = k_splits;
   t.m_tiles = static_cast<int>((rows + BM - 1) / BM);
-  const bool narrow_ok = GemmCfg<BN, EpiSwiGLU>::kNarrow;
+  const bool narrow_ok = GemmCfg<BN, Epi>::kNarrow && k_splits == 1;
   t.full_n = narrow_ok ? n / BN : (n + BN - 1) / BN;
   const bool native_half = narrow_ok && n % BN != 0;  // n % BN == BN / 2 (QKV)
   const int full = t.m_tiles * t.full_n;
@@ -608,7 +622,7 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const TileSched sched = tile_sched<BN>(rows, n, sm_count(dev), k_splits);
+  const TileSched sched = tile_sched<BN, Epi>(rows, n, sm_count(dev), k_splits);
   const int grid = sched.num_units < sm_count(dev) ? sched.num_units : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
                     gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,

@@ -305,15 +305,25 @@ struct EpiResid {
   static constexpr int kSmem = 2 * kHidden * 4;
   static constexpr bool kTmaStore = true;
   static constexpr bool kTmaInput = true;
+  // Narrow 128 x 64 units (small batches): each column half of the epilogue warps takes one
+  // 32-column block of the unit; the second input barrier gets a plain arrival, so both barriers
+  // complete one phase per unit whatever its width.
+  static constexpr bool kNarrowOk = true;
   using Pre = NoPre;
   __device__ Pre prefetch(int n0, const EpiCtx &c) const {
     if (c.lane == 0) {
       bulk_wait_read<0>();  // the previous tile's stores have read both blocks
+      if (c.narrow) {
+        mbar_arrive_expect_tx(&c.in_bar[0], kStageBlockBytes);
+        tma_load_2d(c.staging, c.out_map, &c.in_bar[0], n0 + 32 * c.half, c.row0);
+        mbar_arrive(&c.in_bar[1]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        mbar_arrive_expect_tx(&c.in_bar[j], kStageBlockBytes);
-        tma_load_2d(c.staging + j * kStageBlockBytes, c.out_map, &c.in_bar[j], n0 + 32 * j,
-                    c.row0);
+        for (int j = 0; j < 2; ++j) {
+          mbar_arrive_expect_tx(&c.in_bar[j], kStageBlockBytes);
+          tma_load_2d(c.staging + j * kStageBlockBytes, c.out_map, &c.in_bar[j], n0 + 32 * j,
+                      c.row0);
+        }
       }
     }
     return {};
@@ -329,8 +339,15 @@ struct EpiResid {
     const float *sb = reinterpret_cast<const float *>(c.smem);
     const float *sl = sb + kHidden;
     const int sw = (c.lane >> 1) & 3;
+    // narrow: the unit's accumulator starts at taddr; this column half's block is block 0 of the
+    // staging, at TMEM column 32 * half and output column n0 + 32 * half
+    const int blocks = c.narrow ? 1 : 2;
+    if (c.narrow) {
+      taddr += 32 * c.half;
+      n0 += 32 * c.half;
+    }
 #pragma unroll 1
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < blocks; ++j) {
       uint32_t r[32];
       tmem_ld32(taddr + 32 * j, r);
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&c.in_bar[j], c.iter & 1u, c.abort_flag));
