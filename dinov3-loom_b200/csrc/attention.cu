@@ -34,6 +34,9 @@
 //              w, P = f16(w) (keys >= 201 zero) stored to TMEM. Once O is in TMEM: O / sum rounded
 //              to f16 into a per-warp 32-row staging tile (128-byte swizzle), written out by one
 //              TMA store per warp.
+// Small batches (two query tiles per item still fit one CTA each, 2 x items <= SMs): the grid
+// has two CTAs per item and each computes one query tile (tile_split); the other tile's roles
+// idle, so an item costs one tile's chain instead of one and a half.
 // The probabilities are rounded to f16 before PV and the normaliser is the f32 sum of the
 // unrounded weights, as in the reference kernel (:214-216).
 //
@@ -166,7 +169,8 @@ __device__ __forceinline__ uint32_t scaled_pair(uint32_t a, uint32_t b, float in
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmq,
                      const __grid_constant__ CUtensorMap tmkv,
-                     const __grid_constant__ CUtensorMap tmo, int n_items, uint32_t *status) {
+                     const __grid_constant__ CUtensorMap tmo, int n_items, int tile_split,
+                     uint32_t *status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t *smem = smem_raw + pad;
@@ -180,15 +184,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(load_full + 14);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // Items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
-  const int count = static_cast<int>(blockIdx.x) < n_items
+  // Items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ... With tile_split (small batches,
+  // a grid of two CTAs per item) CTA b takes only query tile b & 1 of item b >> 1, and the other
+  // tile's roles have nothing to do.
+  const int only_tile = tile_split ? static_cast<int>(blockIdx.x & 1u) : -1;
+  const int count = tile_split ? (static_cast<int>(blockIdx.x >> 1) < n_items ? 1 : 0)
+                    : static_cast<int>(blockIdx.x) < n_items
                         ? (n_items - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
                         : 0;
+  auto item_of = [&](int k) {
+    return tile_split ? static_cast<int>(blockIdx.x >> 1)
+                      : static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&load_full[i], 1);
-      mbar_init(&load_empty[i], 2);  // one commit per tile's issuer
+      mbar_init(&load_empty[i], tile_split ? 1 : 2);  // one commit per active tile's issuer
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
@@ -226,12 +238,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           *abort_flag = 1;
           break;
         }
-        const int item = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+        const int item = item_of(k);
         const int img = item / kHeads, head = item % kHeads;
         uint8_t *st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&load_full[s], kLoadBytes);
-        tma_load_3d(st + kStageQ0, &tmq, &load_full[s], head * 64, 0, img);
-        tma_load_3d(st + kStageQ1, &tmq, &load_full[s], head * 64, 128, img);
+        mbar_arrive_expect_tx(&load_full[s], only_tile < 0 ? kLoadBytes : kLoadBytes - kQBytes);
+        if (only_tile != 1) tma_load_3d(st + kStageQ0, &tmq, &load_full[s], head * 64, 0, img);
+        if (only_tile != 0) tma_load_3d(st + kStageQ1, &tmq, &load_full[s], head * 64, 128, img);
         tma_load_3d(st + kStageK, &tmkv, &load_full[s], kHidden + head * 64, 0, img);
         tma_load_3d(st + kStageV, &tmkv, &load_full[s], 2 * kHidden + head * 64, 0, img);
         armed |= 1u << s;
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
     // One issuer thread per tile, so neither tile's MMAs wait behind the other's issue.
-    if (lane == 0) {
+    if (lane == 0 && (only_tile < 0 || warp - kMmaWarp == only_tile)) {
       const int t = warp - kMmaWarp;
       constexpr uint32_t idesc_s = idesc_f16_f32(128, kSKeys, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(128, 64, true);
@@ -284,12 +296,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     const int t = warp >> 2, q = warp & 3;
+    const int my_count = only_tile < 0 || t == only_tile ? count : 0;
     const int r = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + t * kTileCols;
     const bool active = !(t == 1 && q == 3);  // warp-uniform
     uint8_t *stg = smem + kStagingOff + warp * kStagingBytes;
     uint8_t *stg_row = stg + r % 32 * 128;
-    for (int k = 0; k < count; ++k) {
+    for (int k = 0; k < my_count; ++k) {
       const uint32_t par = k & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], par, abort_flag))) {
         if (lane == 0) {
@@ -336,7 +349,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          const int item = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+          const int item = item_of(k);
           tma_store_3d(&tmo, stg, (item % kHeads) * 64, t * 128 + q * 32, item / kHeads);
           bulk_commit();
         }
@@ -378,9 +391,11 @@ cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t 
     configured[dev] = true;
   }
   const int n_items = static_cast<int>(rows / kTokens) * kHeads;
-  const int grid = n_items < sm_count(dev) ? n_items : sm_count(dev);
+  // Small batches (every query tile fits its own SM): one CTA per query tile.
+  const int tile_split = 2 * n_items <= sm_count(dev) ? 1 : 0;
+  const int grid = tile_split ? 2 * n_items : (n_items < sm_count(dev) ? n_items : sm_count(dev));
   return launch_pdl(attention_kernel, dim3(grid), dim3(kAttnThreads), kAttnSmem, stream, maps.q,
-                    maps.kv, maps.out, n_items, status);
+                    maps.kv, maps.out, n_items, tile_split, status);
 }
 
 }  // namespace dv3
