@@ -21,9 +21,9 @@
 // 32-column chunks (tcgen05.ld 32x32b.x32). Two warps per SM sub-partition hide the latency of
 // the epilogue arithmetic, which otherwise limits the whole GEMM.
 //
-// Tiles are walked m-major with the N tile fastest (tile t -> m = t / n_tiles, n = t % n_tiles)
-// by a grid of min(tiles, SMs) persistent CTAs, so the CTAs working at one time share A rows
-// through L2.
+// Units of work (TileSched: full tiles in m-major order with the N tile fastest, so the CTAs
+// working at one time share A rows through L2, then narrow half-width units) are dealt
+// round-robin to a grid of min(units, SMs) persistent CTAs.
 #include <type_traits>
 
 #include "gemm_epilogues.cuh"
@@ -135,10 +135,8 @@ struct GemmCfg {
   static constexpr int kTmemCols = kAccBufs * BN <= 256 ? 256 : 512;
   // kEarly: epilogue warps whose staging region lies in the first freed stage (the rest go to
   // the second); each warp's region is Epi::kWarpStaging bytes.
-  static constexpr int kEarlyA =
-      kEarly ? (kStage / EpiWarpStaging<Epi>::value < kEpilogueWarps ? kStage / EpiWarpStaging<Epi>::value
-                                                                     : kEpilogueWarps)
-             : 0;
+  static constexpr int kWarpsPerStage = kEarly ? kStage / EpiWarpStaging<Epi>::value : 0;
+  static constexpr int kEarlyA = kWarpsPerStage < kEpilogueWarps ? kWarpsPerStage : kEpilogueWarps;
   static_assert(!kEarly || (kStages >= 3 && kEarlyA > 0 &&
                             (kEpilogueWarps - kEarlyA) * EpiWarpStaging<Epi>::value <= kStage),
                 "early epilogue input: two freed stages hold every warp's staging region");
@@ -158,10 +156,11 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
 // The units of work of one launch, dealt round-robin to the persistent CTAs (unit u to CTA
 // u % grid). Units [0, split_from) are full BM x BN tiles in m-major order with the N tile
 // fastest (full_n of them per M tile, so the CTAs working at one time share A rows through L2);
-// the rest are narrow BM x BN/2 units (BN = 256 only): first the two halves of each full tile
-// from split_from on, then, when N leaves half a tile over (N = full_n*BN + BN/2), the narrow
-// tile of each M tile at column full_n*BN. Narrow units at the end fill a partial last wave
-// with half-length work instead of whole tiles that leave most CTAs idle.
+// the rest are narrow BM x BN/2 units (GemmCfg::kNarrow configurations): first the two halves of
+// each full tile from split_from on, then, when N leaves half a tile over (N = full_n*BN + BN/2),
+// the narrow tile of each M tile at column full_n*BN. Narrow units at the end fill a partial last
+// wave with half-length work instead of whole tiles that leave most CTAs idle; at small batches
+// every tile runs as two narrow units. Split-K launches repeat the full tiles once per K slice.
 struct TileSched {
   int m_tiles;
   int full_n;      // full-width tiles per M tile

@@ -16,7 +16,14 @@
 //       processes COLS accumulator columns starting at TMEM address `taddr` (this warp's lane
 //       quarter) that belong to output columns n0..n0+COLS-1 of output row ctx.row. ctx.row may
 //       be >= M on the last M tile: TMEM loads still run, because tcgen05.ld is
-//       warp-collective, but global accesses are skipped (TMA stores clip such rows).
+//       warp-collective, but global accesses are skipped (TMA stores clip such rows). For a
+//       narrow unit (ctx.narrow) taddr and n0 are the unit's start and the epilogue takes its
+//       column half's part itself (by ctx.half).
+//   Optional traits: kNarrowOk (a BN = 128 epilogue that takes narrow 128 x 64 units),
+//       kStagingBufs (TMA-store staging blocks per warp, default 2), kStagingInTiles (stages in
+//       the mainloop's tile buffers; one tile per CTA), kEarlyInput (the TMA producer loads the
+//       input blocks into the stage buffers the last k-blocks free first), kWarpStaging (bytes
+//       of a warp's staging region in the tile buffers).
 //
 // Output path of kTmaStore epilogues: each warp owns 32 rows (its TMEM lane quarter) and emits
 // 32 columns at a time: the 32x32 f16 block goes into one of the warp's two 2 KB shared-memory
