@@ -475,13 +475,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // The residual GEMMs run on full 384-wide rows (one tile per CTA, A read once: about 0.56 us per
 // 64-deep k-block for three 128-column tiles' worth of MMAs, against 0.31 us per k-block for one
-// 128-wide tile) once 128-wide tiles would need more than one wave of CTAs, as long as all the
-// full-row tiles fit one wave. Below that the 128-wide tiles keep three times as many SMs busy.
+// 128-wide tile; the LayerNorm fused) once the row tiles outnumber half the SMs, as long as they
+// all fit one wave. Below that the 128-wide tiles (with narrow units for a partial second wave)
+// keep three times as many SMs busy and fit about one and a half waves, which measured faster
+// (batch 32: 852 against 897 us per forward; even at 48, faster from 56 on).
 bool resid_wide(uint32_t rows) {
   int dev = 0;
   cudaGetDevice(&dev);
   const uint32_t m_tiles = (rows + BM - 1) / BM, sms = static_cast<uint32_t>(sm_count(dev));
-  return 3 * m_tiles > sms && m_tiles <= sms;
+  return 2 * m_tiles > sms && m_tiles <= sms;
 }
 
 uint32_t splitk_splits(uint32_t rows) {

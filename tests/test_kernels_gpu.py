@@ -202,10 +202,11 @@ def test_attention(b):
     assert_close16(out, ref)
 
 
-# Up to 94 images the residual GEMM runs on full 384-wide rows (one tile per CTA); 100 images
-# take the 128-wide tile path.
+# From 48 to 94 images the residual GEMM runs on full 384-wide rows (one tile per CTA); fewer
+# images take 128-wide tiles (narrow 128x64 units at 1 and 3), 100 images 128-wide tiles with
+# narrow units for the partial last wave, like 40 (189 tiles: 148, then 41 as 82 narrow units).
 @pytest.mark.parametrize("k", [384, 1536])
-@pytest.mark.parametrize("b", [1, 3, 64, 100])
+@pytest.mark.parametrize("b", [1, 3, 40, 64, 100])
 def test_matmul_resid(k, b):
     rng = np.random.default_rng(50 + b + k)
     r = rows_of(b)
