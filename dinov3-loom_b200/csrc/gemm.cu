@@ -552,7 +552,9 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
   // weight boxes: one per MMA of the K step (BN = 384: two of 192 rows), or BN/2 rows for the
   // ops that take narrow units (BN = 256, and the 128-wide residual GEMMs): two per full tile,
   // one per narrow unit
-  const bool narrow_ops = s.bn == 256 || (s.bn == 128 && (op == GemmOp::Resid384 || op == GemmOp::Resid1536));
+  const bool narrow_ops =
+      s.bn == 256 ||
+      (s.bn == 128 && (op == GemmOp::Resid384 || op == GemmOp::Resid1536 || op == GemmOp::Patch));
   const uint32_t b_rows = s.bn >= 256 || narrow_ops ? s.bn / 2 : s.bn;
   if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err) ||
       !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))

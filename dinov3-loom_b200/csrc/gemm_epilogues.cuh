@@ -161,6 +161,7 @@ struct EpiPatch {
   __half *x;
   static constexpr int kSmem = kHidden * 4;
   static constexpr bool kTmaStore = false;
+  static constexpr bool kNarrowOk = true;  // a narrow 128 x 64 unit: 32 columns per column half
   using Pre = NoPre;
   __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
@@ -171,8 +172,9 @@ struct EpiPatch {
     const float *sb = reinterpret_cast<const float *>(c.smem);
     const bool ok = c.row < c.M;
     const int token = (c.row / kPatches) * kTokens + kPrefix + c.row % kPatches;
+    const int k0 = c.narrow ? 32 * c.half : 0, k1 = c.narrow ? k0 + 32 : COLS;
 #pragma unroll 1
-    for (int k = 0; k < COLS; k += 32) {
+    for (int k = k0; k < k1; k += 32) {
       uint32_t r[32];
       tmem_load32(taddr + k, r);
       float v[32];
