@@ -310,6 +310,36 @@ int dv3k_splitk_reduce_layernorm(const float *partials, uint32_t rows, uint32_t 
                        "splitk_reduce_layernorm");
 }
 
+int dv3k_down_splitk_noalloc(const uint16_t *a, uint32_t rows, const uint16_t *w, uint32_t splits,
+                             const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
+                             void *stream) {
+  if (!all_aligned(a, w, bias, lambda, x)) return bad_args("pointers must be 16-byte aligned");
+  if (splits == 0 || (dv3::kMlp / 64) % splits != 0)
+    return bad_args("splits must divide 24 (the 64-wide k-blocks of 1536)");
+  if (rows == 0) return DV3_OK;
+  size_t capacity = 0;
+  float *partials = dv3::splitk_scratch(&capacity);
+  if (!partials) return fail(DV3_DEVICE, "split-K scratch: no device address");
+  if (static_cast<size_t>(splits) * rows * dv3::kHidden > capacity)
+    return bad_args("splits x rows exceeds the 6144 partial rows of the no-alloc scratch");
+  dv3::GemmMaps maps;
+  std::string err;
+  if (!dv3::make_gemm_maps(dv3::GemmOp::SplitK1536, a, rows, w, partials, &maps, &err, nullptr,
+                           false, splits))
+    return bad_args(err.c_str());
+  dv3::GemmArgs g;
+  g.partials = partials;
+  g.splits = splits;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rc = launch_status(dv3::launch_gemm(dv3::GemmOp::SplitK1536, maps, rows, g, status, s),
+                               dv3::gemm_name(dv3::GemmOp::SplitK1536));
+  if (rc != DV3_OK) return rc;
+  return launch_status(dv3::launch_splitk_reduce(partials, rows, splits, bias, lambda,
+                                                 reinterpret_cast<__half *>(x), nullptr, nullptr,
+                                                 nullptr, nullptr, s),
+                       "splitk_reduce");
+}
+
 int dv3k_matmul_resid(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
                       const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
                       void *stream) {

@@ -486,6 +486,24 @@ bool resid_wide(uint32_t rows) {
   return 2 * m_tiles > sms && m_tiles <= sms;
 }
 
+// Partial slabs of the no-alloc split-K entry point (dv3k_down_splitk_noalloc): a file-scope
+// device array, so that call needs no workspace from its caller and allocates nothing. Sized for
+// the largest splits x rows the plan uses (2 slices of 3015 rows at batch 15; 8 of 603 at 3).
+constexpr size_t kSplitkScratchFloats = static_cast<size_t>(6144) * kHidden;
+static __device__ __align__(256) float g_splitk_scratch[kSplitkScratchFloats];
+
+float *splitk_scratch(size_t *capacity_floats) {
+  static void *addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev] && cudaGetSymbolAddress(&addr[dev], g_splitk_scratch) != cudaSuccess) {
+    addr[dev] = nullptr;
+    return nullptr;
+  }
+  if (capacity_floats) *capacity_floats = kSplitkScratchFloats;
+  return static_cast<float *>(addr[dev]);
+}
+
 uint32_t splitk_splits(uint32_t rows) {
   int dev = 0;
   cudaGetDevice(&dev);

@@ -99,6 +99,9 @@ struct GemmArgs {
 // 128x128 partial tiles still fit one wave of CTAs; 1 means no split (the unsplit residual
 // GEMM runs instead).
 uint32_t splitk_splits(uint32_t rows);
+// The device address (current device) of the file-scope partial-slab array of the no-alloc
+// split-K entry point, and its size in floats; null if the address cannot be had.
+float *splitk_scratch(size_t *capacity_floats);
 
 cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const GemmArgs &args,
                         uint32_t *status, cudaStream_t stream);

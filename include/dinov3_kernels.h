@@ -129,6 +129,15 @@ int dv3k_splitk_reduce_layernorm(const float *partials, uint32_t rows, uint32_t 
                                  const float *gamma, const float *beta, uint16_t *h,
                                  float *out_f32, void *stream);
 
+/* dv3k_matmul_splitk followed by dv3k_splitk_reduce (x[row][n] = f16(x + lambda[n] * (sum of
+ * the slices + bias[n])), in place) without a workspace argument: the partial slabs live in a
+ * file-scope device array of the library (6144 x 384 floats, so splits x rows <= 6144), and the
+ * call allocates nothing. Two launches on `stream`; calls on different streams must not overlap,
+ * since they share that array. */
+int dv3k_down_splitk_noalloc(const uint16_t *a, uint32_t rows, const uint16_t *w, uint32_t splits,
+                             const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
+                             void *stream);
+
 /* Gate/up projection with SwiGLU: act[row][j] = f16(silu(g) * u), g = h@Wg^T+bg, u = h@Wu^T+bu,
  * j < 1536, from the interleaved gateup_w / gateup_b. Replaces
  * kernels/matmul_swiglu_f16_wmma.loom (k=384, n=1536). */
