@@ -190,6 +190,25 @@ def test_full_size_batch_properties(models, oracles):
     np.testing.assert_array_equal(model.forward(images), out)
 
 
+@pytest.mark.parametrize("b", [12, 40])
+def test_mid_size_batch_plans(models, oracles, b):
+    """Batch sizes between the batch-1 and batch-64 plans: 12 images run the down projection as 2
+    K slices and attention as one CTA per query tile; 40 images run 128-wide residual tiles with
+    narrow 128x64 units for their partial second wave and QKV with a partial last wave. Every
+    image matches its single-image forward, two match the float64 oracle, repeats are bitwise."""
+    model = models("stress", max_batch=64)
+    images = synth.images(300 + b, b)
+    out = model.forward(images)
+    assert np.isfinite(out).all()
+    for i in (0, b // 2, b - 1):
+        assert cos(out[i], model.forward(images[i:i + 1])[0]) > 0.99999, f"image {i}"
+    want = oracles("stress").forward(images[[1, b - 2]], threads=0)
+    for got, ref in zip(out[[1, b - 2]], want):
+        assert cos(got, ref) > 0.9999 and cos(got[0], ref[0]) > 0.9999
+        assert np.abs(got - ref).max() < MAX_ABS
+    np.testing.assert_array_equal(model.forward(images), out)
+
+
 def test_benchmark_and_profile(models):
     model = models("baseline", max_batch=4)
     images = synth.images(3, 2)
