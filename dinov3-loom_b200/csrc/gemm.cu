@@ -607,9 +607,9 @@ static cudaError_t configure_one() {
 }
 
 // The schedule of a launch (TileSched). BN = 256: N = full_n*256 (+ 128 for QKV's last
-// columns, one narrow unit per M tile, last); when a partial last wave of L full tiles would
-// hold at most half the CTAs, those L tiles run as 2L narrow units, so the last wave costs half
-// a tile instead of a whole one.
+// columns, one narrow unit per M tile, last); when the 2L halves of a partial last wave of L
+// full tiles (plus QKV's narrow tiles) fit one wave of CTAs, those L tiles run as 2L narrow
+// units, so the last wave costs half a tile instead of a whole one.
 template <int BN, class Epi>
 static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
   TileSched t;
@@ -620,9 +620,9 @@ static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
   const bool native_half = narrow_ok && n % BN != 0;  // n % BN == BN / 2 (QKV)
   const int full = t.m_tiles * t.full_n;
   t.split_from = full;
-  if (narrow_ok && !native_half && full > sms) {
-    const int left = full % sms;
-    if (left > 0 && 2 * left <= sms) t.split_from = full - left;
+  if (narrow_ok && full > sms) {  // the halves of a partial last wave, with QKV's native narrow
+    const int left = full % sms;  // tiles, in at most one more wave of narrow units
+    if (left > 0 && 2 * left + (native_half ? t.m_tiles : 0) <= sms) t.split_from = full - left;
   }
   // Small batches: when even the halves of every tile fit one wave, all of them run as narrow
   // units, so twice as many SMs share the work and each epilogue has half as much.
