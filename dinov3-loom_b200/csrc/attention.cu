@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmq,
                      const __grid_constant__ CUtensorMap tmkv,
                      const __grid_constant__ CUtensorMap tmo, int n_items, int tile_split,
-                     uint32_t *status) {
+                     const void *l2_next, size_t l2_next_bytes, uint32_t *status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t *smem = smem_raw + pad;
@@ -226,6 +226,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // the QKV rows of the previous kernel are complete from here on
   pdl_trigger();
+  // the producer warp's idle lane starts a later kernel's weights toward L2
+  if (warp == kProducerWarp && lane == 1 && l2_next) l2_prefetch_share(l2_next, l2_next_bytes);
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -380,7 +382,7 @@ cudaError_t configure_attention_kernel() {
 }
 
 cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const void *l2_next, size_t l2_next_bytes) {
   if (rows == 0) return cudaSuccess;
   static bool configured[64] = {};
   int dev = 0;
@@ -395,7 +397,8 @@ cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t 
   const int tile_split = 2 * n_items <= sm_count(dev) ? 1 : 0;
   const int grid = tile_split ? 2 * n_items : (n_items < sm_count(dev) ? n_items : sm_count(dev));
   return launch_pdl(attention_kernel, dim3(grid), dim3(kAttnThreads), kAttnSmem, stream, maps.q,
-                    maps.kv, maps.out, n_items, tile_split, status);
+                    maps.kv, maps.out, n_items, tile_split, l2_next,
+                    l2_next_bytes & ~static_cast<size_t>(15), status);
 }
 
 }  // namespace dv3

@@ -167,6 +167,8 @@ struct TileSched {
   int split_from;  // full tiles processed whole
   int num_units;
   int k_splits;    // split-K: the full tiles repeat for each K slice (slice-major); else 1
+  const void *l2_next;    // weights of a later kernel to prefetch into L2 (or null)
+  size_t l2_next_bytes;
 };
 
 template <int BN>
@@ -253,6 +255,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   pdl_wait();  // activations of the previous kernel are complete from here on
   pdl_trigger();
+  // an epilogue thread, idle until the first accumulator, starts the next weights toward L2
+  if (threadIdx.x == 64 && sched.l2_next) l2_prefetch_share(sched.l2_next, sched.l2_next_bytes);
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = sched.num_units;
   if (C::kInTiles && num_tiles > static_cast<int>(gridDim.x)) {  // the host never launches this
@@ -629,12 +633,15 @@ static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
   if (narrow_ok && 2 * full <= sms) t.split_from = 0;
   t.num_units = t.split_from + 2 * (full - t.split_from) + (native_half ? t.m_tiles : 0);
   if (k_splits > 1) t.num_units = full * k_splits;  // full tiles only, repeated per K slice
+  t.l2_next = nullptr;
+  t.l2_next_bytes = 0;
   return t;
 }
 
 template <int BN, class Epi>
 static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k, const Epi &epi,
-                              uint32_t *status, cudaStream_t stream, int k_splits = 1) {
+                              uint32_t *status, cudaStream_t stream, const GemmArgs &args,
+                              int k_splits = 1) {
   static bool configured[64] = {};  // per template instance and device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -643,7 +650,9 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const TileSched sched = tile_sched<BN, Epi>(rows, n, sm_count(dev), k_splits);
+  TileSched sched = tile_sched<BN, Epi>(rows, n, sm_count(dev), k_splits);
+  sched.l2_next = args.l2_next;
+  sched.l2_next_bytes = args.l2_next_bytes & ~static_cast<size_t>(15);
   const int grid = sched.num_units < sm_count(dev) ? sched.num_units : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
                     gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,
@@ -673,28 +682,30 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
   const GemmShape s = gemm_shape(op);
   switch (op) {
     case GemmOp::Patch:
-      return launch_one<128>(maps, rows, s.n, s.k, EpiPatch{args.bias, args.out}, status, stream);
+      return launch_one<128>(maps, rows, s.n, s.k, EpiPatch{args.bias, args.out}, status, stream,
+                             args);
     case GemmOp::QkvRope:
       return launch_one<256>(maps, rows, s.n, s.k,
-                             EpiQkvRope{args.bias, args.rope_cos, args.rope_sin}, status, stream);
+                             EpiQkvRope{args.bias, args.rope_cos, args.rope_sin}, status, stream, args);
     case GemmOp::Resid384:
     case GemmOp::Resid1536:
       if (resid_wide(rows))
         return launch_one<384>(maps, rows, s.n, s.k, EpiResidWide{args.bias, args.lambda}, status,
-                               stream);
+                               stream, args);
       return launch_one<128>(maps, rows, s.n, s.k, EpiResid{args.bias, args.lambda},
-                             status, stream);
+                             status, stream, args);
     case GemmOp::SwiGLU:
-      return launch_one<256>(maps, rows, s.n, s.k, EpiSwiGLU{args.bias}, status, stream);
+      return launch_one<256>(maps, rows, s.n, s.k, EpiSwiGLU{args.bias}, status, stream,
+                             args);
     case GemmOp::ResidLN384:
     case GemmOp::ResidLN1536:
       return launch_one<384>(maps, rows, s.n, s.k,
                              EpiResidLN{args.bias, args.lambda, args.gamma, args.beta,
                                         args.ln_out_f32 != nullptr},
-                             status, stream);
+                             status, stream, args);
     case GemmOp::SplitK1536:
       if (args.splits == 0 || (kMlp / BK) % args.splits != 0) return cudaErrorInvalidValue;
-      return launch_one<128>(maps, rows, s.n, s.k, EpiPartialF32{}, status, stream,
+      return launch_one<128>(maps, rows, s.n, s.k, EpiPartialF32{}, status, stream, args,
                              static_cast<int>(args.splits));
   }
   return cudaErrorInvalidValue;

@@ -92,6 +92,10 @@ struct GemmArgs {
   float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
   float *partials = nullptr;     // SplitK1536: [splits][rows][384] f32
   uint32_t splits = 1;           // SplitK1536: K slices (a divisor of 24, the 64-wide k-blocks)
+  // Weights of a later kernel (16-byte aligned; no kernel writes them) that this launch starts
+  // toward L2, so that kernel's first tiles do not wait for DRAM.
+  const void *l2_next = nullptr;
+  size_t l2_next_bytes = 0;
 };
 
 // The K split of the down projection over `rows` rows in the model's plan: the most slices (at
@@ -117,8 +121,10 @@ struct AttentionMaps {
 };
 bool make_attention_map(const void *qkv, const void *out, uint32_t rows, AttentionMaps *maps,
                         std::string *err);
+// l2_next/l2_next_bytes: weights of a later kernel to prefetch into L2 (see GemmArgs).
 cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
-                             cudaStream_t stream);
+                             cudaStream_t stream, const void *l2_next = nullptr,
+                             size_t l2_next_bytes = 0);
 
 // ---- bandwidth kernels (elementwise.cu) ----
 cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,

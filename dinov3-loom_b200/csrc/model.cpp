@@ -232,6 +232,14 @@ bool Model::fuse_layernorm(size_t b) const {
   return resid_wide(static_cast<uint32_t>(kTokens * b));
 }
 
+// Bytes of each projection's f16 weights. Each launch of the plan starts the weights of a GEMM
+// one or two launches later toward L2 (GemmArgs::l2_next), so that kernel's first tiles do not
+// wait for DRAM: the weights are read once per forward, after activations have cycled the L2.
+constexpr size_t kQkvWBytes = size_t{kQkv} * kHidden * 2;
+constexpr size_t kOWBytes = size_t{kHidden} * kHidden * 2;
+constexpr size_t kGateUpWBytes = size_t{kGateUp} * kHidden * 2;
+constexpr size_t kDownWBytes = size_t{kHidden} * kMlp * 2;
+
 Plan &Model::prepare(size_t b, int slot) {
   auto it = plans_.find({b, slot});
   if (it != plans_.end()) return it->second;
@@ -263,6 +271,8 @@ Plan &Model::prepare(size_t b, int slot) {
   });
   add(gemm_name(GemmOp::Patch), [=](cudaStream_t s) {
     GemmArgs g;
+    g.l2_next = w.layer[0].qkv_w;
+    g.l2_next_bytes = kQkvWBytes;
     g.bias = w.patch_b;
     g.out = x;
     return launch_gemm(GemmOp::Patch, patch_maps, p, g, st, s);
@@ -297,9 +307,13 @@ Plan &Model::prepare(size_t b, int slot) {
       g.rope_cos = w.rope_cos;
       g.rope_sin = w.rope_sin;
       g.out = qkv;
+      g.l2_next = l.o_w;
+      g.l2_next_bytes = kOWBytes;
       return launch_gemm(GemmOp::QkvRope, qkv_maps, r, g, st, s);
     });
-    add("attention", [=](cudaStream_t s) { return launch_attention(attn_map, r, st, s); });
+    add("attention", [=](cudaStream_t s) {
+      return launch_attention(attn_map, r, st, s, l.gateup_w, kGateUpWBytes);
+    });
     // o-proj + LayerScale 1 + residual, and LN2 of this layer (fused or separate): x -> x, h
     add(gemm_name(o_op), [=](cudaStream_t s) {
       GemmArgs g;
@@ -309,6 +323,8 @@ Plan &Model::prepare(size_t b, int slot) {
       g.gamma = l.norm2_w;
       g.beta = l.norm2_b;
       g.ln_out = h;
+      g.l2_next = l.down_w;
+      g.l2_next_bytes = kDownWBytes;
       return launch_gemm(o_op, o_maps, r, g, st, s);
     });
     if (!fuse)
@@ -319,6 +335,10 @@ Plan &Model::prepare(size_t b, int slot) {
       GemmArgs g;
       g.bias = l.gateup_b;
       g.out = act;
+      if (i < 11) {
+        g.l2_next = w.layer[i + 1].qkv_w;
+        g.l2_next_bytes = kQkvWBytes;
+      }
       return launch_gemm(GemmOp::SwiGLU, gu_maps, r, g, st, s);
     });
     // down-proj + LayerScale 2 + residual, fused with LN1 of the next layer (f16 h) or, after

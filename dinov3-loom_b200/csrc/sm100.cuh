@@ -126,6 +126,21 @@ __device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
 // ---------------------------------------------------------------------------------------------
 // TMA (bulk tensor copies global -> shared, completion counted on an mbarrier)
 // ---------------------------------------------------------------------------------------------
+// This CTA's share of an L2 prefetch of [p, p + bytes) (16-byte aligned, a multiple of 16
+// bytes): 64 KB pieces dealt round-robin over the grid, each one cp.async.bulk.prefetch.L2 with
+// no shared memory and nothing to wait for. Used for weights of a later kernel, which no kernel
+// writes.
+__device__ __forceinline__ void l2_prefetch_share(const void *p, size_t bytes) {
+  constexpr size_t kPiece = 65536;
+  for (size_t off = blockIdx.x * kPiece; off < bytes; off += gridDim.x * kPiece) {
+    const uint32_t n = static_cast<uint32_t>(bytes - off < kPiece ? bytes - off : kPiece);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                     reinterpret_cast<uint64_t>(static_cast<const uint8_t *>(p) + off)),
+                 "r"(n)
+                 : "memory");
+  }
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
