@@ -19,9 +19,12 @@ namespace dv3 {
 __global__ void __launch_bounds__(256)
     patchify_kernel(const float *__restrict__ images, int n_images,
                     const float *__restrict__ prefix, __half *__restrict__ patches,
-                    __half *__restrict__ x, uint32_t *status) {
+                    __half *__restrict__ x, uint32_t *status, const void *l2_next,
+                    size_t l2_next_bytes) {
   pdl_wait();  // the input upload (and the previous forward's readers) are done from here on
   pdl_trigger();
+  // the patch GEMM's weights toward L2 (64 KB per block, the first blocks of the grid)
+  if (threadIdx.x == 0 && l2_next) l2_prefetch_share(l2_next, l2_next_bytes);
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n_patch_chunks = static_cast<int64_t>(n_images) * kPatches * 96;
   const int64_t n_prefix_chunks = static_cast<int64_t>(n_images) * kPrefix * 48;
@@ -147,12 +150,14 @@ __global__ void __launch_bounds__(256)
 }
 
 cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,
-                            __half *patches, __half *x, uint32_t *status, cudaStream_t stream) {
+                            __half *patches, __half *x, uint32_t *status, cudaStream_t stream,
+                            const void *l2_next, size_t l2_next_bytes) {
   if (n_images == 0) return cudaSuccess;
   const int64_t total = static_cast<int64_t>(n_images) * (kPatches * 96 + kPrefix * 48);
   const int blocks = static_cast<int>((total + 255) / 256);
   return launch_pdl(patchify_kernel, dim3(blocks), dim3(256), 0, stream, images,
-                    static_cast<int>(n_images), prefix, patches, x, status);
+                    static_cast<int>(n_images), prefix, patches, x, status, l2_next,
+                    l2_next_bytes & ~static_cast<size_t>(15));
 }
 
 cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *gamma,

@@ -127,8 +127,10 @@ cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t 
                              size_t l2_next_bytes = 0);
 
 // ---- bandwidth kernels (elementwise.cu) ----
+// l2_next/l2_next_bytes: weights of a later kernel to prefetch into L2 (see GemmArgs).
 cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,
-                            __half *patches, __half *x, uint32_t *status, cudaStream_t stream);
+                            __half *patches, __half *x, uint32_t *status, cudaStream_t stream,
+                            const void *l2_next = nullptr, size_t l2_next_bytes = 0);
 cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, __half *out, cudaStream_t stream);
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,

@@ -267,7 +267,8 @@ Plan &Model::prepare(size_t b, int slot) {
   need(make_attention_map(qkv, attn, r, &attn_map, &err));
 
   add("patchify", [=](cudaStream_t s) {
-    return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s);
+    return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s, w.patch_w,
+                           size_t{kHidden} * kPatchK * 2);
   });
   add(gemm_name(GemmOp::Patch), [=](cudaStream_t s) {
     GemmArgs g;
