@@ -529,7 +529,7 @@ GemmShape gemm_shape(GemmOp op, uint32_t rows) {
 GemmShape gemm_shape(GemmOp op) {
   switch (op) {
     case GemmOp::Patch: return {128, kHidden, kPatchK};
-    case GemmOp::QkvRope: return {256, kQkv, kHidden};  // 5 tiles; the last half-tile is zeros
+    case GemmOp::QkvRope: return {256, kQkv, kHidden};  // 4 full tiles + a narrow one per M tile
     case GemmOp::Resid384: return {128, kHidden, kHidden};
     case GemmOp::Resid1536: return {128, kHidden, kMlp};
     case GemmOp::SwiGLU: return {256, kGateUp, kHidden};
