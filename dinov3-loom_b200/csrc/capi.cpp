@@ -45,6 +45,10 @@ int check_model(dv3_model *m) {
 
 }  // namespace
 
+namespace dv3 {
+bool hub_weights(bool offline, std::string *path, std::string *err);
+}
+
 extern "C" {
 
 dv3_options dv3_default_options(void) {
@@ -63,6 +67,16 @@ int dv3_load(const char *path, dv3_options options, dv3_model **out) {
     if (!path) throw dv3::Error(DV3_INVALID_ARGUMENT, "null path");
     *out = new dv3_model(path, options);
   });
+}
+
+int dv3_from_pretrained(dv3_options options, dv3_model **out) {
+  if (!out) return fail(DV3_INVALID_ARGUMENT, "null output handle");
+  *out = nullptr;
+  if (options.max_batch < 1 || options.max_batch > DV3_MAX_BATCH_LIMIT)
+    return fail(DV3_INVALID_ARGUMENT, "max_batch must be 1..=64");
+  std::string path, err;
+  if (!dv3::hub_weights(false, &path, &err)) return fail(DV3_WEIGHTS, err);
+  return dv3_load(path.c_str(), options, out);
 }
 
 int dv3_forward(dv3_model *m, const float *pixels, size_t n, float *out, size_t out_n) {
@@ -139,6 +153,17 @@ int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *
     }
     if (count) *count = r.size();
   });
+}
+
+int dv3_hub_weights(int offline, char *path, size_t capacity) {
+  if (!path || capacity == 0) return fail(DV3_INVALID_ARGUMENT, "null path buffer");
+  std::string p, err;
+  if (!dv3::hub_weights(offline != 0, &p, &err)) return fail(DV3_WEIGHTS, err);
+  if (p.size() + 1 > capacity)
+    return fail(DV3_INVALID_ARGUMENT, "path buffer too small: " + std::to_string(p.size() + 1) +
+                                          " bytes needed");
+  std::memcpy(path, p.c_str(), p.size() + 1);
+  return DV3_OK;
 }
 
 int dv3_pack_f16(const char *name, const float *values, size_t n, uint16_t *out, size_t *bad) {

@@ -30,7 +30,7 @@ OK, INVALID_ARGUMENT, WEIGHTS, DEVICE, POISONED = range(5)
 
 __all__ = [
     "DINOv3", "DINOv3Error", "Options", "ForwardTimings", "Distribution", "LibraryMissing",
-    "IMAGE_ELEMENTS", "TOKENS", "HIDDEN", "pack_f16",
+    "IMAGE_ELEMENTS", "TOKENS", "HIDDEN", "pack_f16", "hub_weights",
 ]
 
 
@@ -78,6 +78,19 @@ class DINOv3:
             options = lib.dv3_default_options()
         h = ctypes.c_void_p()
         _check(lib.dv3_load(str(path).encode(), options, ctypes.byref(h)))
+        m = cls(h.value)
+        m.options = Options(options.device, options.max_batch)
+        return m
+
+    @classmethod
+    def from_pretrained(cls, options: Options | None = None) -> "DINOv3":
+        """DINOv3::from_pretrained (src/lib.rs:40-46): the pinned weights from the Hugging Face
+        cache (hub_weights); a miss raises DINOv3Error, nothing is downloaded."""
+        lib = _lib.load()
+        if options is None:
+            options = lib.dv3_default_options()
+        h = ctypes.c_void_p()
+        _check(lib.dv3_from_pretrained(options, ctypes.byref(h)))
         m = cls(h.value)
         m.options = Options(options.device, options.max_batch)
         return m
@@ -225,3 +238,12 @@ def pack_f16(name: str, values) -> np.ndarray:
     _check(_lib.load().dv3_pack_f16(name.encode(), arr.ctypes.data, arr.size, out.ctypes.data,
                                     ctypes.byref(bad)))
     return out.view(np.float16)
+
+
+def hub_weights(offline: bool = False) -> str:
+    """Path of the pinned model.safetensors in the shared Hugging Face cache (src/hub.rs:17-54).
+    Offline when `offline` or HF_HUB_OFFLINE is set to anything but "" or "0"; a file that is not
+    cached raises DINOv3Error (WEIGHTS) with the reference's message. Nothing is downloaded."""
+    buf = ctypes.create_string_buffer(4096)
+    _check(_lib.load().dv3_hub_weights(1 if offline else 0, buf, len(buf)))
+    return buf.value.decode()

@@ -71,6 +71,8 @@ SIGNATURES = {
     "dv3_launches_per_forward": ([_P, _SZ, ctypes.POINTER(_SZ)], _I),
     "dv3_profile_launches": ([_P, _SZ, _SZ, _P, _P, _SZ, ctypes.POINTER(_SZ)], _I),
     "dv3_pack_f16": ([ctypes.c_char_p, _P, _SZ, _P, ctypes.POINTER(_SZ)], _I),
+    "dv3_hub_weights": ([_I, ctypes.c_char_p, _SZ], _I),
+    "dv3_from_pretrained": ([Options, ctypes.POINTER(_P)], _I),
     # dinov3_kernels.h
     "dv3k_patchify": ([_P, _U32, _P, _P, _P, _P, _P], _I),
     "dv3k_patch_embed": ([_P, _U32, _P, _P, _P, _P, _P], _I),

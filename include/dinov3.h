@@ -73,6 +73,10 @@ dv3_options dv3_default_options(void);
  * sm_100), uploads, allocates and builds the kernels' state. */
 int dv3_load(const char *safetensors_path, dv3_options options, dv3_model **out);
 
+/* DINOv3::from_pretrained (src/lib.rs:40-46): checks max_batch, resolves the pinned weights with
+ * dv3_hub_weights(0, ...) (a cache miss is DV3_WEIGHTS; nothing is downloaded), then dv3_load. */
+int dv3_from_pretrained(dv3_options options, dv3_model **out);
+
 /* DINOv3::forward (src/lib.rs:90-114). `pixels` holds n_floats = k*DV3_IMAGE_ELEMENTS floats
  * (k >= 0); `out` must have room for k*201*384 floats (out_floats). Synchronous. Inputs larger
  * than max_batch are processed in chunks of max_batch. Non-finite input is an error; it is
@@ -160,6 +164,19 @@ int dv3_launches_per_forward(dv3_model *m, size_t batch, size_t *out);
  * next forward recomputes them). */
 int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *ms,
                          const char **names, size_t capacity, size_t *count);
+
+/* ---- Pinned weights in the Hugging Face cache (src/hub.rs), usable without a GPU. ---- */
+
+/* Path of facebook/dinov3-vits16plus-pretrain-lvd1689m at revision
+ * c93d816fc9e567563bc068f01475bec89cc634a6, model.safetensors, in the shared Hugging Face cache
+ * (HF_HUB_CACHE, else HF_HOME/hub, else XDG_CACHE_HOME/huggingface/hub, else
+ * ~/.cache/huggingface/hub; .../models--facebook--dinov3-vits16plus-pretrain-lvd1689m/
+ * snapshots/<revision>/model.safetensors), written NUL-terminated into `path`. Offline when
+ * `offline` is nonzero or HF_HUB_OFFLINE is set to anything but "" or "0". A file that is not
+ * cached gives DV3_WEIGHTS with the reference's message "<org>/<name> at <revision>:
+ * model.safetensors is not cached and model downloads are disabled" (offline), or, since this
+ * library has no network client, a "cannot download ..." message otherwise. */
+int dv3_hub_weights(int offline, char *path, size_t capacity);
 
 /* ---- Weight packing (src/weights.rs:6-17), usable without a GPU. ---- */
 

@@ -163,3 +163,88 @@ def test_null_model_is_an_error():
     assert lib.dv3_forward(None, None, 0, None, 0) == dv.INVALID_ARGUMENT
     assert lib.dv3_run(None, 1) == dv.INVALID_ARGUMENT
     lib.dv3_free(None)
+
+
+HUB_SNAPSHOT = ("models--facebook--dinov3-vits16plus-pretrain-lvd1689m/snapshots/"
+                "c93d816fc9e567563bc068f01475bec89cc634a6/model.safetensors")
+
+
+def test_hub_offline_miss_then_cached_hit(tmp_path, monkeypatch):
+    """src/hub.rs:60-81: an offline miss names the file and says it is not cached; once the pinned
+    snapshot file exists, both offline and online lookups return it without a server."""
+    monkeypatch.setenv("HF_HUB_CACHE", str(tmp_path))
+    monkeypatch.delenv("HF_HUB_OFFLINE", raising=False)
+    with pytest.raises(dv.DINOv3Error) as e:
+        dv.hub_weights(offline=True)
+    assert e.value.code == dv.WEIGHTS
+    assert "not cached" in str(e.value) and "model.safetensors" in str(e.value)
+    assert "c93d816fc9e567563bc068f01475bec89cc634a6" in str(e.value)
+    with pytest.raises(dv.DINOv3Error, match="cannot download"):   # no network client here
+        dv.hub_weights(offline=False)
+    path = tmp_path / HUB_SNAPSHOT
+    path.parent.mkdir(parents=True)
+    path.write_bytes(b"cached model")
+    for offline in (True, False):
+        assert dv.hub_weights(offline) == str(path)
+
+
+@pytest.mark.parametrize("value,offline", [("1", True), ("0", False), ("", False)])
+def test_hub_offline_environment(tmp_path, monkeypatch, value, offline):
+    monkeypatch.setenv("HF_HUB_CACHE", str(tmp_path))
+    monkeypatch.setenv("HF_HUB_OFFLINE", value)
+    with pytest.raises(dv.DINOv3Error) as e:
+        dv.hub_weights(offline=False)
+    assert ("downloads are disabled" in str(e.value)) == offline
+
+
+def test_hub_cache_directory_order(tmp_path, monkeypatch):
+    """HF_HUB_CACHE, else HF_HOME/hub, else XDG_CACHE_HOME/huggingface/hub, else
+    ~/.cache/huggingface/hub."""
+    for var in ("HF_HUB_CACHE", "HF_HOME", "XDG_CACHE_HOME"):
+        monkeypatch.delenv(var, raising=False)
+    for base, cache in [("home", "home/.cache/huggingface/hub"),
+                        ("xdg", "xdg/huggingface/hub"),
+                        ("hf", "hf/hub")]:
+        f = tmp_path / cache / HUB_SNAPSHOT
+        f.parent.mkdir(parents=True)
+        f.write_bytes(b"x")
+    monkeypatch.setenv("HOME", str(tmp_path / "home"))
+    assert dv.hub_weights(True) == str(tmp_path / "home/.cache/huggingface/hub" / HUB_SNAPSHOT)
+    monkeypatch.setenv("XDG_CACHE_HOME", str(tmp_path / "xdg"))
+    assert dv.hub_weights(True) == str(tmp_path / "xdg/huggingface/hub" / HUB_SNAPSHOT)
+    monkeypatch.setenv("HF_HOME", str(tmp_path / "hf"))
+    assert dv.hub_weights(True) == str(tmp_path / "hf/hub" / HUB_SNAPSHOT)
+    monkeypatch.setenv("HF_HUB_CACHE", str(tmp_path / "xdg/huggingface/hub"))
+    assert dv.hub_weights(True) == str(tmp_path / "xdg/huggingface/hub" / HUB_SNAPSHOT)
+
+
+def test_hub_path_buffer_too_small(tmp_path, monkeypatch):
+    monkeypatch.setenv("HF_HUB_CACHE", str(tmp_path))
+    f = tmp_path / HUB_SNAPSHOT
+    f.parent.mkdir(parents=True)
+    f.write_bytes(b"x")
+    buf = ctypes.create_string_buffer(8)
+    assert _lib.load().dv3_hub_weights(1, buf, len(buf)) == dv.INVALID_ARGUMENT
+    assert "too small" in _lib.last_error()
+
+
+def test_from_pretrained_checks_options_then_the_cache(tmp_path, monkeypatch, weights_file):
+    """src/lib.rs:40-46: max_batch first, then the cache lookup, then DINOv3::load (which stops at
+    the device check on a machine without a GPU)."""
+    import torch
+
+    monkeypatch.setenv("HF_HUB_CACHE", str(tmp_path))
+    monkeypatch.setenv("HF_HUB_OFFLINE", "1")
+    with pytest.raises(dv.DINOv3Error, match=r"max_batch must be 1\.\.=64"):
+        dv.DINOv3.from_pretrained(dv.Options(0, 65))
+    with pytest.raises(dv.DINOv3Error, match="not cached") as e:
+        dv.DINOv3.from_pretrained(dv.Options())
+    assert e.value.code == dv.WEIGHTS
+    if torch.cuda.is_available():
+        return
+    f = tmp_path / HUB_SNAPSHOT
+    f.parent.mkdir(parents=True)
+    f.symlink_to(weights_file(0, "baseline"))   # the cache's snapshot entries are symlinks
+    with pytest.raises(dv.DINOv3Error) as e:
+        dv.DINOv3.from_pretrained(dv.Options())
+    assert e.value.code == dv.DEVICE
