@@ -551,8 +551,12 @@ struct EpiResidLN {
       c.failed = true;
       return;
     }
-    // x = f16(x + lambda (acc + b)) in place; back into TMEM as packed f16; out by TMA
-    float2 s2 = make_float2(0.f, 0.f);
+    // x = f16(x + lambda (acc + b)) in place; back into TMEM as packed f16; out by TMA. Each
+    // 32-column chunk's shared-memory loads come before its stores, so they issue together
+    // instead of one 16-byte group at a time behind the previous group's store. The mean and the
+    // centred sum of squares of this warp's 192 columns build up chunk by chunk from the stored
+    // f16 values in registers (two passes within a chunk, chunks merged by Chan's formula).
+    float mean = 0.f, m2 = 0.f;
     uint32_t ra[32], rb[32];
     tmem_ld32(taddr, ra);
     tmem_wait_ld(ra);
@@ -562,12 +566,15 @@ struct EpiResidLN {
       uint32_t(&rn)[32] = (j & 1) ? ra : rb;
       if (j + 1 < kSub) tmem_ld32(taddr + 32 * (j + 1), rn);
       uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
+      uint4 q[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        q[k] = *reinterpret_cast<const uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4));
       uint32_t o[16];
+      float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        uint4 *qp = reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4));
-        const uint4 q = *qp;
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        const uint32_t w[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
         float bb[8], ll[8];
         lds8(sv + n0 + 32 * j + 8 * k, bb);
         lds8(sv + kHidden + n0 + 32 * j + 8 * k, ll);
@@ -579,10 +586,31 @@ struct EpiResidLN {
           o[4 * k + p] = pack_half2(v.x, v.y);
           s2 = __fadd2_rn(s2, unpack_half2(o[4 * k + p]));
         }
-        *qp = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
       }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) =
+            make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
       tmem_st16(taddr + 32 * j, o);
-      if (j + 1 < kSub) tmem_wait_ld(rn);
+      const float cm = (s2.x + s2.y) * (1.0f / 32);
+      const float2 ncm = make_float2(-cm, -cm);
+      float2 qa = make_float2(0.f, 0.f), qb = qa;
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const float2 d0 = __fadd2_rn(unpack_half2(o[i]), ncm);
+        qa = __ffma2_rn(d0, d0, qa);
+        const float2 d1 = __fadd2_rn(unpack_half2(o[i + 1]), ncm);
+        qb = __ffma2_rn(d1, d1, qb);
+      }
+      const float cq = (qa.x + qa.y) + (qb.x + qb.y);
+      if (j == 0) {
+        mean = cm;
+        m2 = cq;
+      } else {  // j chunks so far (32 j values) merged with 32 more
+        const float d = cm - mean;
+        mean += d * (1.0f / (j + 1));
+        m2 += cq + d * d * (32.0f * j / (j + 1));
+      }
       if (j & 1) {  // a 64-column block is complete
         fence_proxy_async_smem();
         __syncwarp();
@@ -591,34 +619,17 @@ struct EpiResidLN {
           bulk_commit();
         }
       }
+      if (j + 1 < kSub) tmem_wait_ld(rn);
     }
     tmem_st_wait();
-    // this warp's mean and centred sum of squares, merged with the other half of the row
-    const float mh = (s2.x + s2.y) * (1.0f / (kHidden / 2));
-    const float2 nmh = make_float2(-mh, -mh);
-    float2 q2 = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < kSub; j += 2) {
-      uint32_t x0[16], x1[16];
-      tmem_ld16(taddr + 32 * j, x0);
-      tmem_ld16(taddr + 32 * (j + 1), x1);
-      tmem_ld_wait();
-      tmem_regs_ready16(x0);
-      tmem_regs_ready16(x1);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 d0 = __fadd2_rn(unpack_half2(x0[i]), nmh);
-        q2 = __ffma2_rn(d0, d0, q2);
-        const float2 d1 = __fadd2_rn(unpack_half2(x1[i]), nmh);
-        q2 = __ffma2_rn(d1, d1, q2);
-      }
-    }
-    red[c.half * 128 + c.r] = mh;
-    red[256 + c.half * 128 + c.r] = q2.x + q2.y;
+    // merged with the other half of the row
+    red[c.half * 128 + c.r] = mean;
+    red[256 + c.half * 128 + c.r] = m2;
     named_barrier(1, kEpilogueThreads);
     const float m0 = red[c.r], m1 = red[128 + c.r];
-    const float mean = 0.5f * (m0 + m1), d = m1 - m0;
-    const float m2 = red[256 + c.r] + red[384 + c.r] + d * d * (kHidden / 4);
+    const float d = m1 - m0;
+    mean = 0.5f * (m0 + m1);
+    m2 = red[256 + c.r] + red[384 + c.r] + d * d * (kHidden / 4);
     const float rstd = rsqrtf(m2 * (1.0f / kHidden) + 1e-5f);
     // h = (x - mean) rstd gamma + beta, staged where the x blocks were
     if (c.lane == 0) bulk_wait_read<0>();  // the x stores have read the staging region
