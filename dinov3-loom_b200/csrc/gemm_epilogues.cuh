@@ -547,94 +547,102 @@ struct EpiResidLN {
     float *red = const_cast<float *>(sv) + kVecs;  // [0..255] means, [256..511] M2
     const int sw = c.lane & 7;
     uint8_t *const stage = c.staging;
-    if (!__all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag))) {
-      c.failed = true;
-      return;
-    }
+    // A warp whose residual never lands (the kernel is aborting) skips its work but still meets
+    // its partner warp at the barrier below, then reports the failure.
+    const bool landed =
+        __all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag));
     // x = f16(x + lambda (acc + b)) in place; back into TMEM as packed f16; out by TMA. Each
     // 32-column chunk's shared-memory loads come before its stores, so they issue together
     // instead of one 16-byte group at a time behind the previous group's store. The mean and the
     // centred sum of squares of this warp's 192 columns build up chunk by chunk from the stored
     // f16 values in registers (two passes within a chunk, chunks merged by Chan's formula).
     float mean = 0.f, m2 = 0.f;
-    uint32_t ra[32], rb[32];
-    tmem_ld32(taddr, ra);
-    tmem_wait_ld(ra);
+    if (landed) {
+      uint32_t ra[32], rb[32];
+      tmem_ld32(taddr, ra);
+      tmem_wait_ld(ra);
 #pragma unroll
-    for (int j = 0; j < kSub; ++j) {
-      uint32_t(&r)[32] = (j & 1) ? rb : ra;
-      uint32_t(&rn)[32] = (j & 1) ? ra : rb;
-      if (j + 1 < kSub) tmem_ld32(taddr + 32 * (j + 1), rn);
-      uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
-      uint4 q[4];
+      for (int j = 0; j < kSub; ++j) {
+        uint32_t(&r)[32] = (j & 1) ? rb : ra;
+        uint32_t(&rn)[32] = (j & 1) ? ra : rb;
+        if (j + 1 < kSub) tmem_ld32(taddr + 32 * (j + 1), rn);
+        uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
+        uint4 q[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        q[k] = *reinterpret_cast<const uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4));
-      uint32_t o[16];
-      float2 s2 = make_float2(0.f, 0.f);
+        for (int k = 0; k < 4; ++k)
+          q[k] = *reinterpret_cast<const uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4));
+        uint32_t o[16];
+        float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t w[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
-        float bb[8], ll[8];
-        lds8(sv + n0 + 32 * j + 8 * k, bb);
-        lds8(sv + kHidden + n0 + 32 * j + 8 * k, ll);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t w[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
+          float bb[8], ll[8];
+          lds8(sv + n0 + 32 * j + 8 * k, bb);
+          lds8(sv + kHidden + n0 + 32 * j + 8 * k, ll);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float2 a = make_float2(u2f(r[8 * k + 2 * p]), u2f(r[8 * k + 2 * p + 1]));
-          const float2 t = __fadd2_rn(a, make_float2(bb[2 * p], bb[2 * p + 1]));
-          const float2 v = __ffma2_rn(make_float2(ll[2 * p], ll[2 * p + 1]), t, unpack_half2(w[p]));
-          o[4 * k + p] = pack_half2(v.x, v.y);
-          s2 = __fadd2_rn(s2, unpack_half2(o[4 * k + p]));
+          for (int p = 0; p < 4; ++p) {
+            const float2 a = make_float2(u2f(r[8 * k + 2 * p]), u2f(r[8 * k + 2 * p + 1]));
+            const float2 t = __fadd2_rn(a, make_float2(bb[2 * p], bb[2 * p + 1]));
+            const float2 v =
+                __ffma2_rn(make_float2(ll[2 * p], ll[2 * p + 1]), t, unpack_half2(w[p]));
+            o[4 * k + p] = pack_half2(v.x, v.y);
+            s2 = __fadd2_rn(s2, unpack_half2(o[4 * k + p]));
+          }
         }
-      }
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) =
-            make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
-      tmem_st16(taddr + 32 * j, o);
-      const float cm = (s2.x + s2.y) * (1.0f / 32);
-      const float2 ncm = make_float2(-cm, -cm);
-      float2 qa = make_float2(0.f, 0.f), qb = qa;
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) =
+              make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        tmem_st16(taddr + 32 * j, o);
+        const float cm = (s2.x + s2.y) * (1.0f / 32);
+        const float2 ncm = make_float2(-cm, -cm);
+        float2 qa = make_float2(0.f, 0.f), qb = qa;
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const float2 d0 = __fadd2_rn(unpack_half2(o[i]), ncm);
-        qa = __ffma2_rn(d0, d0, qa);
-        const float2 d1 = __fadd2_rn(unpack_half2(o[i + 1]), ncm);
-        qb = __ffma2_rn(d1, d1, qb);
-      }
-      const float cq = (qa.x + qa.y) + (qb.x + qb.y);
-      if (j == 0) {
-        mean = cm;
-        m2 = cq;
-      } else {  // j chunks so far (32 j values) merged with 32 more
-        const float d = cm - mean;
-        mean += d * (1.0f / (j + 1));
-        m2 += cq + d * d * (32.0f * j / (j + 1));
-      }
-      if (j & 1) {  // a 64-column block is complete
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (c.lane == 0) {
-          tma_store_2d(c.out_map, stage + (j >> 1) * kBlockBytes, n0 + 64 * (j >> 1), c.row0);
-          bulk_commit();
+        for (int i = 0; i < 16; i += 2) {
+          const float2 d0 = __fadd2_rn(unpack_half2(o[i]), ncm);
+          qa = __ffma2_rn(d0, d0, qa);
+          const float2 d1 = __fadd2_rn(unpack_half2(o[i + 1]), ncm);
+          qb = __ffma2_rn(d1, d1, qb);
         }
+        const float cq = (qa.x + qa.y) + (qb.x + qb.y);
+        if (j == 0) {
+          mean = cm;
+          m2 = cq;
+        } else {  // j chunks so far (32 j values) merged with 32 more
+          const float d = cm - mean;
+          mean += d * (1.0f / (j + 1));
+          m2 += cq + d * d * (32.0f * j / (j + 1));
+        }
+        if (j & 1) {  // a 64-column block is complete
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (c.lane == 0) {
+            tma_store_2d(c.out_map, stage + (j >> 1) * kBlockBytes, n0 + 64 * (j >> 1), c.row0);
+            bulk_commit();
+          }
+        }
+        if (j + 1 < kSub) tmem_wait_ld(rn);
       }
-      if (j + 1 < kSub) tmem_wait_ld(rn);
+      tmem_st_wait();
     }
-    tmem_st_wait();
-    // merged with the other half of the row
+    // merged with the other half of the row: only the two warps of this lane quarter meet
     red[c.half * 128 + c.r] = mean;
     red[256 + c.half * 128 + c.r] = m2;
-    named_barrier(1, kEpilogueThreads);
+    named_barrier(1 + (c.r >> 5), 64);
+    if (!landed) {
+      c.failed = true;
+      return;
+    }
     const float m0 = red[c.r], m1 = red[128 + c.r];
     const float d = m1 - m0;
     mean = 0.5f * (m0 + m1);
     m2 = red[256 + c.r] + red[384 + c.r] + d * d * (kHidden / 4);
     const float rstd = rsqrtf(m2 * (1.0f / kHidden) + 1e-5f);
-    // h = (x - mean) rstd gamma + beta, staged where the x blocks were
-    if (c.lane == 0) bulk_wait_read<0>();  // the x stores have read the staging region
-    __syncwarp();
-    const float2 nm = make_float2(-mean, -mean), rs = make_float2(rstd, rstd);
+    // h = (x rstd - mean rstd) gamma + beta, staged where the x blocks were. Each output block
+    // overwrites a block whose store was committed three groups earlier (an x block, or for f32
+    // output the first round of f32 blocks), so waiting until at most two groups are still
+    // reading lets it go ahead.
+    const float2 nm = make_float2(-mean * rstd, -mean * rstd), rs = make_float2(rstd, rstd);
     uint32_t xa[16], xb[16];
     tmem_ld16(taddr, xa);
     tmem_ld_wait();
@@ -652,7 +660,7 @@ struct EpiResidLN {
         lds8(sv + 3 * kHidden + n0 + 32 * j + 8 * k, tt);
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const float2 z = __fmul2_rn(__fadd2_rn(unpack_half2(xr[4 * k + p]), nm), rs);
+          const float2 z = __ffma2_rn(unpack_half2(xr[4 * k + p]), rs, nm);
           const float2 v = __ffma2_rn(z, make_float2(gg[2 * p], gg[2 * p + 1]),
                                       make_float2(tt[2 * p], tt[2 * p + 1]));
           y[8 * k + 2 * p] = v.x;
@@ -661,6 +669,10 @@ struct EpiResidLN {
       }
       if (!f32_out) {
         uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
+        if (!(j & 1)) {
+          if (c.lane == 0) bulk_wait_read<2>();
+          __syncwarp();
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) = pack8(y, k);
@@ -674,10 +686,8 @@ struct EpiResidLN {
         }
       } else {
         // f32: 32 columns (128-byte rows, 128-byte swizzle) per block, three blocks at a time
-        if (j == 3) {
-          if (c.lane == 0) bulk_wait_read<0>();  // the first round's stores have read their blocks
-          __syncwarp();
-        }
+        if (c.lane == 0) bulk_wait_read<2>();
+        __syncwarp();
         uint8_t *blk = stage + (j % 3) * kF32Block;
         uint8_t *rowp = blk + c.lane * 128;
 #pragma unroll
