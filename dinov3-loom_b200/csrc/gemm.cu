@@ -95,6 +95,19 @@ struct NarrowOk<Epi, decltype(void(Epi::kNarrowOk))> {
   static constexpr bool value = Epi::kNarrowOk;
 };
 
+// Whether the epilogue warps write the bias into the (single) accumulator before the first MMA,
+// which then accumulates onto it (Epi::kBiasInTmem, one tile per CTA): the epilogue reads
+// acc + b from TMEM. The fill runs while the previous kernel finishes (before the dependency
+// wait).
+template <class Epi, class = void>
+struct BiasInTmem {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct BiasInTmem<Epi, decltype(void(Epi::kBiasInTmem))> {
+  static constexpr bool value = Epi::kBiasInTmem;
+};
+
 // Bytes of one epilogue warp's staging region in the tile buffers: Epi::kWarpStaging when it
 // exists.
 template <class Epi, class = void>
@@ -124,6 +137,8 @@ struct GemmCfg {
       Epi::kTmaStore && !kInTiles ? kEpilogueWarps * StagingBufs<Epi>::value * kStageBlockBytes : 0;
   static constexpr bool kInput = TmaInput<Epi>::value;
   static constexpr bool kEarly = EarlyInput<Epi>::value;
+  static constexpr bool kBiasInit = BiasInTmem<Epi>::value;
+  static_assert(!kBiasInit || (BN == 384 && kInTiles), "bias fill: one full-row tile per CTA");
   static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
   static constexpr int kFixed = 1024 + kStaging + kBarBytes + ((Epi::kSmem + 127) / 128) * 128;
   static constexpr int kFit = (227 * 1024 - kFixed) / kStage;
@@ -253,6 +268,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if constexpr (C::kBiasInit) {
+    // Each epilogue warp writes the bias into its lane quarter and column half of the
+    // accumulator; the MMAs of the CTA's one tile accumulate onto it.
+    if (warp >= 2) {
+      const int q = warp & 3, half = (warp - 2) >> 2;
+      epi.fill_acc(*tmem_slot + (static_cast<uint32_t>(q * 32) << 16) +
+                       static_cast<uint32_t>(half * (BN / 2)),
+                   extra, half);
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
   pdl_wait();  // activations of the previous kernel are complete from here on
   pdl_trigger();
   // an epilogue thread, idle until the first accumulator, starts the next weights toward L2
@@ -368,7 +397,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
               umma_f16(d + s * C::kMmaN, adesc + 2 * k, bdesc + 2 * k, idesc,
-                       (kb | k) != 0 ? 1u : 0u);
+                       C::kBiasInit || (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::kStages) {

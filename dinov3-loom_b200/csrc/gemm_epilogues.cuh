@@ -519,6 +519,7 @@ struct EpiResidLN {
   static constexpr bool kTmaInput = true;
   static constexpr bool kStagingInTiles = true;
   static constexpr bool kEarlyInput = true;
+  static constexpr bool kBiasInTmem = true;  // the accumulator starts at b (gemm_kernel fills it)
   static constexpr int kBlockBytes = 32 * 128;              // 32 rows x 64 f16 columns
   static constexpr int kInBlocks = 3;                       // per warp (192 columns)
   static constexpr int kWarpStaging = kInBlocks * kBlockBytes;
@@ -532,6 +533,23 @@ struct EpiResidLN {
     stage_floats(s + kHidden, lambda, kHidden, tid, n);
     stage_floats(s + 2 * kHidden, gamma, kHidden, tid, n);
     stage_floats(s + 3 * kHidden, beta, kHidden, tid, n);
+  }
+  // The bias of this warp's 192 columns into its 32 TMEM lanes (every lane the same row).
+  __device__ void fill_acc(uint32_t taddr, const uint8_t *smem, int half) const {
+    const float *b = reinterpret_cast<const float *>(smem) + half * (kHidden / 2);
+#pragma unroll
+    for (int j = 0; j < kSub; ++j) {
+      uint32_t r[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 v = reinterpret_cast<const float4 *>(b + 32 * j)[i / 4];
+        r[i] = __float_as_uint(v.x);
+        r[i + 1] = __float_as_uint(v.y);
+        r[i + 2] = __float_as_uint(v.z);
+        r[i + 3] = __float_as_uint(v.w);
+      }
+      tmem_st32(taddr + 32 * j, r);
+    }
   }
   // Eight consecutive floats of a staged vector (a shared-memory broadcast).
   __device__ static void lds8(const float *p, float (&v)[8]) {
@@ -551,7 +569,8 @@ struct EpiResidLN {
     // its partner warp at the barrier below, then reports the failure.
     const bool landed =
         __all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag));
-    // x = f16(x + lambda (acc + b)) in place; back into TMEM as packed f16; out by TMA. Each
+    // x = f16(x + lambda (acc + b)) in place (the accumulator started at b); back into TMEM as
+    // packed f16; out by TMA. Each
     // 32-column chunk's shared-memory loads come before its stores, so they issue together
     // instead of one 16-byte group at a time behind the previous group's store. The mean and the
     // centred sum of squares of this warp's 192 columns build up chunk by chunk from the stored
@@ -576,13 +595,11 @@ struct EpiResidLN {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t w[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
-          float bb[8], ll[8];
-          lds8(sv + n0 + 32 * j + 8 * k, bb);
+          float ll[8];
           lds8(sv + kHidden + n0 + 32 * j + 8 * k, ll);
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
-            const float2 a = make_float2(u2f(r[8 * k + 2 * p]), u2f(r[8 * k + 2 * p + 1]));
-            const float2 t = __fadd2_rn(a, make_float2(bb[2 * p], bb[2 * p + 1]));
+            const float2 t = make_float2(u2f(r[8 * k + 2 * p]), u2f(r[8 * k + 2 * p + 1]));
             const float2 v =
                 __ffma2_rn(make_float2(ll[2 * p], ll[2 * p + 1]), t, unpack_half2(w[p]));
             o[4 * k + p] = pack_half2(v.x, v.y);
