@@ -251,6 +251,24 @@ int dv3k_patch_embed(const uint16_t *patches, uint32_t n_patches, const uint16_t
   return gemm_entry(dv3::GemmOp::Patch, patches, n_patches, w, g, status, stream);
 }
 
+int dv3k_patch_embed_pixels(const float *images, uint32_t n_images, const uint16_t *w,
+                            const float *bias, const float *prefix, uint16_t *x, uint32_t *status,
+                            void *stream) {
+  if (n_images == 0) return DV3_OK;
+  if (!all_aligned(images, w, bias, prefix, x)) return bad_args("pointers must be 16-byte aligned");
+  const uint32_t rows = n_images * dv3::kPatches;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if ((rows + 127) / 128 > static_cast<uint32_t>(dv3::sm_count(dev)))
+    return bad_args("too many images for one wave of 128-patch tiles");
+  dv3::GemmArgs g;
+  g.bias = bias;
+  g.out = reinterpret_cast<__half *>(x);
+  g.images = images;
+  g.prefix = prefix;
+  return gemm_entry(dv3::GemmOp::PatchPixels, nullptr, rows, w, g, status, stream);
+}
+
 int dv3k_layernorm_f16(const uint16_t *x, uint32_t rows, const float *gamma, const float *beta,
                        uint16_t *out, void *stream) {
   if (!all_aligned(x, gamma, beta, out)) return bad_args("pointers must be 16-byte aligned");

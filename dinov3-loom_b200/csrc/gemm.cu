@@ -108,6 +108,18 @@ struct BiasInTmem<Epi, decltype(void(Epi::kBiasInTmem))> {
   static constexpr bool value = Epi::kBiasInTmem;
 };
 
+// Whether the epilogue warps build the A tiles from f32 NCHW images (Epi::kAFromPixels, the
+// fused patchify of the patch embedding) while the producer loads only the weights. One tile per
+// CTA: the epilogue warps are idle during its mainloop.
+template <class Epi, class = void>
+struct AFromPixels {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct AFromPixels<Epi, decltype(void(Epi::kAFromPixels))> {
+  static constexpr bool value = Epi::kAFromPixels;
+};
+
 // Bytes of one epilogue warp's staging region in the tile buffers: Epi::kWarpStaging when it
 // exists.
 template <class Epi, class = void>
@@ -138,7 +150,14 @@ struct GemmCfg {
   static constexpr bool kInput = TmaInput<Epi>::value;
   static constexpr bool kEarly = EarlyInput<Epi>::value;
   static constexpr bool kBiasInit = BiasInTmem<Epi>::value;
-  static_assert(!kBiasInit || (BN == 384 && kInTiles), "bias fill: one full-row tile per CTA");
+  static constexpr bool kAPix = AFromPixels<Epi>::value;
+  // configurations whose launches have exactly one tile per CTA
+  static constexpr bool kOneTile = kInTiles || kBiasInit || kAPix;
+  static_assert(!kBiasInit || BN == 384, "bias fill: one full-row tile per CTA");
+  static_assert(!kAPix || (kBiasInit && BN == 384), "pixel A tiles: one full-row tile per CTA");
+  // full-barrier arrivals per stage: the producer's (with the TMA bytes), and with kAPix one per
+  // epilogue warp once its rows of the A tile are written
+  static constexpr int kFullArrivals = kAPix ? 1 + kEpilogueWarps : 1;
   static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
   static constexpr int kFixed = 1024 + kStaging + kBarBytes + ((Epi::kSmem + 127) / 128) * 128;
   static constexpr int kFit = (227 * 1024 - kFixed) / kStage;
@@ -215,6 +234,76 @@ __device__ __forceinline__ void unit_coords(const TileSched &s, int u, int &m0, 
 }
 
 // ---------------------------------------------------------------------------------------------
+// The patchify of the patch embedding inside its mainloop (Epi::kAFromPixels). A[p][k] is pixel
+// (c, dy, dx) = (k / 256, k / 16 % 16, k % 16) of patch p (src/lib.rs:265-280), so the 64
+// columns of k-block kb are channel kb / 4, pixel rows 4 (kb % 4) .. + 3 of the patch, 16 pixels
+// each. Lane l of epilogue warp ew takes tile row 16 ew + l / 2 and two of those pixel rows
+// (l % 2): 32 floats as eight 16-byte loads, rounded to f16 like patchify and written as four
+// 16-byte chunks of the 128-byte-swizzled row (chunk j of row r at j ^ (r % 8)). The loads of
+// the next two k-blocks are issued before the wait for a free stage, so three k-blocks of pixel
+// reads are in flight per thread (the reads are latency-bound: HBM under the whole grid's load). Rows past `rows` are zeros. Any non-finite pixel sets status[1] bit 0,
+// the flag patchify sets. Returns false when a stage never frees (the kernel is aborting).
+// ---------------------------------------------------------------------------------------------
+template <class C>
+__device__ bool pixel_a_tiles(const float *images, int rows, int m0, int ew, int lane,
+                              uint8_t *tiles, uint64_t *full, uint64_t *empty, int k_blocks,
+                              volatile int *abort_flag, uint32_t *status) {
+  const int r = 16 * ew + (lane >> 1);
+  const int part = lane & 1;
+  const int p = m0 + r;
+  const bool valid = p < rows;
+  const int img = valid ? p / kPatches : 0, pp = valid ? p % kPatches : 0;
+  const float *base = images + static_cast<int64_t>(img) * 3 * kImage * kImage +
+                      (pp / 14) * 16 * kImage + (pp % 14) * 16 + 2 * part * kImage;
+  auto load = [&](int kb, float4 (&v)[8]) {
+    const float4 *src =
+        reinterpret_cast<const float4 *>(base + (kb >> 2) * kImage * kImage + (kb & 3) * 4 * kImage);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = valid ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 + i] = valid ? __ldg(src + kImage / 4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float4 cur[8], nxt[8], nxt2[8];
+  load(0, cur);
+  if (k_blocks > 1) load(1, nxt);
+  int stage = 0;
+  uint32_t phase = 0;
+  bool bad = false, ok = true;
+  for (int kb = 0; kb < k_blocks; ++kb) {
+    if (kb + 2 < k_blocks) load(kb + 2, nxt2);
+    if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag))) {
+      ok = false;
+      break;
+    }
+    uint8_t *row = tiles + stage * C::kStage + r * 128;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 a = cur[2 * j], b = cur[2 * j + 1];
+      bad |= !(isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w) &&
+               isfinite(b.x) && isfinite(b.y) && isfinite(b.z) && isfinite(b.w));
+      *reinterpret_cast<uint4 *>(row + (((4 * part + j) ^ (r & 7)) << 4)) =
+          make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
+                     pack_half2(b.z, b.w));
+    }
+    fence_proxy_async_smem();  // the MMA reads the tile through the async proxy
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&full[stage]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      cur[i] = nxt[i];
+      nxt[i] = nxt2[i];
+    }
+    if (++stage == C::kStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  if (__any_sync(0xffffffffu, bad) && lane == 0 && status) atomicOr(status + 1, 1u);
+  return ok;
+}
+
+// ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
 template <int BN, class Epi>
@@ -243,7 +332,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], C::kFullArrivals);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < C::kAccBufs; ++a) {
@@ -288,7 +377,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 64 && sched.l2_next) l2_prefetch_share(sched.l2_next, sched.l2_next_bytes);
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = sched.num_units;
-  if (C::kInTiles && num_tiles > static_cast<int>(gridDim.x)) {  // the host never launches this
+  if (C::kOneTile && num_tiles > static_cast<int>(gridDim.x)) {  // the host never launches this
     if (threadIdx.x == 0) report(status, kErrEpilogueWait);
     tc_fence_before();
     __syncthreads();
@@ -303,6 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      uint32_t armed = 0, last_parity = 0;  // per stage: loads issued, parity of the last phase
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int m0, n0, k_slice;
@@ -319,11 +409,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           uint8_t *a = tiles + stage * C::kStage;
-          mbar_arrive_expect_tx(&full[stage], C::kA + b_boxes * C::kBBox * BK * 2);
-          tma_load_2d(a, &tmA, &full[stage], (kb0 + kb) * BK, m0);
+          mbar_arrive_expect_tx(&full[stage], (C::kAPix ? 0 : C::kA) + b_boxes * C::kBBox * BK * 2);
+          if constexpr (!C::kAPix) tma_load_2d(a, &tmA, &full[stage], (kb0 + kb) * BK, m0);
           for (int s = 0; s < b_boxes; ++s)
             tma_load_2d(a + C::kA + s * C::kBBox * BK * 2, &tmB, &full[stage], (kb0 + kb) * BK,
                         n0 + s * C::kBBox);
+          armed |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -359,6 +451,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      // Copies still in flight (only after an abort) land before shared memory is released.
+      for (int st = 0; st < C::kStages; ++st)
+        if ((armed >> st) & 1u) mbar_drain(&full[st], (last_parity >> st) & 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -442,6 +537,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ctx.iter = 0;
     ctx.abort_flag = abort_flag;
     ctx.failed = false;
+    if constexpr (C::kAPix) {
+      // the CTA's one tile: this warp writes rows 16 (warp - 2) .. + 15 of each k-block's A tile
+      int m0, n0_unused, k_slice_unused;
+      bool narrow_unused;
+      unit_coords<BN>(sched, blockIdx.x, m0, n0_unused, narrow_unused, k_slice_unused);
+      if (!pixel_a_tiles<C>(epi.images, M, m0, warp - 2, lane, tiles, full, empty, k_blocks,
+                            abort_flag, status) &&
+          lane == 0) {
+        report(status, kErrProducerWait);
+        *abort_flag = 1;
+      }
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
     bool in_pending = false;  // input blocks requested for a tile not yet processed
@@ -565,6 +672,7 @@ GemmShape gemm_shape(GemmOp op) {
     case GemmOp::ResidLN384: return {384, kHidden, kHidden};
     case GemmOp::ResidLN1536: return {384, kHidden, kMlp};
     case GemmOp::SplitK1536: return {128, kHidden, kMlp};
+    case GemmOp::PatchPixels: return {384, kHidden, kPatchK};
   }
   return {0, 0, 0};
 }
@@ -579,6 +687,7 @@ const char *gemm_name(GemmOp op) {
     case GemmOp::ResidLN384: return "gemm_o_resid_layernorm";
     case GemmOp::ResidLN1536: return "gemm_down_resid_layernorm";
     case GemmOp::SplitK1536: return "gemm_down_splitk";
+    case GemmOp::PatchPixels: return "gemm_patch_pixels";
   }
   return "?";
 }
@@ -607,8 +716,10 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
       s.bn == 256 ||
       (s.bn == 128 && (op == GemmOp::Resid384 || op == GemmOp::Resid1536 || op == GemmOp::Patch));
   const uint32_t b_rows = s.bn >= 256 || narrow_ops ? s.bn / 2 : s.bn;
-  if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err) ||
-      !encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err))
+  if (!encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err)) return false;
+  if (op == GemmOp::PatchPixels)
+    maps->a = maps->b;  // no A map: the epilogue warps build the A tiles from the images
+  else if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err))
     return false;
   maps->d = maps->a;  // unused unless the epilogue writes a LayerNorm output
   if (op == GemmOp::SplitK1536)  // f32 partial slabs [splits][rows][384], 32x32 blocks
@@ -699,6 +810,7 @@ cudaError_t configure_gemm_kernels() {
   if ((e = configure_one<256, EpiSwiGLU>()) != cudaSuccess) return e;
   if ((e = configure_one<384, EpiResidLN>()) != cudaSuccess) return e;
   if ((e = configure_one<128, EpiPartialF32>()) != cudaSuccess) return e;
+  if ((e = configure_one<384, EpiPatchPixels>()) != cudaSuccess) return e;
   int dev = 0;
   cudaGetDevice(&dev);
   sm_count(dev);
@@ -736,6 +848,17 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
       if (args.splits == 0 || (kMlp / BK) % args.splits != 0) return cudaErrorInvalidValue;
       return launch_one<128>(maps, rows, s.n, s.k, EpiPartialF32{}, status, stream, args,
                              static_cast<int>(args.splits));
+    case GemmOp::PatchPixels: {
+      // one tile per CTA: at most one wave of 128-row tiles (96 images on 148 SMs)
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!args.images || !args.prefix || !args.out || rows % kPatches != 0 ||
+          (rows + BM - 1) / BM > static_cast<uint32_t>(sm_count(dev)))
+        return cudaErrorInvalidValue;
+      return launch_one<384>(maps, rows, s.n, s.k,
+                             EpiPatchPixels{args.bias, args.out, args.images, args.prefix},
+                             status, stream, args);
+    }
   }
   return cudaErrorInvalidValue;
 }

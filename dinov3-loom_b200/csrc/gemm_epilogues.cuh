@@ -130,6 +130,24 @@ __device__ __forceinline__ void store_half32(__half *dst, const float (&v)[32]) 
   for (int j = 0; j < 4; ++j) d[j] = pack8(v, j);
 }
 
+// The bias of 192 columns (`b`, in shared memory) into 32 TMEM lanes x 192 columns from `taddr`,
+// every lane the same row: the start value of a full-row accumulator (Epi::kBiasInTmem).
+__device__ __forceinline__ void fill_acc_bias192(uint32_t taddr, const float *b) {
+#pragma unroll
+  for (int j = 0; j < 6; ++j) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 v = reinterpret_cast<const float4 *>(b + 32 * j)[i / 4];
+      r[i] = __float_as_uint(v.x);
+      r[i + 1] = __float_as_uint(v.y);
+      r[i + 2] = __float_as_uint(v.z);
+      r[i + 3] = __float_as_uint(v.w);
+    }
+    tmem_st32(taddr + 32 * j, r);
+  }
+}
+
 // Emit this warp's 32 rows x 32 columns (f16 of v, one row per lane) at output column `col`
 // through a staging block and a TMA store.
 __device__ __forceinline__ void tma_emit32(EpiCtx &c, const float (&v)[32], int col) {
@@ -182,6 +200,65 @@ struct EpiPatch {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] += u2f(r[i]);
       if (ok) store_half32(x + static_cast<size_t>(token) * kHidden + n0 + k, v);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Patch embedding with the patchify fused into the mainloop (GemmOp::PatchPixels, full 384-wide
+// rows, one tile per CTA): the epilogue warps build the A tiles from the images while the
+// producer loads the weights (pixel_a_tiles in gemm.cu), and the accumulator starts at the bias.
+// The epilogue writes x[(p/196)*201 + 5 + p%196] = f16(acc) for its row's 192 columns, and the
+// thread of each image's first patch row also writes that image's 5 prefix rows (CLS and
+// register tokens, f16 of the f32 weights: the prefix half of kernels/embed_scatter_f32.loom).
+// ---------------------------------------------------------------------------------------------
+struct EpiPatchPixels {
+  const float *bias;
+  __half *x;
+  const float *images;
+  const float *prefix;
+  static constexpr int kSmem = kHidden * 4;
+  static constexpr bool kTmaStore = false;
+  static constexpr bool kBiasInTmem = true;
+  static constexpr bool kAFromPixels = true;
+  using Pre = NoPre;
+  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
+  __device__ void init(uint8_t *smem, int tid, int n) const {
+    stage_floats(reinterpret_cast<float *>(smem), bias, kHidden, tid, n);
+  }
+  __device__ void fill_acc(uint32_t taddr, const uint8_t *smem, int half) const {
+    fill_acc_bias192(taddr, reinterpret_cast<const float *>(smem) + half * (kHidden / 2));
+  }
+  template <int COLS>
+  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
+    static_assert(COLS == 192, "a column half of a full row");
+    const bool ok = c.row < c.M;
+    const int img = c.row / kPatches, pp = c.row % kPatches;
+    __half *dst = x + (static_cast<size_t>(img) * kTokens + kPrefix + pp) * kHidden + n0;
+    uint32_t ra[32], rb[32];
+    tmem_ld32(taddr, ra);
+#pragma unroll
+    for (int j = 0; j < COLS / 32; ++j) {
+      uint32_t(&r)[32] = (j & 1) ? rb : ra;
+      uint32_t(&rn)[32] = (j & 1) ? ra : rb;
+      tmem_wait_ld(r);
+      if (j + 1 < COLS / 32) tmem_ld32(taddr + 32 * (j + 1), rn);
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = u2f(r[i]);
+      if (ok) store_half32(dst + 32 * j, v);
+    }
+    if (ok && pp == 0) {
+      __half *pre_dst = x + static_cast<size_t>(img) * kTokens * kHidden + n0;
+#pragma unroll 1
+      for (int t = 0; t < kPrefix; ++t) {
+#pragma unroll
+        for (int j = 0; j < COLS / 32; ++j) {
+          float v[32];
+          ldg32(prefix + t * kHidden + n0 + 32 * j, v);
+          store_half32(pre_dst + t * kHidden + 32 * j, v);
+        }
+      }
     }
   }
 };
@@ -536,20 +613,7 @@ struct EpiResidLN {
   }
   // The bias of this warp's 192 columns into its 32 TMEM lanes (every lane the same row).
   __device__ void fill_acc(uint32_t taddr, const uint8_t *smem, int half) const {
-    const float *b = reinterpret_cast<const float *>(smem) + half * (kHidden / 2);
-#pragma unroll
-    for (int j = 0; j < kSub; ++j) {
-      uint32_t r[32];
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 v = reinterpret_cast<const float4 *>(b + 32 * j)[i / 4];
-        r[i] = __float_as_uint(v.x);
-        r[i + 1] = __float_as_uint(v.y);
-        r[i + 2] = __float_as_uint(v.z);
-        r[i + 3] = __float_as_uint(v.w);
-      }
-      tmem_st32(taddr + 32 * j, r);
-    }
+    fill_acc_bias192(taddr, reinterpret_cast<const float *>(smem) + half * (kHidden / 2));
   }
   // Eight consecutive floats of a staged vector (a shared-memory broadcast).
   __device__ static void lds8(const float *p, float (&v)[8]) {

@@ -19,7 +19,8 @@ constexpr int kQkv = 1152;
 constexpr int kMlp = 1536;
 constexpr int kGateUp = 3072;
 constexpr int kPatchK = 768;
-constexpr int kImageElements = 3 * 224 * 224;
+constexpr int kImage = 224;  // image side in pixels
+constexpr int kImageElements = 3 * kImage * kImage;
 
 // ---- tensor maps (tma.cpp) ----
 // 2D f16 tensor [rows][cols] (row-major, `cols` contiguous), box = box_cols x box_rows, 128-byte
@@ -50,8 +51,22 @@ bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uin
 // rows, followed in the same kernel by the LayerNorm of the updated row into ln_out (f16) or
 // ln_out_f32. SplitK1536: the down projection's K split into `splits` slices, each CTA writing
 // the f32 partial product of its slice (no bias) into slab s of partials [splits][rows][384]
-// (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it.
-enum class GemmOp { Patch, QkvRope, Resid384, Resid1536, SwiGLU, ResidLN384, ResidLN1536, SplitK1536 };
+// (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it. PatchPixels: the patch
+// embedding with the patchify fused into its A operand: the epilogue warps build each A tile from
+// the f32 NCHW images (`images`, f16 rounding as patchify, non-finite pixels flagged in
+// status[1]) while the producer loads only the weights; full 384-wide rows, one tile per CTA; the
+// epilogue writes the patch rows and each image's prefix rows (`prefix`) of x.
+enum class GemmOp {
+  Patch,
+  QkvRope,
+  Resid384,
+  Resid1536,
+  SwiGLU,
+  ResidLN384,
+  ResidLN1536,
+  SplitK1536,
+  PatchPixels
+};
 
 struct GemmShape {
   int bn;      // tile width along N
@@ -73,7 +88,9 @@ struct GemmMaps {
   CUtensorMap c;  // the epilogue's output, for epilogues that store through TMA
   CUtensorMap d;  // ResidLN*: the LayerNorm output (f16 h, or the f32 final output)
 };
-// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch). ResidLN* also takes
+// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch and PatchPixels, which
+// write x through GemmArgs). PatchPixels takes no `a` (null): its A operand comes from the images.
+// ResidLN* also takes
 // the LayerNorm output: `ln_out` f16 [rows][384], or f32 when `ln_f32`.
 // SplitK1536: `out` is the f32 partials [splits][rows][384].
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
@@ -91,6 +108,8 @@ struct GemmArgs {
   __half *ln_out = nullptr;      // ResidLN*: f16 LayerNorm output, or
   float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
   float *partials = nullptr;     // SplitK1536: [splits][rows][384] f32
+  const float *images = nullptr;  // PatchPixels: f32 NCHW images, rows / 196 of them
+  const float *prefix = nullptr;  // PatchPixels: the 5 prefix rows (CLS, registers) f32 [5][384]
   uint32_t splits = 1;           // SplitK1536: K slices (a divisor of 24, the 64-wide k-blocks)
   // Weights of a later kernel (16-byte aligned; no kernel writes them) that this launch starts
   // toward L2, so that kernel's first tiles do not wait for DRAM.

@@ -210,15 +210,16 @@ void Model::release() {
   cudaGetLastError();
 }
 
-// The launch plan of one batch size (src/lib.rs:149-263): patchify, patch GEMM (with the
-// embed scatter), LN1 of layer 0, then per layer QKV+RoPE, attention, o-proj+LS1+residual+LN2,
-// gate/up+SwiGLU, and down-proj+LS2+residual+(LN1 of the next layer | final LN). The reference
-// launches each LayerNorm separately (87 launches at b > 1); here each one after layer 0's
-// first rides in the epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches),
-// whenever the residual GEMMs run on full rows (large batches; see resid_wide); small batches
-// keep 128-wide residual tiles and separate LayerNorm launches (3 + 12*7 = 87).
-// DV3_FUSE_LAYERNORM=0 in the environment restores the separate LayerNorm launches (3 + 12*7 =
-// 87, the reference's plan) for comparison; =1 forces fusion.
+// The launch plan of one batch size (src/lib.rs:149-263): patchify, the patch GEMM (with the
+// embed scatter; or both in one launch, PatchPixels, with DV3_FUSE_PATCHIFY=1), LN1 of layer 0,
+// then per layer QKV+RoPE, attention, o-proj+LS1+residual+LN2, gate/up+SwiGLU, and
+// down-proj+LS2+residual+(LN1 of the next layer | final LN). The reference launches each
+// LayerNorm separately (87 launches at b > 1); here each one after layer 0's first rides in the
+// epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches), whenever the
+// residual GEMMs run on full rows (large batches; see resid_wide); small batches keep 128-wide
+// residual tiles and separate LayerNorm launches (3 + 12*7 = 87).
+// DV3_FUSE_LAYERNORM=0 in the environment restores the separate LayerNorm launches (the
+// reference's plan) for comparison; =1 forces fusion.
 // K slices of the down projection at this batch size (1: unsplit). DV3_SPLITK=0 in the
 // environment turns the split off for comparison.
 uint32_t Model::down_splits(uint32_t rows) const {
@@ -230,6 +231,17 @@ uint32_t Model::down_splits(uint32_t rows) const {
 bool Model::fuse_layernorm(size_t b) const {
   if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
   return resid_wide(static_cast<uint32_t>(kTokens * b));
+}
+
+// Whether the patch GEMM builds its A tiles from the images itself (GemmOp::PatchPixels: one
+// launch instead of patchify + patch GEMM, no f16 patch matrix in memory). Off unless
+// DV3_FUSE_PATCHIFY=1: its one full-row tile per CTA (98 CTAs at batch 64, 2 at batch 1) waits
+// on pixel reads that patchify streams at full bandwidth, and measured slower at every batch
+// size tried (batch 64: 1.189 against 1.184 ms per forward; batch 1: 0.400 against 0.382 ms).
+bool Model::fuse_patchify(size_t b) const {
+  if (const char *v = std::getenv("DV3_FUSE_PATCHIFY")) return v[0] == '1';
+  (void)b;
+  return false;
 }
 
 // Bytes of each projection's f16 weights. Each launch of the plan starts the weights of a GEMM
@@ -261,22 +273,27 @@ Plan &Model::prepare(size_t b, int slot) {
   float *image = image_slot_[slot], *out = out_slot_[slot];
   __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
 
+  const bool pix = fuse_patchify(b);
+  const GemmOp patch_op = pix ? GemmOp::PatchPixels : GemmOp::Patch;
   GemmMaps patch_maps;
-  need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, x, &patch_maps, &err));
+  need(make_gemm_maps(patch_op, patches, p, w.patch_w, x, &patch_maps, &err));
   AttentionMaps attn_map;
   need(make_attention_map(qkv, attn, r, &attn_map, &err));
 
-  add("patchify", [=](cudaStream_t s) {
-    return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s, w.patch_w,
-                           size_t{kHidden} * kPatchK * 2);
-  });
-  add(gemm_name(GemmOp::Patch), [=](cudaStream_t s) {
+  if (!pix)
+    add("patchify", [=](cudaStream_t s) {
+      return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s,
+                             w.patch_w, size_t{kHidden} * kPatchK * 2);
+    });
+  add(gemm_name(patch_op), [=](cudaStream_t s) {
     GemmArgs g;
     g.l2_next = w.layer[0].qkv_w;
     g.l2_next_bytes = kQkvWBytes;
     g.bias = w.patch_b;
     g.out = x;
-    return launch_gemm(GemmOp::Patch, patch_maps, p, g, st, s);
+    g.images = image;    // PatchPixels
+    g.prefix = w.prefix;
+    return launch_gemm(patch_op, patch_maps, p, g, st, s);
   });
   add("layernorm_f16", [=](cudaStream_t s) {
     return launch_layernorm_f16(x, r, w.layer[0].norm1_w, w.layer[0].norm1_b, h, s);

@@ -76,6 +76,7 @@ SIGNATURES = {
     # dinov3_kernels.h
     "dv3k_patchify": ([_P, _U32, _P, _P, _P, _P, _P], _I),
     "dv3k_patch_embed": ([_P, _U32, _P, _P, _P, _P, _P], _I),
+    "dv3k_patch_embed_pixels": ([_P, _U32, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_layernorm_f16": ([_P, _U32, _P, _P, _P, _P], _I),
     "dv3k_layernorm_f32out": ([_P, _U32, _P, _P, _P, _P], _I),
     "dv3k_qkv_rope": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P], _I),

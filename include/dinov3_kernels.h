@@ -15,8 +15,8 @@
  *     rows == 0 launches nothing and returns 0.
  *   - `status` is an optional device array of two uint32_t words (NULL allowed). Word 0
  *     collects device-side failure bits (a bounded wait that expired; the kernel then exits
- *     without finishing). Word 1 is set nonzero by dv3k_patchify when an input value is not
- *     finite. The caller clears and reads them.
+ *     without finishing). Word 1 is set nonzero by dv3k_patchify and dv3k_patch_embed_pixels
+ *     when an input value is not finite. The caller clears and reads them.
  *   - `stream` is a cudaStream_t (NULL: the legacy default stream). Launches are asynchronous.
  *   - Return value: 0, DV3_INVALID_ARGUMENT (shape/alignment) or DV3_DEVICE (launch failed),
  *     with the message in dv3_last_error().
@@ -59,6 +59,15 @@ int dv3k_patchify(const float *images, uint32_t n_images, const float *prefix, u
  * with f32 accumulation, for p < n_patches. */
 int dv3k_patch_embed(const uint16_t *patches, uint32_t n_patches, const uint16_t *w,
                      const float *bias, uint16_t *x, uint32_t *status, void *stream);
+
+/* dv3k_patchify and dv3k_patch_embed in one kernel (the device patchify fused into the patch
+ * GEMM's A loader): the same x rows, bit for bit, including the prefix rows, and the same
+ * status[1] flag for non-finite pixels, without the f16 patch matrix in memory. Full 384-wide
+ * rows, one 128-patch tile per CTA: n_images * 196 patch rows must fit one wave of tiles
+ * (n_images <= 96 on a 148-SM B200). */
+int dv3k_patch_embed_pixels(const float *images, uint32_t n_images, const uint16_t *w,
+                            const float *bias, const float *prefix, uint16_t *x, uint32_t *status,
+                            void *stream);
 
 /* LayerNorm over 384 channels, eps 1e-5, f16 -> f16. Replaces
  * kernels/layernorm_rowwave_f16.loom. */

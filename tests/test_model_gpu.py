@@ -269,6 +269,32 @@ def test_split_k_plan(weights_file, monkeypatch):
         assert cos(split[i], plain[i]) > 0.99999
 
 
+@pytest.mark.parametrize("b", [1, 64])
+def test_fused_patchify_plan(weights_file, monkeypatch, b):
+    """The default plan runs patchify and the patch GEMM as two launches; DV3_FUSE_PATCHIFY=1
+    (read when a batch size's graph is built) makes the patch GEMM build its A tiles from the
+    images in one launch. Both give the same result within the bias's position in the f32 sum,
+    and the fused launch flags a non-finite pixel like patchify."""
+    path = weights_file(1, "stress")
+    images = synth.images(44, b)
+    with dv.DINOv3.load(path, dv.Options(0, b)) as model:
+        names = [n for n, _ in model.profile_launches(b, 1)]
+        assert names[:2] == ["patchify", "gemm_patch_embed"]
+        plain = model.forward(images)
+    monkeypatch.setenv("DV3_FUSE_PATCHIFY", "1")
+    with dv.DINOv3.load(path, dv.Options(0, b)) as model:
+        names = [n for n, _ in model.profile_launches(b, 1)]
+        assert names[0] == "gemm_patch_pixels" and "patchify" not in names
+        fused = model.forward(images)
+        bad = images.copy()
+        bad[b - 1, 0, 17, 200] = np.inf
+        with pytest.raises(dv.DINOv3Error, match="finite"):
+            model.forward(bad)
+        np.testing.assert_array_equal(model.forward(images), fused)  # still usable, bitwise
+    for i in range(b):
+        assert cos(fused[i], plain[i]) > 0.99999
+
+
 def test_submit_wait_serving_path(models):
     """Serving path (dv3_submit / dv3_wait): submissions of changing size, two in flight and a
     third that first completes the oldest, waited out of order, give exactly the synchronous
