@@ -7,6 +7,8 @@
 //   ResidLN*  the same on full rows, then LayerNorm        + kernels/layernorm_rowwave_*.loom
 //   SwiGLU    act = f16(silu(A Wg^T + bg) (A Wu^T + bu))   kernels/matmul_swiglu_f16_wmma.loom
 //   SplitK    partials[s] = A[:, K_s] W[:, K_s]^T (f32)     kernels/matmul_splitk_f16_wmma.loom
+//   PatchPixels  Patch with A built from the f32 images    + the patchify of src/lib.rs:265-280
+//                in the mainloop (pixel_a_tiles)
 //
 // Layout: A [M][K] f16 activations and W [N][K] f16 weights, both K-major, are streamed by TMA
 // in 128-row x 64-column boxes with the 128-byte swizzle into a ring of shared-memory stages.
