@@ -257,9 +257,7 @@ int dv3k_patch_embed_pixels(const float *images, uint32_t n_images, const uint16
   if (n_images == 0) return DV3_OK;
   if (!all_aligned(images, w, bias, prefix, x)) return bad_args("pointers must be 16-byte aligned");
   const uint32_t rows = n_images * dv3::kPatches;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if ((rows + 127) / 128 > static_cast<uint32_t>(dv3::sm_count(dev)))
+  if ((rows + 127) / 128 > static_cast<uint32_t>(dv3::sm_count(current_device())))
     return bad_args("too many images for one wave of 128-patch tiles");
   dv3::GemmArgs g;
   g.bias = bias;

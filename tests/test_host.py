@@ -156,6 +156,11 @@ def test_kernel_entry_points_check_arguments_without_launching():
     assert rc == dv.INVALID_ARGUMENT and "multiple of 201" in _lib.last_error()
     rc = lib.dv3k_layernorm_f16(base + 2, 8, base, base, base, None)
     assert rc == dv.INVALID_ARGUMENT and "aligned" in _lib.last_error()
+    assert lib.dv3k_patch_embed_pixels(None, 0, None, None, None, None, None, None) == 0
+    rc = lib.dv3k_patch_embed_pixels(base + 4, 1, base, base, base, base, None, None)
+    assert rc == dv.INVALID_ARGUMENT and "aligned" in _lib.last_error()
+    rc = lib.dv3k_patch_embed_pixels(base, 100, base, base, base, base, None, None)
+    assert rc == dv.INVALID_ARGUMENT and "one wave" in _lib.last_error()
 
 
 def test_null_model_is_an_error():
