@@ -209,6 +209,25 @@ def test_mid_size_batch_plans(models, oracles, b):
     np.testing.assert_array_equal(model.forward(images), out)
 
 
+def test_every_batch_size_matches_single_images(models, oracles):
+    """Every resident batch size 1..64 (each crosses its own mix of plan variants: split-K down
+    projection up to 15 images, one attention CTA per query tile up to 12, narrow GEMM units,
+    full-row residual+LayerNorm GEMMs from 48): each image of a batch matches that image's
+    single-image forward, and two images of the largest batch match the float64 oracle."""
+    model = models("stress", max_batch=64)
+    images = synth.images(4096, 64)
+    single = np.stack([model.forward(images[i:i + 1])[0] for i in range(64)])
+    for b in range(1, 65):
+        out = model.forward(images[:b])
+        assert np.isfinite(out).all(), f"batch {b}"
+        for i in range(b):
+            assert cos(out[i], single[i]) > 0.99999, f"batch {b} image {i}"
+            assert cos(out[i][0], single[i][0]) > 0.99999, f"batch {b} image {i} CLS"
+    want = oracles("stress").forward(images[[0, 63]], threads=0)
+    for got, ref in zip(out[[0, 63]], want):
+        assert cos(got, ref) > 0.9999 and np.abs(got - ref).max() < MAX_ABS
+
+
 def test_benchmark_and_profile(models):
     model = models("baseline", max_batch=4)
     images = synth.images(3, 2)
