@@ -112,6 +112,20 @@ def test_valid_weights_reach_the_device_check(weights_file):
     assert e.value.code == dv.DEVICE
 
 
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+def test_low_precision_checkpoints_pack(weights_file_lowp, dtype):
+    """src/weights.rs:19-51 accepts F16 and BF16 tensors: a complete file of either packs without
+    error; without a GPU the load then stops at the device."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    low, _ = weights_file_lowp(dtype)
+    with pytest.raises(dv.DINOv3Error) as e:
+        dv.DINOv3.load(low, dv.Options())
+    assert e.value.code == dv.DEVICE
+
+
 def test_packing_preserves_finite_values_at_float16_limits():
     """src/weights.rs:148-169: 65519 rounds to 65504; -0 keeps its sign."""
     out = dv.pack_f16("weights", [0.0, -0.0, 1.0, -1.0, 65504.0, -65504.0, 65519.0, -65519.0])

@@ -228,6 +228,20 @@ def test_every_batch_size_matches_single_images(models, oracles):
         assert cos(got, ref) > 0.9999 and np.abs(got - ref).max() < MAX_ABS
 
 
+@pytest.mark.parametrize("dtype", ["F16", "BF16"])
+def test_low_precision_checkpoint_forward(weights_file_lowp, dtype):
+    """An F16 or BF16 checkpoint packs to the same device weights as an F32 file holding the same
+    values, so the forwards agree bit for bit (src/weights.rs:19-51)."""
+    low, f32 = weights_file_lowp(dtype)
+    images = synth.images(77, 3)
+    with dv.DINOv3.load(low, dv.Options(0, 4)) as model:
+        got = model.forward(images)
+    with dv.DINOv3.load(f32, dv.Options(0, 4)) as model:
+        want = model.forward(images)
+    assert np.isfinite(got).all()
+    np.testing.assert_array_equal(got, want)
+
+
 def test_benchmark_and_profile(models):
     model = models("baseline", max_batch=4)
     images = synth.images(3, 2)
