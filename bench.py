@@ -240,35 +240,18 @@ def run_ours(args):
 
     import dinov3_b200 as dv
     from dinov3_b200 import synth
+    from dinov3_b200.replicas import Replicas
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-
-    def barrier():
-        if dist is not None:
-            t = torch.zeros(1, device="cuda")
-            dist.all_reduce(t)
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    # one replica per GPU; NCCL only for the barriers around timed regions and the max over ranks
+    reps = Replicas("nccl", timeout_s=120)
+    barrier, max_over_ranks = reps.barrier, reps.max
 
     wdir = tempfile.mkdtemp(prefix=f"dv3_bench_{rank}_")
     wpath = synth.write_weights(os.path.join(wdir, "w.safetensors"), seed=0, flavor="baseline")
     model = dv.DINOv3.load(wpath, dv.Options(local, BATCH))
-    images = synth.images(1000 + rank * BATCH, BATCH)
+    images = synth.images(1000, BATCH, first=reps.first_image(BATCH))  # this rank's slice
     stream = torch.cuda.ExternalStream(model.stream, device=torch.device("cuda", local))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     n_img = BATCH * 3 * 224 * 224
@@ -282,7 +265,7 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     if args.serve:
-        run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist)
+        run_serving(args, model, images, reps)
         return
 
     if args.forward_only:
@@ -316,7 +299,7 @@ def run_ours(args):
         barrier()
     total_ms = sum(s.elapsed_time(e) for s, e in ev)
     total_ms = max_over_ranks(total_ms)
-    value = world * BATCH * args.steps / (total_ms / 1000.0)
+    value = reps.throughput(BATCH * args.steps, total_ms / 1000.0)
 
     # ---- end to end through the public API (pinned host buffers) ----
     pin_in = torch.from_numpy(images).pin_memory()
@@ -335,7 +318,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_sync_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev2))
-    e2e_sync = world * BATCH * e2e_steps / (e2e_sync_ms / 1000.0)
+    e2e_sync = reps.throughput(BATCH * e2e_steps, e2e_sync_ms / 1000.0)
     assert np.isfinite(pin_out.numpy()).all()
 
     # ---- end to end, pipelined through the serving API (dv3_submit / dv3_wait) ----
@@ -367,7 +350,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0)
     barrier()
-    e2e_value = world * BATCH * e2e_steps / (e2e_ms / 1000.0)
+    e2e_value = reps.throughput(BATCH * e2e_steps, e2e_ms / 1000.0)
     assert all(np.isfinite(o.numpy()).all() for o in pins_out)
 
     # ---- batch-1 latency (p50), device-resident and end to end ----
@@ -450,12 +433,10 @@ def run_ours(args):
             "wall_s_timed_region": wall,
         }
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        barrier()
-        dist.destroy_process_group()
+    reps.close()
 
 
-def run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist):
+def run_serving(args, model, images, reps):
     """each rank serves its share of `--serve-images` images in calls of seeded
     uniform random size 1..64, from pinned host memory into pinned host memory, timed on the
     host clock per call. Two passes: synchronous dv3_forward per call, then dv3_submit with two
@@ -464,8 +445,10 @@ def run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist)
     import numpy as np
     import torch
 
+    rank, world = reps.rank, reps.world
+    barrier, max_over_ranks = reps.barrier, reps.max
     rng = np.random.default_rng(4 + rank)
-    share = args.serve_images // world
+    share = reps.share(args.serve_images)
     sizes = []
     while sum(sizes) < share:
         sizes.append(int(min(rng.integers(1, BATCH + 1), share - sum(sizes))))
@@ -504,7 +487,7 @@ def run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist)
                 lat.append((time.perf_counter() - ts) * 1000)
         wall = time.perf_counter() - t_start
         wall_max = max_over_ranks(wall)
-        results[mode] = {"images_per_s": share * world / wall_max,
+        results[mode] = {"images_per_s": args.serve_images / wall_max,
                          "p50_ms": percentile(lat, 50), "p99_ms": percentile(lat, 99),
                          "calls_per_gpu": len(sizes), "wall_s": wall_max}
     if rank == 0:
@@ -514,12 +497,10 @@ def run_serving(args, model, images, rank, world, barrier, max_over_ranks, dist)
             "higher_is_better": True, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "BASELINE config 4: seeded uniform call sizes 1..64, pinned host "
                                    "buffers in and out, every call's full output read back",
-                       "images": share * world, "parallelism": f"replicas{world}"},
+                       "images": args.serve_images, "parallelism": f"replicas{world}"},
             "sync": results["sync"], "pipelined": results["pipelined"]}), flush=True)
     model.close()
-    if dist is not None:
-        barrier()
-        dist.destroy_process_group()
+    reps.close()
 
 
 def main():
