@@ -416,6 +416,34 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
                     status, stream);
 }
 
+int dv3k_down_layernorm_qkv(const uint16_t *act, uint32_t rows, const uint16_t *down_w,
+                            const float *down_b, const float *lambda, uint16_t *x,
+                            const float *gamma, const float *beta, const uint16_t *qkv_w,
+                            const float *qkv_b, const float *rope_cos, const float *rope_sin,
+                            uint16_t *qkv, uint32_t *status, void *stream) {
+  if (rows == 0) return DV3_OK;
+  if (!all_aligned(act, down_w, down_b, lambda, x, gamma, beta, qkv_w, qkv_b, rope_cos, rope_sin,
+                   qkv))
+    return bad_args("pointers must be 16-byte aligned");
+  if (rows % dv3::kTokens != 0) return bad_args("rows must be a multiple of 201");
+  if (rows > 128u * static_cast<uint32_t>(dv3::sm_count(current_device())))
+    return bad_args("rows must fit one 128-row tile per SM");
+  dv3::DownQkvMaps maps;
+  std::string err;
+  if (!dv3::make_down_qkv_maps(act, rows, down_w, x, qkv_w, qkv, &maps, &err))
+    return bad_args(err.c_str());
+  dv3::GemmArgs d, q;
+  d.bias = down_b;
+  d.lambda = lambda;
+  d.gamma = gamma;
+  d.beta = beta;
+  q.bias = qkv_b;
+  q.rope_cos = rope_cos;
+  q.rope_sin = rope_sin;
+  return launch_status(dv3::launch_down_qkv(maps, rows, d, q, status, static_cast<cudaStream_t>(stream)),
+                       "gemm_down_ln_qkv");
+}
+
 int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_w,
                        const float *gateup_b, uint16_t *act, uint32_t *status, void *stream) {
   if (!all_aligned(h, gateup_w, gateup_b, act)) return bad_args("pointers must be 16-byte aligned");

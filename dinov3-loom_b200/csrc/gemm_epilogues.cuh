@@ -62,6 +62,8 @@ struct EpiCtx {
   uint32_t iter;       // tiles this warp has processed (input-block barrier parity)
   volatile int *abort_flag;
   bool failed;         // a bounded wait expired inside run()
+  uint8_t *blocks[3];  // EpiResidLN: this warp's three 4 KB staging blocks
+  bool h_in_smem;      // EpiResidLN: h stays in the staging blocks (the fused QKV reads it)
 };
 
 struct NoPre {};
@@ -601,7 +603,6 @@ struct EpiResidLN {
   static constexpr int kInBlocks = 3;                       // per warp (192 columns)
   static constexpr int kWarpStaging = kInBlocks * kBlockBytes;
   static constexpr int kSub = 6;                            // 32-column accumulator chunks
-  static constexpr int kF32Block = 32 * 128;                // 32 rows x 32 f32 columns
   using Pre = NoPre;
   __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
   __device__ void init(uint8_t *smem, int tid, int n) const {
@@ -628,11 +629,11 @@ struct EpiResidLN {
     const float *sv = reinterpret_cast<const float *>(c.smem);
     float *red = const_cast<float *>(sv) + kVecs;  // [0..255] means, [256..511] M2
     const int sw = c.lane & 7;
-    uint8_t *const stage = c.staging;
-    // A warp whose residual never lands (the kernel is aborting) skips its work but still meets
-    // its partner warp at the barrier below, then reports the failure.
+    // A warp whose accumulator (c.failed on entry) or residual never arrives (the kernel is
+    // aborting) skips its work but still meets its partner warp at the barrier below, then
+    // reports the failure.
     const bool landed =
-        __all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag));
+        !c.failed && __all_sync(0xffffffffu, mbar_wait(&c.in_bar[0], c.iter & 1u, c.abort_flag));
     // x = f16(x + lambda (acc + b)) in place (the accumulator started at b); back into TMEM as
     // packed f16; out by TMA. Each
     // 32-column chunk's shared-memory loads come before its stores, so they issue together
@@ -649,7 +650,7 @@ struct EpiResidLN {
         uint32_t(&r)[32] = (j & 1) ? rb : ra;
         uint32_t(&rn)[32] = (j & 1) ? ra : rb;
         if (j + 1 < kSub) tmem_ld32(taddr + 32 * (j + 1), rn);
-        uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
+        uint8_t *rowp = c.blocks[j >> 1] + c.lane * 128;
         uint4 q[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -698,7 +699,7 @@ struct EpiResidLN {
           fence_proxy_async_smem();
           __syncwarp();
           if (c.lane == 0) {
-            tma_store_2d(c.out_map, stage + (j >> 1) * kBlockBytes, n0 + 64 * (j >> 1), c.row0);
+            tma_store_2d(c.out_map, c.blocks[j >> 1], n0 + 64 * (j >> 1), c.row0);
             bulk_commit();
           }
         }
@@ -749,19 +750,22 @@ struct EpiResidLN {
         }
       }
       if (!f32_out) {
-        uint8_t *rowp = stage + (j >> 1) * kBlockBytes + c.lane * 128;
-        if (!(j & 1)) {
-          if (c.lane == 0) bulk_wait_read<2>();
+        uint8_t *rowp = c.blocks[j >> 1] + c.lane * 128;
+        if (!(j & 1)) {  // with h kept in shared memory no h stores join the groups: wait for all
+          if (c.lane == 0) {
+            if (c.h_in_smem) bulk_wait_read<0>();
+            else bulk_wait_read<2>();
+          }
           __syncwarp();
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) = pack8(y, k);
-        if (j & 1) {
+        if ((j & 1) && !c.h_in_smem) {
           fence_proxy_async_smem();
           __syncwarp();
           if (c.lane == 0) {
-            tma_store_2d(c.ln_map, stage + (j >> 1) * kBlockBytes, n0 + 64 * (j >> 1), c.row0);
+            tma_store_2d(c.ln_map, c.blocks[j >> 1], n0 + 64 * (j >> 1), c.row0);
             bulk_commit();
           }
         }
@@ -769,7 +773,7 @@ struct EpiResidLN {
         // f32: 32 columns (128-byte rows, 128-byte swizzle) per block, three blocks at a time
         if (c.lane == 0) bulk_wait_read<2>();
         __syncwarp();
-        uint8_t *blk = stage + (j % 3) * kF32Block;
+        uint8_t *blk = c.blocks[j % 3];  // three 4 KB f32 blocks at a time
         uint8_t *rowp = blk + c.lane * 128;
 #pragma unroll
         for (int k = 0; k < 8; ++k)

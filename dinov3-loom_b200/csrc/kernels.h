@@ -117,6 +117,19 @@ struct GemmArgs {
   size_t l2_next_bytes = 0;
 };
 
+// The down projection of one layer with its residual update and the next layer's LN1, then that
+// layer's QKV GEMM with RoPE on the LayerNorm's rows, in one kernel (one 128-row tile per CTA,
+// h kept in shared memory; at most one wave of tiles). `down`: bias, lambda, gamma, beta of the
+// residual + LayerNorm (x updated in place); `qkv`: bias, rope_cos, rope_sin. Maps: act
+// [rows][1536], down_w [384][1536], x [rows][384], qkv_w [1152][384], qkv [rows][1152].
+struct DownQkvMaps {
+  CUtensorMap a, b, x, w, qkv;
+};
+bool make_down_qkv_maps(const void *act, uint32_t rows, const void *down_w, void *x,
+                        const void *qkv_w, void *qkv, DownQkvMaps *maps, std::string *err);
+cudaError_t launch_down_qkv(const DownQkvMaps &maps, uint32_t rows, const GemmArgs &down,
+                            const GemmArgs &qkv, uint32_t *status, cudaStream_t stream);
+
 // The K split of the down projection over `rows` rows in the model's plan: the most slices (at
 // most 8, a divisor of 24, so each CTA walks at least three 64-wide k-blocks) whose
 // 128x128 partial tiles still fit one wave of CTAs; 1 means no split (the unsplit residual

@@ -233,6 +233,17 @@ bool Model::fuse_layernorm(size_t b) const {
   return resid_wide(static_cast<uint32_t>(kTokens * b));
 }
 
+// Whether each down projection (layers 0-10, full-row plans only) also runs the next layer's QKV
+// GEMM on the LayerNorm rows it keeps in shared memory (launch_down_qkv: one launch instead of
+// two, h not written; bit for bit the same output). Off unless DV3_FUSE_QKV=1: its QKV phase
+// follows the LayerNorm serially on 101 CTAs with three 32 KB weight stages, and the batch-64
+// forward measured 1.246 against 1.189 ms.
+bool Model::fuse_qkv(size_t b) const {
+  if (!fuse_layernorm(b)) return false;
+  if (const char *v = std::getenv("DV3_FUSE_QKV")) return v[0] == '1';
+  return false;
+}
+
 // Whether the patch GEMM builds its A tiles from the images itself (GemmOp::PatchPixels: one
 // launch instead of patchify + patch GEMM, no f16 patch matrix in memory). Off unless
 // DV3_FUSE_PATCHIFY=1: its one full-row tile per CTA (98 CTAs at batch 64, 2 at batch 1) waits
@@ -306,9 +317,13 @@ Plan &Model::prepare(size_t b, int slot) {
   // reference splits K at batch 1, src/lib.rs:218-226).
   const uint32_t splits = fuse ? 1u : down_splits(r);
   float *partials = partials_;
+  const bool fqkv = fuse_qkv(b) && splits == 1;
   for (int i = 0; i < 12; ++i) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
+    DownQkvMaps dq_maps;
+    if (fqkv && i < 11)
+      need(make_down_qkv_maps(act, r, l.down_w, x, w.layer[i + 1].qkv_w, qkv, &dq_maps, &err));
     need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, qkv, &qkv_maps, &err));
     need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err, h));
     need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, act, &gu_maps, &err));
@@ -319,6 +334,7 @@ Plan &Model::prepare(size_t b, int slot) {
       need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err,
                           i == 11 ? static_cast<const void *>(out) : static_cast<const void *>(h),
                           i == 11));
+    if (!(fqkv && i > 0))  // else the previous layer's down projection ran this QKV
     add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;
@@ -374,6 +390,21 @@ Plan &Model::prepare(size_t b, int slot) {
       add("splitk_reduce_layernorm", [=](cudaStream_t s) {
         return launch_splitk_reduce(partials, r, splits, l.down_b, l.ls2, x, ng, nb,
                                     last ? nullptr : h, last ? out : nullptr, s);
+      });
+      continue;
+    }
+    if (fqkv && !last) {
+      const LayerWeights &n = w.layer[i + 1];
+      add("gemm_down_ln_qkv", [=](cudaStream_t s) {
+        GemmArgs d, q;
+        d.bias = l.down_b;
+        d.lambda = l.ls2;
+        d.gamma = ng;
+        d.beta = nb;
+        q.bias = n.qkv_b;
+        q.rope_cos = w.rope_cos;
+        q.rope_sin = w.rope_sin;
+        return launch_down_qkv(dq_maps, r, d, q, st, s);
       });
       continue;
     }

@@ -86,6 +86,7 @@ class Model {
   void drain();                                  // finish every outstanding submission
   bool fuse_layernorm(size_t batch) const;      // plan variant for this batch size
   bool fuse_patchify(size_t batch) const;       // patchify inside the patch GEMM
+  bool fuse_qkv(size_t batch) const;            // next QKV inside the down projection
   uint32_t down_splits(uint32_t rows) const;    // split-K slices of the down projection
   void check_status();                          // read the device status words (synchronous)
   void activate() const;

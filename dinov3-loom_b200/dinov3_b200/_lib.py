@@ -83,6 +83,7 @@ SIGNATURES = {
     "dv3k_attention": ([_P, _U32, _P, _P, _P], _I),
     "dv3k_matmul_resid": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_resid_layernorm": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "dv3k_down_layernorm_qkv": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_swiglu": ([_P, _U32, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_splitk": ([_P, _U32, _P, _U32, _P, _P, _P], _I),
     "dv3k_splitk_reduce": ([_P, _U32, _U32, _P, _P, _P, _P], _I),

@@ -115,6 +115,16 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
                                 const float *gamma, const float *beta, uint16_t *h,
                                 float *out_f32, uint32_t *status, void *stream);
 
+/* dv3k_matmul_resid_layernorm (k = 1536, f16 h) followed by dv3k_qkv_rope on its h, in one
+ * kernel: each 128-row tile's LayerNorm rows stay in shared memory as the QKV GEMM's A operand
+ * (h is not written to memory). x and qkv are bit for bit those of the two calls. rows: a
+ * multiple of 201, at most one 128-row tile per SM. */
+int dv3k_down_layernorm_qkv(const uint16_t *act, uint32_t rows, const uint16_t *down_w,
+                            const float *down_b, const float *lambda, uint16_t *x,
+                            const float *gamma, const float *beta, const uint16_t *qkv_w,
+                            const float *qkv_b, const float *rope_cos, const float *rope_sin,
+                            uint16_t *qkv, uint32_t *status, void *stream);
+
 /* Down projection split over K (kernels/matmul_splitk_f16_wmma.loom, launched at batch 1 by
  * src/lib.rs:218-224 with the specialisation of :297): for each slice s < splits of the 1536-long
  * reduction, partials[s][row][n] = sum over k in slice s of a[row][k] * w[n][k], f32, no bias.

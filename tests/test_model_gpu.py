@@ -328,6 +328,25 @@ def test_fused_patchify_plan(weights_file, monkeypatch, b):
         assert cos(fused[i], plain[i]) > 0.99999
 
 
+def test_fused_down_qkv_plan(weights_file, monkeypatch):
+    """DV3_FUSE_QKV=1 (read when a batch size's graph is built; full-row plans only) runs each
+    down projection of layers 0-10 together with the next layer's QKV GEMM (h kept in shared
+    memory): 11 launches fewer, and bit for bit the default plan's output."""
+    path = weights_file(1, "stress")
+    images = synth.images(55, 64)
+    with dv.DINOv3.load(path, dv.Options(0, 64)) as model:
+        n_default = model.launches_per_forward(64)
+        want = model.forward(images)
+    monkeypatch.setenv("DV3_FUSE_QKV", "1")
+    with dv.DINOv3.load(path, dv.Options(0, 64)) as model:
+        assert model.launches_per_forward(64) == n_default - 11
+        names = [n for n, _ in model.profile_launches(64, 1)]
+        assert names.count("gemm_down_ln_qkv") == 11 and names.count("gemm_qkv_rope") == 1
+        got = model.forward(images)
+        assert model.launches_per_forward(16) == 3 + 12 * 7  # small batches: unchanged
+    np.testing.assert_array_equal(got, want)
+
+
 def test_submit_wait_serving_path(models):
     """Serving path (dv3_submit / dv3_wait): submissions of changing size, two in flight and a
     third that first completes the oldest, waited out of order, give exactly the synchronous
