@@ -641,7 +641,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 namespace {
 constexpr int kDqQTile = BM * BK * 2;             // 16 KB: one h k-block tile
 constexpr int kDqWStage = 256 * BK * 2;           // 32 KB: one QKV weight k-block
-constexpr int kDqBars = 36;                        // mbarriers of the fused kernel
+constexpr int kDqBars = 35;                        // mbarriers of the fused kernel
 constexpr int kDqBarBytes = 512;
 constexpr int kDqStagingBytes = kEpilogueWarps * kStageBlockBytes;
 using DqCfg = GemmCfg<384, EpiResidLN>;
@@ -667,9 +667,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t *tiles = smem;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kTiles);
   uint64_t *empty = full + 3;
-  uint64_t *tfull = empty + 3;
-  uint64_t *tempty = tfull + 1;
-  uint64_t *in_bars = tempty + 1;  // 2 per epilogue warp (the first used)
+  uint64_t *tfull = empty + 3;  // the down projection's accumulator is complete
+  uint64_t *in_bars = tfull + 1;  // 2 per epilogue warp (the first used)
   uint64_t *full2 = in_bars + 2 * kEpilogueWarps;
   uint64_t *empty2 = full2 + 3;
   uint64_t *tfull2 = empty2 + 3;
@@ -703,7 +702,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty2[s], 1);
     }
     mbar_init(&tfull[0], 1);
-    mbar_init(&tempty[0], kEpilogueThreads);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull2[a], 1);
       mbar_init(&tempty2[a], kEpilogueThreads);
