@@ -173,11 +173,13 @@ def device_view(ptr, n):
     return torch.as_tensor(_DeviceArray(ptr, n), device="cuda")
 
 
-def test_full_size_batch_properties(models, oracles):
-    """Batch 64 (the benchmark configuration): per-image results match single-image forwards,
-    two images match the oracle, and repeats are bitwise identical."""
+@pytest.mark.parametrize("source", ["seeded", "reference"])
+def test_full_size_batch_properties(models, oracles, source):
+    """Batch 64 (the benchmark configuration), on seeded images and on the reference test's own
+    input pattern (tests/model.rs:72-74): per-image results match single-image forwards, two
+    images match the oracle, and repeats are bitwise identical."""
     model = models("baseline", max_batch=64)
-    images = synth.images(2024, 64)
+    images = synth.images(2024, 64) if source == "seeded" else synth.reference_test_images(64)
     # batch 64 fuses the LayerNorms into the residual GEMMs; single images use the split plan
     assert model.launches_per_forward(64) == 3 + 12 * 5
     assert model.launches_per_forward(1) == 3 + 12 * 7
