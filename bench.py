@@ -16,13 +16,22 @@ barrier and the max-over-ranks of the timings).
           synchronisations, max over ranks. `e2e_sync` beside it: one blocking dv3_forward per
           step (upload, forward and download in series), CUDA events on the model's stream.
   roofline the dominant kernel (gate/up GEMM + SwiGLU, 46.5 % of the FLOPs): its algorithmic FLOPs
-          per launch / its average launch time (CUDA event nodes between the launches of a graph
-          replay of the forward on the model's stream, `--profile-iters` replays), against the
-          measured bf16/f16 dense peak (MEASURED_PEAKS.json). `traffic` comes from the committed
-          ncu summary in profiles/ when it lists this kernel.
+          per launch / its average launch time, measured inside whole forwards after the timed
+          region (dv3_profile_forward: `--profile-iters` forwards of the same staged batch, the
+          L2 flushed before each, every launch enqueued on the model's stream between two CUDA
+          events), against the measured burst bf16/f16 dense peak (MEASURED_PEAKS.json
+          bf16_tflops; `frac_of_sustained` beside it). `per_kernel` lists every kernel of the
+          plan the same way: FLOPs and algorithmic bytes per launch, the measured time, the
+          floor max(FLOPs / tensor peak, bytes / HBM bandwidth) and floor / time. `traffic` comes
+          from the committed ncu summary in profiles/ when it lists the kernel.
   cpu_baseline the float64 CPU oracle (C restatement of the reference's own float64 forward,
           tests/support/reference.rs) on this host, OpenMP over images, rank 0 at N = 1 only.
-Reference arm (--impl reference): the same CPU oracle with all host threads, rank 0 only.
+Reference arm (--impl reference): the same CPU oracle with all host threads, rank 0 only; a
+step is one forward of as many images as host threads (a bounded sample of the batch-64 step).
+--ops: BASELINE config 3, every kernel entry point (include/dinov3_kernels.h) alone at batch 64
+(12,864 token rows), inputs N(0,1) and weights N(0,1)/sqrt(K), with cold L2: each timed graph
+cycles over enough copies of the operands to exceed twice the L2, so no launch finds its inputs
+cached (a warm figure, one set of operands repeated, is given beside it).
 """
 from __future__ import annotations
 
@@ -45,8 +54,48 @@ BATCH = 64
 METRIC = "images/sec (224², ViT-S+/16) at batch 64 on 1/2/4/8 B200; p50 batch-1 latency"
 UNIT = "images/s"
 GFLOP_PER_IMAGE = 12.2415
-GATEUP_GFLOP_B64 = 2 * 12864 * 384 * 3072 / 1e9  # 30.350 GFLOP per launch at batch 64
-GATEUP_BYTES_B64 = (12864 * 384 + 3072 * 384 + 12864 * 1536) * 2 + 3072 * 4  # algorithmic
+R64, P64 = 201 * BATCH, 196 * BATCH  # token rows and patch rows at batch 64
+
+
+def kernel_work(name: str, b: int = BATCH, last: bool = False):
+    """(FLOPs, algorithmic bytes) of one launch of kernel `name` over b images: FLOPs 2*M*K*N per
+    GEMM and 4*T^2*d per attention slice; bytes = every input and weight read once, every output
+    written once, the residual read and written (the minimum HBM traffic)."""
+    r, p, d = 201 * b, 196 * b, 384
+    f16, f32 = 2, 4
+    if name == "patchify":
+        return 0.0, b * 3 * 224 * 224 * f32 + p * 768 * f16 + b * 5 * d * f16
+    if name == "gemm_patch_embed":
+        return 2.0 * p * 768 * d, (p * 768 + d * 768 + p * d) * f16 + d * f32
+    if name in ("layernorm_f16", "layernorm_f32out"):
+        return 0.0, r * d * f16 + r * d * (f32 if name == "layernorm_f32out" else f16) + 2 * d * f32
+    if name == "gemm_qkv_rope":
+        return 2.0 * r * d * 1152, (r * d + 1152 * d + r * 1152) * f16 + (1152 + 2 * 196 * 64) * f32
+    if name == "attention":
+        return 4.0 * 201 * 201 * 64 * 6 * b, (r * 1152 + r * d) * f16
+    if name in ("gemm_o_resid", "gemm_o_resid_layernorm"):
+        ln = name.endswith("layernorm")
+        return 2.0 * r * d * d, (r * d + d * d + 2 * r * d + (r * d if ln else 0)) * f16 + 4 * d * f32
+    if name == "gemm_gateup_swiglu":
+        return 2.0 * r * d * 3072, (r * d + 3072 * d + r * 1536) * f16 + 3072 * f32
+    if name in ("gemm_down_resid", "gemm_down_resid_layernorm"):
+        ln = name.endswith("layernorm")
+        out = (r * d * (f32 if last else f16)) if ln else 0
+        return 2.0 * r * 1536 * d, (r * 1536 + d * 1536 + 2 * r * d) * f16 + out + 4 * d * f32
+    return 0.0, 0.0
+
+
+def roofline_entry(name, ms, flops, nbytes, peaks):
+    """Floor = max(FLOPs / burst tensor peak, bytes / HBM copy bandwidth); frac = floor / time."""
+    t_tensor = flops / (peaks["bf16_tflops"] * 1e12) * 1e3 if flops else 0.0
+    t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e3
+    floor = max(t_tensor, t_hbm)
+    return {"kernel": name, "us": ms * 1e3, "gflop": flops / 1e9, "mbytes": nbytes / 1e6,
+            "bound": "tensor" if t_tensor >= t_hbm else "hbm",
+            "tflops": flops / ms / 1e9 if flops else 0.0, "gbs": nbytes / ms / 1e6,
+            "floor_us": floor * 1e3, "frac": floor / ms}
+
+
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 WORKLOAD = "DINOv3 ViT-S+/16 forward, 224x224, batch 64 per GPU (config 2), fp16 weights/activations, fp32 accumulate"
 
@@ -67,6 +116,9 @@ def parse_args():
                          "1..64 from pinned host memory, synchronous and two-deep pipelined")
     ap.add_argument("--serve-images", type=int, default=8192,
                     help="images over all GPUs in the serving measurement")
+    ap.add_argument("--ops", action="store_true",
+                    help="per-op microbenchmark (BASELINE config 3): every kernel entry point "
+                         "alone at batch 64, cold and warm L2")
     return ap.parse_args()
 
 
@@ -201,7 +253,9 @@ def run_reference(args):
     model.forward(images, threads=threads)
     est = time.perf_counter() - t0
     steps = max(1, min(args.steps, int(args.cpu_budget_s * 6 // max(est, 1e-3))))
-    warm = min(args.warmup, 1)
+    # the same warm-up count as our arm, within the CPU time budget (the estimate above was a
+    # first warm-up forward already)
+    warm = max(0, min(args.warmup - 1, int(args.cpu_budget_s * 2 // max(est, 1e-3))))
     for _ in range(warm):
         model.forward(images, threads=threads)
     t0 = time.perf_counter()
@@ -214,9 +268,12 @@ def run_reference(args):
                      f"float64 C oracle of tests/support/reference.rs, OpenMP over images "
                      f"({steps} of the requested {args.steps} steps fit the CPU time budget)"}
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": steps, "warmup": warm, "ms_per_step": 1000 * dt / steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": BATCH * args.gpus, "batch_per_gpu": BATCH,
+            "steps": steps, "warmup": warm + 1, "ms_per_step": 1000 * dt / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": threads, "images_per_step": threads,
+                       "sample_of": f"the batch-{BATCH} step: one float64 forward of {threads} "
+                                    f"images (one per host thread) per step",
                        "parallelism": f"replicas{args.gpus}"},
             "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -232,6 +289,35 @@ def cpu_model():
     except Exception:
         pass
     return f"unknown x{os.cpu_count()}"
+
+
+def kernel_table(prof, peaks):
+    """Per kernel of the plan: launches, average time, algorithmic work per launch and its roofline
+    (roofline_entry); the time shares; the gate/up GEMM's entry."""
+    total_ms = sum(ms for _, ms in prof)
+    agg = {}
+    n_down = sum(1 for n, _ in prof if n.startswith("gemm_down"))
+    seen_down = 0
+    for name, ms in prof:
+        last = False
+        if name.startswith("gemm_down"):
+            seen_down += 1
+            last = seen_down == n_down
+        flops, nbytes = kernel_work(name, BATCH, last)
+        a = agg.setdefault(name, [0, 0.0, 0.0, 0.0])
+        a[0] += 1
+        a[1] += ms
+        a[2] += flops
+        a[3] += nbytes
+    table, share = [], {}
+    for name, (n, ms, flops, nbytes) in agg.items():
+        e = roofline_entry(name, ms / n, flops / n, nbytes / n, peaks)
+        e["launches"] = n
+        e["traffic"] = committed_traffic(name)
+        table.append(e)
+        share[name] = round(ms / total_ms, 4)
+    gate = next(e for e in table if e["kernel"] == "gemm_gateup_swiglu")
+    return table, share, gate
 
 
 def run_ours(args):
@@ -370,16 +456,12 @@ def run_ours(args):
             lat_dev.append(s.elapsed_time(e))
             lat_e2e.append((t1 - t0) * 1000)
 
-    # ---- dominant kernel roofline ----
-    prof = model.profile_launches(BATCH, args.profile_iters)
-    by_kernel = {}
-    for name, ms in prof:
-        by_kernel.setdefault(name, []).append(ms)
-    gate_ms = statistics.mean(by_kernel["gemm_gateup_swiglu"])
+    # ---- per-kernel times inside whole forwards (L2 flushed before each) and rooflines ----
+    prof = model.profile_forward(BATCH, args.profile_iters, 256 << 20)
     peaks, peak_src = load_peaks()
-    achieved = GATEUP_GFLOP_B64 / gate_ms  # GFLOP/ms == TFLOP/s
-    peak = peaks["bf16_tflops_sustained"]
-    kernel_share = {k: round(sum(v) / sum(ms for _, ms in prof), 4) for k, v in by_kernel.items()}
+    per_kernel, kernel_share, gate = kernel_table(prof, peaks)
+    gate_ms = gate["us"] / 1e3
+    achieved = gate["tflops"]
 
     steps_launches = launches * args.steps
     model.synchronize()
@@ -420,10 +502,17 @@ def run_ours(args):
                                 "download in series), CUDA events on the model's stream"},
             "gpu_launches": steps_launches,
             "roofline": {"kernel": "gemm_gateup_swiglu", "bound": "tensor", "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops"],
+                         "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
+                         "peak_source": f"{peak_src} bf16_tflops (burst; of measured)",
                          "traffic": committed_traffic("gemm_gateup_swiglu"),
-                         "algorithmic_bytes": GATEUP_BYTES_B64, "avg_launch_ms": gate_ms},
+                         "algorithmic_flops": gate["gflop"] * 1e9,
+                         "algorithmic_bytes": gate["mbytes"] * 1e6, "avg_launch_ms": gate_ms,
+                         "timing": f"dv3_profile_forward: {args.profile_iters} forwards, L2 "
+                                   "flushed before each, CUDA events around every launch on "
+                                   "the model's stream",
+                         "per_kernel": per_kernel},
             "cpu_baseline": cpu,
             "cpu_baseline_single": cpu_single,
             "p50_batch1_latency_ms": {"device": statistics.median(lat_dev), "e2e": statistics.median(lat_e2e)},
@@ -503,10 +592,162 @@ def run_serving(args, model, images, reps):
     reps.close()
 
 
+def run_ops(args):
+    """each kernel entry point of include/dinov3_kernels.h alone at batch 64
+    (12,864 token rows, 12,544 patch rows), activations N(0,1), weights N(0,1)/sqrt(K). Each op's
+    launches are captured K times into a CUDA graph that cycles over S copies of its operands,
+    S x (operand bytes) > 2 x L2 (cold: every launch reads operands the L2 no longer holds), and
+    over one copy (warm); one replay after a warm-up replay is timed with CUDA events on the
+    launching stream, time per launch = interval / K. Rank 0 only; prints one JSON line."""
+    import numpy as np
+    import torch
+
+    from dinov3_b200 import _lib
+
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = _lib.load()
+    peaks, peak_src = load_peaks()
+    l2 = 126 << 20
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    r, p, d = R64, P64, 384
+    st = torch.zeros(2, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def randn(shape, scale=1.0, dtype=torch.float16):
+        return (torch.randn(shape, generator=gen, device=dev) * scale).to(dtype)
+
+    def empty(shape, dtype=torch.float16):
+        return torch.empty(shape, dtype=dtype, device=dev)
+
+    def vec(n, lo=-0.1, hi=0.1):
+        return torch.rand(n, generator=gen, device=dev) * (hi - lo) + lo
+
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    w = {"patch": randn((d, 768), 768 ** -0.5), "qkv": randn((1152, d), d ** -0.5),
+         "o": randn((d, d), d ** -0.5), "gateup": randn((3072, d), d ** -0.5),
+         "down": randn((d, 1536), 1536 ** -0.5)}
+    v = {"bias": vec(3072), "lam": vec(d, 0.05, 0.2), "gamma": vec(d, 0.5, 1.5), "beta": vec(d),
+         "cos": vec(196 * 64, -1, 1), "sin": vec(196 * 64, -1, 1), "prefix": vec(5 * d, -1, 1)}
+
+    def check(rc):
+        if rc != 0:
+            raise RuntimeError(_lib.last_error())
+
+    def time_op(name, make, launch, flops, nbytes, set_bytes):
+        sets = [make() for _ in range(max(2, -(-2 * l2 // set_bytes) + 1))]
+        with torch.cuda.stream(stream):
+            for ops in sets:  # validates the arguments and configures the kernel outside capture
+                check(launch(ops, stream.cuda_stream))
+        stream.synchronize()
+        out = {}
+        for mode, use in (("cold", sets), ("warm", sets[:1])):
+            k = len(use) * max(2, -(-24 // len(use)))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                cs = torch.cuda.current_stream().cuda_stream
+                for i in range(k):
+                    check(launch(use[i % len(use)], cs))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                g.replay()
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            e1.synchronize()
+            out[mode] = e0.elapsed_time(e1) / k
+            del g
+        if st.cpu().tolist() != [0, 0]:
+            raise RuntimeError(f"{name}: device status {st.cpu().tolist()}")
+        del sets
+        torch.cuda.empty_cache()
+        e = roofline_entry(name, out["cold"], flops, nbytes, peaks)
+        e["warm_us"] = out["warm"] * 1e3
+        e["operand_sets"] = -(-2 * l2 // set_bytes) + 1
+        return e
+
+    f16b, f32b = 2, 4
+    results = []
+    results.append(time_op(
+        "patchify", lambda: (randn((BATCH, 3, 224, 224), dtype=torch.float32), empty((p, 768)),
+                             empty((r, d))),
+        lambda o, s: lib.dv3k_patchify(ptr(o[0]), BATCH, ptr(v["prefix"]), ptr(o[1]), ptr(o[2]),
+                                       ptr(st), s),
+        *kernel_work("patchify"), BATCH * 150528 * f32b + p * 768 * f16b + r * d * f16b))
+    results.append(time_op(
+        "gemm_patch_embed", lambda: (randn((p, 768)), empty((r, d))),
+        lambda o, s: lib.dv3k_patch_embed(ptr(o[0]), p, ptr(w["patch"]), ptr(v["bias"]), ptr(o[1]),
+                                          ptr(st), s),
+        *kernel_work("gemm_patch_embed"), (p * 768 + r * d) * f16b))
+    results.append(time_op(
+        "layernorm_f16", lambda: (randn((r, d)), empty((r, d))),
+        lambda o, s: lib.dv3k_layernorm_f16(ptr(o[0]), r, ptr(v["gamma"]), ptr(v["beta"]),
+                                            ptr(o[1]), s),
+        *kernel_work("layernorm_f16"), 2 * r * d * f16b))
+    results.append(time_op(
+        "layernorm_f32out", lambda: (randn((r, d)), empty((r, d), torch.float32)),
+        lambda o, s: lib.dv3k_layernorm_f32out(ptr(o[0]), r, ptr(v["gamma"]), ptr(v["beta"]),
+                                               ptr(o[1]), s),
+        *kernel_work("layernorm_f32out"), r * d * (f16b + f32b)))
+    results.append(time_op(
+        "gemm_qkv_rope", lambda: (randn((r, d)), empty((r, 1152))),
+        lambda o, s: lib.dv3k_qkv_rope(ptr(o[0]), r, ptr(w["qkv"]), ptr(v["bias"]), ptr(v["cos"]),
+                                       ptr(v["sin"]), ptr(o[1]), ptr(st), s),
+        *kernel_work("gemm_qkv_rope"), r * (d + 1152) * f16b))
+    results.append(time_op(
+        "attention", lambda: (randn((r, 1152)), empty((r, d))),
+        lambda o, s: lib.dv3k_attention(ptr(o[0]), r, ptr(o[1]), ptr(st), s),
+        *kernel_work("attention"), r * (1152 + d) * f16b))
+    for k, wname in ((384, "o"), (1536, "down")):
+        base = "gemm_o_resid" if k == 384 else "gemm_down_resid"
+        results.append(time_op(
+            base, lambda k=k: (randn((r, k)), randn((r, d))),
+            lambda o, s, k=k, wname=wname: lib.dv3k_matmul_resid(
+                ptr(o[0]), r, k, ptr(w[wname]), ptr(v["bias"]), ptr(v["lam"]), ptr(o[1]), ptr(st), s),
+            *kernel_work(base), r * (k + d) * f16b))
+        results.append(time_op(
+            base + "_layernorm", lambda k=k: (randn((r, k)), randn((r, d)), empty((r, d))),
+            lambda o, s, k=k, wname=wname: lib.dv3k_matmul_resid_layernorm(
+                ptr(o[0]), r, k, ptr(w[wname]), ptr(v["bias"]), ptr(v["lam"]), ptr(o[1]),
+                ptr(v["gamma"]), ptr(v["beta"]), ptr(o[2]), None, ptr(st), s),
+            *kernel_work(base + "_layernorm"), r * (k + 2 * d) * f16b))
+    results.append(time_op(
+        "gemm_gateup_swiglu", lambda: (randn((r, d)), empty((r, 1536))),
+        lambda o, s: lib.dv3k_matmul_swiglu(ptr(o[0]), r, ptr(w["gateup"]), ptr(v["bias"]),
+                                            ptr(o[1]), ptr(st), s),
+        *kernel_work("gemm_gateup_swiglu"), r * (d + 1536) * f16b))
+
+    def splitk_pair(o, s, splits=2):
+        rc = lib.dv3k_matmul_splitk(ptr(o[0]), r, ptr(w["down"]), splits, ptr(o[2]), ptr(st), s)
+        return rc or lib.dv3k_splitk_reduce(ptr(o[2]), r, splits, ptr(v["bias"]), ptr(v["lam"]),
+                                            ptr(o[1]), s)
+
+    e = time_op("gemm_down_splitk2+splitk_reduce",
+                lambda: (randn((r, 1536)), randn((r, d)), empty((2, r, d), torch.float32)),
+                splitk_pair, *kernel_work("gemm_down_resid"), r * (1536 + d) * f16b + 2 * r * d * f32b)
+    e["note"] = "two launches (split-K GEMM over 2 K slices into f32 slabs, then the reduce)"
+    results.append(e)
+    line = {"metric": "per-op device time at batch 64 (BASELINE config 3), cold L2",
+            "unit": "us", "n_gpus": 1, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "each kernel entry point alone, 12864 token rows (12544 patch "
+                                   "rows), activations N(0,1), weights N(0,1)/sqrt(K)",
+                       "l2": "cold: operand copies cycled, more than twice the L2 in total"},
+            "peaks": {"tflops": peaks["bf16_tflops"], "hbm_gbs": peaks["hbm_gbs"],
+                      "source": f"{peak_src} (burst)"},
+            "ops": results}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.ops:
+        run_ops(args)
     else:
         run_ours(args)
 

@@ -42,6 +42,8 @@
 //
 // Every wait is bounded; on a timeout the kernel records kErrAttentionWait, raises the CTA's
 // abort flag, lets its own copies and MMAs in flight land, frees TMEM and returns.
+#include <atomic>
+
 #include "kernels.h"
 #include "sm100.cuh"
 
@@ -384,13 +386,14 @@ cudaError_t configure_attention_kernel() {
 cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
                              cudaStream_t stream, const void *l2_next, size_t l2_next_bytes) {
   if (rows == 0) return cudaSuccess;
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev >= 0 && dev < 64 && !configured[dev].load(std::memory_order_acquire)) {
+    // setting the attribute twice (two threads racing here) is harmless
     cudaError_t e = configure_attention_kernel();
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   const int n_items = static_cast<int>(rows / kTokens) * kHeads;
   // Small batches (every query tile fits its own SM): one CTA per query tile.

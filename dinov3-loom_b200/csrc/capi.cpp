@@ -155,6 +155,24 @@ int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *
   });
 }
 
+int dv3_profile_forward(dv3_model *m, size_t batch, size_t replays, size_t flush_bytes,
+                        double *ms, const char **names, size_t capacity, size_t *count) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] {
+    auto r = m->impl.profile_forward(batch, replays, flush_bytes);
+    for (size_t i = 0; i < r.size() && i < capacity; ++i) {
+      if (ms) ms[i] = r[i].second;
+      if (names) names[i] = r[i].first;
+    }
+    if (count) *count = r.size();
+  });
+}
+
+int dv3_debug_inject_fault(dv3_model *m, uint32_t bits) {
+  if (int rc = check_model(m)) return rc;
+  return guarded([&] { m->impl.inject_fault(bits); });
+}
+
 int dv3_hub_weights(int offline, char *path, size_t capacity) {
   if (!path || capacity == 0) return fail(DV3_INVALID_ARGUMENT, "null path buffer");
   std::string p, err;
@@ -249,22 +267,6 @@ int dv3k_patch_embed(const uint16_t *patches, uint32_t n_patches, const uint16_t
   g.bias = bias;
   g.out = reinterpret_cast<__half *>(x);
   return gemm_entry(dv3::GemmOp::Patch, patches, n_patches, w, g, status, stream);
-}
-
-int dv3k_patch_embed_pixels(const float *images, uint32_t n_images, const uint16_t *w,
-                            const float *bias, const float *prefix, uint16_t *x, uint32_t *status,
-                            void *stream) {
-  if (n_images == 0) return DV3_OK;
-  if (!all_aligned(images, w, bias, prefix, x)) return bad_args("pointers must be 16-byte aligned");
-  const uint32_t rows = n_images * dv3::kPatches;
-  if ((rows + 127) / 128 > static_cast<uint32_t>(dv3::sm_count(current_device())))
-    return bad_args("too many images for one wave of 128-patch tiles");
-  dv3::GemmArgs g;
-  g.bias = bias;
-  g.out = reinterpret_cast<__half *>(x);
-  g.images = images;
-  g.prefix = prefix;
-  return gemm_entry(dv3::GemmOp::PatchPixels, nullptr, rows, w, g, status, stream);
 }
 
 int dv3k_layernorm_f16(const uint16_t *x, uint32_t rows, const float *gamma, const float *beta,
@@ -414,34 +416,6 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
   g.ln_out_f32 = out_f32;
   return gemm_entry(k == 384 ? dv3::GemmOp::ResidLN384 : dv3::GemmOp::ResidLN1536, a, rows, w, g,
                     status, stream);
-}
-
-int dv3k_down_layernorm_qkv(const uint16_t *act, uint32_t rows, const uint16_t *down_w,
-                            const float *down_b, const float *lambda, uint16_t *x,
-                            const float *gamma, const float *beta, const uint16_t *qkv_w,
-                            const float *qkv_b, const float *rope_cos, const float *rope_sin,
-                            uint16_t *qkv, uint32_t *status, void *stream) {
-  if (rows == 0) return DV3_OK;
-  if (!all_aligned(act, down_w, down_b, lambda, x, gamma, beta, qkv_w, qkv_b, rope_cos, rope_sin,
-                   qkv))
-    return bad_args("pointers must be 16-byte aligned");
-  if (rows % dv3::kTokens != 0) return bad_args("rows must be a multiple of 201");
-  if (rows > 128u * static_cast<uint32_t>(dv3::sm_count(current_device())))
-    return bad_args("rows must fit one 128-row tile per SM");
-  dv3::DownQkvMaps maps;
-  std::string err;
-  if (!dv3::make_down_qkv_maps(act, rows, down_w, x, qkv_w, qkv, &maps, &err))
-    return bad_args(err.c_str());
-  dv3::GemmArgs d, q;
-  d.bias = down_b;
-  d.lambda = lambda;
-  d.gamma = gamma;
-  d.beta = beta;
-  q.bias = qkv_b;
-  q.rope_cos = rope_cos;
-  q.rope_sin = rope_sin;
-  return launch_status(dv3::launch_down_qkv(maps, rows, d, q, status, static_cast<cudaStream_t>(stream)),
-                       "gemm_down_ln_qkv");
 }
 
 int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_w,

@@ -11,6 +11,8 @@
 //   both loads are contiguous across the warp. Mean and variance are reduced with shuffles in
 //   two passes over the registers (the reference's E[x^2]-mean^2 is replaced by the better
 //   conditioned centred sum), eps 1e-5, f32 arithmetic.
+#include <atomic>
+
 #include "kernels.h"
 #include "sm100.cuh"
 
@@ -354,15 +356,15 @@ cudaError_t launch_bounded_wait_selftest(uint64_t short_ns, uint32_t *status,
 }
 
 int sm_count(int device) {
-  static int cache[64] = {};
+  static std::atomic<int> cache[64] = {};
   if (device < 0 || device >= 64) return 148;
-  if (cache[device] == 0) {
-    int n = 0;
+  int n = cache[device].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
       n = 148;
-    cache[device] = n;
+    cache[device].store(n, std::memory_order_relaxed);
   }
-  return cache[device];
+  return n;
 }
 
 }  // namespace dv3

@@ -7,10 +7,6 @@
 //   ResidLN*  the same on full rows, then LayerNorm        + kernels/layernorm_rowwave_*.loom
 //   SwiGLU    act = f16(silu(A Wg^T + bg) (A Wu^T + bu))   kernels/matmul_swiglu_f16_wmma.loom
 //   SplitK    partials[s] = A[:, K_s] W[:, K_s]^T (f32)     kernels/matmul_splitk_f16_wmma.loom
-//   PatchPixels  Patch with A built from the f32 images    + the patchify of src/lib.rs:265-280
-//                in the mainloop (pixel_a_tiles)
-// and down_qkv_kernel: ResidLN1536 followed in the same CTA by the next layer's QkvRope on the
-// LayerNorm rows it keeps in shared memory (launch_down_qkv).
 //
 // Layout: A [M][K] f16 activations and W [N][K] f16 weights, both K-major, are streamed by TMA
 // in 128-row x 64-column boxes with the 128-byte swizzle into a ring of shared-memory stages.
@@ -28,6 +24,8 @@
 // Units of work (TileSched: full tiles in m-major order with the N tile fastest, so the CTAs
 // working at one time share A rows through L2, then narrow half-width units) are dealt
 // round-robin to a grid of min(units, SMs) persistent CTAs.
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "gemm_epilogues.cuh"
@@ -112,18 +110,6 @@ struct BiasInTmem<Epi, decltype(void(Epi::kBiasInTmem))> {
   static constexpr bool value = Epi::kBiasInTmem;
 };
 
-// Whether the epilogue warps build the A tiles from f32 NCHW images (Epi::kAFromPixels, the
-// fused patchify of the patch embedding) while the producer loads only the weights. One tile per
-// CTA: the epilogue warps are idle during its mainloop.
-template <class Epi, class = void>
-struct AFromPixels {
-  static constexpr bool value = false;
-};
-template <class Epi>
-struct AFromPixels<Epi, decltype(void(Epi::kAFromPixels))> {
-  static constexpr bool value = Epi::kAFromPixels;
-};
-
 // Bytes of one epilogue warp's staging region in the tile buffers: Epi::kWarpStaging when it
 // exists.
 template <class Epi, class = void>
@@ -154,14 +140,9 @@ struct GemmCfg {
   static constexpr bool kInput = TmaInput<Epi>::value;
   static constexpr bool kEarly = EarlyInput<Epi>::value;
   static constexpr bool kBiasInit = BiasInTmem<Epi>::value;
-  static constexpr bool kAPix = AFromPixels<Epi>::value;
   // configurations whose launches have exactly one tile per CTA
-  static constexpr bool kOneTile = kInTiles || kBiasInit || kAPix;
+  static constexpr bool kOneTile = kInTiles || kBiasInit;
   static_assert(!kBiasInit || BN == 384, "bias fill: one full-row tile per CTA");
-  static_assert(!kAPix || (kBiasInit && BN == 384), "pixel A tiles: one full-row tile per CTA");
-  // full-barrier arrivals per stage: the producer's (with the TMA bytes), and with kAPix one per
-  // epilogue warp once its rows of the A tile are written
-  static constexpr int kFullArrivals = kAPix ? 1 + kEpilogueWarps : 1;
   static constexpr int kBarBytes = kInput ? 384 : 256;  // + 2 input-block mbarriers per warp
   static constexpr int kFixed = 1024 + kStaging + kBarBytes + ((Epi::kSmem + 127) / 128) * 128;
   static constexpr int kFit = (227 * 1024 - kFixed) / kStage;
@@ -238,76 +219,6 @@ __device__ __forceinline__ void unit_coords(const TileSched &s, int u, int &m0, 
 }
 
 // ---------------------------------------------------------------------------------------------
-// The patchify of the patch embedding inside its mainloop (Epi::kAFromPixels). A[p][k] is pixel
-// (c, dy, dx) = (k / 256, k / 16 % 16, k % 16) of patch p (src/lib.rs:265-280), so the 64
-// columns of k-block kb are channel kb / 4, pixel rows 4 (kb % 4) .. + 3 of the patch, 16 pixels
-// each. Lane l of epilogue warp ew takes tile row 16 ew + l / 2 and two of those pixel rows
-// (l % 2): 32 floats as eight 16-byte loads, rounded to f16 like patchify and written as four
-// 16-byte chunks of the 128-byte-swizzled row (chunk j of row r at j ^ (r % 8)). The loads of
-// the next two k-blocks are issued before the wait for a free stage, so three k-blocks of pixel
-// reads are in flight per thread (the reads are latency-bound: HBM under the whole grid's load). Rows past `rows` are zeros. Any non-finite pixel sets status[1] bit 0,
-// the flag patchify sets. Returns false when a stage never frees (the kernel is aborting).
-// ---------------------------------------------------------------------------------------------
-template <class C>
-__device__ bool pixel_a_tiles(const float *images, int rows, int m0, int ew, int lane,
-                              uint8_t *tiles, uint64_t *full, uint64_t *empty, int k_blocks,
-                              volatile int *abort_flag, uint32_t *status) {
-  const int r = 16 * ew + (lane >> 1);
-  const int part = lane & 1;
-  const int p = m0 + r;
-  const bool valid = p < rows;
-  const int img = valid ? p / kPatches : 0, pp = valid ? p % kPatches : 0;
-  const float *base = images + static_cast<int64_t>(img) * 3 * kImage * kImage +
-                      (pp / 14) * 16 * kImage + (pp % 14) * 16 + 2 * part * kImage;
-  auto load = [&](int kb, float4 (&v)[8]) {
-    const float4 *src =
-        reinterpret_cast<const float4 *>(base + (kb >> 2) * kImage * kImage + (kb & 3) * 4 * kImage);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[i] = valid ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[4 + i] = valid ? __ldg(src + kImage / 4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  float4 cur[8], nxt[8], nxt2[8];
-  load(0, cur);
-  if (k_blocks > 1) load(1, nxt);
-  int stage = 0;
-  uint32_t phase = 0;
-  bool bad = false, ok = true;
-  for (int kb = 0; kb < k_blocks; ++kb) {
-    if (kb + 2 < k_blocks) load(kb + 2, nxt2);
-    if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag))) {
-      ok = false;
-      break;
-    }
-    uint8_t *row = tiles + stage * C::kStage + r * 128;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 a = cur[2 * j], b = cur[2 * j + 1];
-      bad |= !(isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w) &&
-               isfinite(b.x) && isfinite(b.y) && isfinite(b.z) && isfinite(b.w));
-      *reinterpret_cast<uint4 *>(row + (((4 * part + j) ^ (r & 7)) << 4)) =
-          make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
-                     pack_half2(b.z, b.w));
-    }
-    fence_proxy_async_smem();  // the MMA reads the tile through the async proxy
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&full[stage]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      cur[i] = nxt[i];
-      nxt[i] = nxt2[i];
-    }
-    if (++stage == C::kStages) {
-      stage = 0;
-      phase ^= 1u;
-    }
-  }
-  if (__any_sync(0xffffffffu, bad) && lane == 0 && status) atomicOr(status + 1, 1u);
-  return ok;
-}
-
-// ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
 template <int BN, class Epi>
@@ -336,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], C::kFullArrivals);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < C::kAccBufs; ++a) {
@@ -413,8 +324,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           uint8_t *a = tiles + stage * C::kStage;
-          mbar_arrive_expect_tx(&full[stage], (C::kAPix ? 0 : C::kA) + b_boxes * C::kBBox * BK * 2);
-          if constexpr (!C::kAPix) tma_load_2d(a, &tmA, &full[stage], (kb0 + kb) * BK, m0);
+          mbar_arrive_expect_tx(&full[stage], C::kA + b_boxes * C::kBBox * BK * 2);
+          tma_load_2d(a, &tmA, &full[stage], (kb0 + kb) * BK, m0);
           for (int s = 0; s < b_boxes; ++s)
             tma_load_2d(a + C::kA + s * C::kBBox * BK * 2, &tmB, &full[stage], (kb0 + kb) * BK,
                         n0 + s * C::kBBox);
@@ -542,19 +453,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ctx.abort_flag = abort_flag;
     ctx.failed = false;
     for (int b = 0; b < 3; ++b) ctx.blocks[b] = ctx.staging + b * (32 * 128);  // EpiResidLN
-    ctx.h_in_smem = false;
-    if constexpr (C::kAPix) {
-      // the CTA's one tile: this warp writes rows 16 (warp - 2) .. + 15 of each k-block's A tile
-      int m0, n0_unused, k_slice_unused;
-      bool narrow_unused;
-      unit_coords<BN>(sched, blockIdx.x, m0, n0_unused, narrow_unused, k_slice_unused);
-      if (!pixel_a_tiles<C>(epi.images, M, m0, warp - 2, lane, tiles, full, empty, k_blocks,
-                            abort_flag, status) &&
-          lane == 0) {
-        report(status, kErrProducerWait);
-        *abort_flag = 1;
-      }
-    }
     int acc = 0;
     uint32_t acc_phase = 0;
     bool in_pending = false;  // input blocks requested for a tile not yet processed
@@ -624,369 +522,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------------------------
-// The down projection of layer i with its LayerScale residual and the LayerNorm that follows it
-// (EpiResidLN, one 128-row full-width tile per CTA), then, in the same CTA, layer i+1's QKV GEMM
-// with RoPE (EpiQkvRope) on the 128 h rows the LayerNorm has just produced: those rows are the
-// QKV's whole A operand, so they stay in shared memory instead of going out and back, and the
-// QKV's launch start and its uneven last wave go. Layout after the down projection's mainloop
-// (three 64 KB stages s_a, s_b, s_c in ring order after its last k-block): h as six 16 KB
-// k-block tiles (128 rows x 64 columns, 128-byte swizzle; tiles 0-3 in s_a, 4-5 in the first
-// half of s_b; the residual x arrives in the same slots, updated in place, stored, then
-// overwritten by h), and three 32 KB QKV weight stages (s_c, s_c + 32 KB, s_b + 32 KB). TMEM:
-// the 384-column accumulator, then two 256-column QKV accumulators once the LayerNorm has read
-// its rows back. Units of the QKV phase: columns 0-1023 as four 256-wide tiles and 1024-1151 as
-// one narrow tile, as in the QKV GEMM.
-// ---------------------------------------------------------------------------------------------
-namespace {
-constexpr int kDqQTile = BM * BK * 2;             // 16 KB: one h k-block tile
-constexpr int kDqWStage = 256 * BK * 2;           // 32 KB: one QKV weight k-block
-constexpr int kDqBars = 35;                        // mbarriers of the fused kernel
-constexpr int kDqBarBytes = 512;
-constexpr int kDqStagingBytes = kEpilogueWarps * kStageBlockBytes;
-using DqCfg = GemmCfg<384, EpiResidLN>;
-// the QKV output staging holds 64-byte-swizzled blocks: it starts on a 1024-byte boundary so
-// the swizzle phase of each block row is the one the TMA store applies
-constexpr int kDqStagingOffset =
-    (DqCfg::kTiles + kDqBarBytes + EpiResidLN::kSmem + EpiQkvRope::kSmem + 1023) / 1024 * 1024;
-constexpr int kDqSmem = 1024 + kDqStagingOffset + kDqStagingBytes;
-static_assert(DqCfg::kStages == 3 && DqCfg::kStage == 4 * kDqQTile, "three 64 KB stages");
-static_assert(kDqBars * 8 + 12 <= kDqBarBytes, "barrier region");
-static_assert(kDqSmem <= 227 * 1024, "shared memory budget");
-}  // namespace
-
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    down_qkv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                    const __grid_constant__ CUtensorMap tmQ, int M, int k_blocks, EpiResidLN epi1,
-                    EpiQkvRope epi2, uint32_t *status) {
-  using C = DqCfg;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  uint8_t *smem = smem_raw + pad;
-  uint8_t *tiles = smem;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kTiles);
-  uint64_t *empty = full + 3;
-  uint64_t *tfull = empty + 3;  // the down projection's accumulator is complete
-  uint64_t *in_bars = tfull + 1;  // 2 per epilogue warp (the first used)
-  uint64_t *full2 = in_bars + 2 * kEpilogueWarps;
-  uint64_t *empty2 = full2 + 3;
-  uint64_t *tfull2 = empty2 + 3;
-  uint64_t *tempty2 = tfull2 + 2;
-  uint64_t *h_ready = tempty2 + 2;
-  uint64_t *mma_drain = h_ready + 1;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_drain + 1);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  volatile int *in_armed = abort_flag + 1;
-  uint8_t *extra1 = smem + C::kTiles + kDqBarBytes;
-  uint8_t *extra2 = extra1 + EpiResidLN::kSmem;
-  uint8_t *staging2 = smem + kDqStagingOffset;
-
-  const int warp = threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  const int m0 = static_cast<int>(blockIdx.x) * BM;
-  const int sa = k_blocks % 3, sb = (k_blocks + 1) % 3, sc = (k_blocks + 2) % 3;
-  auto stage_ptr = [&](int s) { return tiles + s * C::kStage; };
-  auto htile = [&](int kb) {
-    return kb < 4 ? stage_ptr(sa) + kb * kDqQTile : stage_ptr(sb) + (kb - 4) * kDqQTile;
-  };
-  auto wstage = [&](int s) {
-    return s == 0 ? stage_ptr(sc) : s == 1 ? stage_ptr(sc) + kDqWStage : stage_ptr(sb) + kDqWStage;
-  };
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < 3; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-      mbar_init(&full2[s], 1);
-      mbar_init(&empty2[s], 1);
-    }
-    mbar_init(&tfull[0], 1);
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull2[a], 1);
-      mbar_init(&tempty2[a], kEpilogueThreads);
-    }
-    for (int i = 0; i < 2 * kEpilogueWarps; ++i) mbar_init(&in_bars[i], 1);
-    mbar_init(h_ready, kEpilogueWarps);
-    mbar_init(mma_drain, 1);
-    *abort_flag = 0;
-    *in_armed = 0;
-    fence_mbar_init();
-    tma_prefetch_map(&tmA);
-    tma_prefetch_map(&tmB);
-    tma_prefetch_map(&tmX);
-    tma_prefetch_map(&tmW);
-    tma_prefetch_map(&tmQ);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
-    tmem_relinquish();
-  }
-  epi1.init(extra1, threadIdx.x, kGemmThreads);  // weights only: may overlap the previous kernel
-  epi2.init(extra2, threadIdx.x, kGemmThreads);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp >= 2) {  // the down projection's accumulator starts at its bias
-    const int q = warp & 3, half = (warp - 2) >> 2;
-    epi1.fill_acc(*tmem_slot + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(half * 192),
-                  extra1, half);
-    tmem_st_wait();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  pdl_wait();  // activations of the previous kernel are complete from here on
-  pdl_trigger();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, armed = 0, last_parity = 0;
-      bool ok = true;
-      auto next = [&] {
-        if (++stage == 3) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      };
-      auto take = [&](int st, uint32_t ph) {  // a phase-1 stage is free (its MMAs completed)
-        if (mbar_wait(&empty[st], ph ^ 1u, abort_flag)) return true;
-        report(status, kErrProducerWait);
-        *abort_flag = 1;
-        return false;
-      };
-      for (int kb = 0; ok && kb < k_blocks; ++kb) {
-        if (!(ok = take(stage, phase))) break;
-        uint8_t *a = stage_ptr(stage);
-        mbar_arrive_expect_tx(&full[stage], C::kA + 2 * C::kBBox * BK * 2);
-        tma_load_2d(a, &tmA, &full[stage], kb * BK, m0);
-        for (int s = 0; s < 2; ++s)
-          tma_load_2d(a + C::kA + s * C::kBBox * BK * 2, &tmB, &full[stage], kb * BK, s * C::kBBox);
-        armed |= 1u << stage;
-        last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-        next();
-      }
-      // Each epilogue warp's x blocks (its lane quarter's 32 rows, its 192 columns) into its h
-      // tile slots: tiles 0-3 once s_a is free (after the last-but-two k-block), 4-5 once s_b is.
-      for (int part = 0; ok && part < 2; ++part) {
-        if (!(ok = take(stage, phase))) break;
-        if (part == 0) {
-          *in_armed = kEpilogueWarps;
-          for (int ew = 0; ew < kEpilogueWarps; ++ew)
-            mbar_arrive_expect_tx(&in_bars[2 * ew], 3 * EpiResidLN::kBlockBytes);
-        }
-        for (int ew = 0; ew < kEpilogueWarps; ++ew) {
-          const int q = (ew + 2) & 3, half = ew >> 2;
-          for (int b = 0; b < 3; ++b) {
-            const int kb = 3 * half + b;
-            if ((kb < 4) == (part == 0))
-              tma_load_2d(htile(kb) + q * EpiResidLN::kBlockBytes, &tmX, &in_bars[2 * ew],
-                          half * 192 + 64 * b, m0 + 32 * q);
-          }
-        }
-        next();
-      }
-      // QKV weights: s_c takes two weight stages once the last k-block's MMAs are done.
-      if (ok) ok = take(stage, phase);
-      int s2 = 0;
-      uint32_t ph2 = 0, armed2 = 0, last2 = 0;
-      for (int u = 0; ok && u < 5; ++u) {
-        const int boxes = u < 4 ? 2 : 1;
-        for (int kb = 0; kb < kHidden / BK; ++kb) {
-          if (!mbar_wait(&empty2[s2], ph2 ^ 1u, abort_flag)) {
-            report(status, kErrProducerWait);
-            *abort_flag = 1;
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full2[s2], boxes * 128 * BK * 2);
-          for (int bx = 0; bx < boxes; ++bx)
-            tma_load_2d(wstage(s2) + bx * 128 * BK * 2, &tmW, &full2[s2], kb * BK,
-                        256 * u + 128 * bx);
-          armed2 |= 1u << s2;
-          last2 = (last2 & ~(1u << s2)) | (ph2 << s2);
-          if (++s2 == 3) {
-            s2 = 0;
-            ph2 ^= 1u;
-          }
-        }
-      }
-      // copies still in flight (only after an abort) land before shared memory is released
-      for (int st = 0; st < 3; ++st) {
-        if ((armed >> st) & 1u) mbar_drain(&full[st], (last_parity >> st) & 1u);
-        if ((armed2 >> st) & 1u) mbar_drain(&full2[st], (last2 >> st) & 1u);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      bool ok = true;
-      {  // the down projection: two N=192 MMAs per K step onto the bias in TMEM
-        constexpr uint32_t idesc = idesc_f16_f32(BM, 192, false);
-        int stage = 0;
-        uint32_t phase = 0;
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!(ok = mbar_wait(&full[stage], phase, abort_flag))) break;
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(stage_ptr(stage));
-          const uint64_t adesc = sw128_desc(a_addr);
-#pragma unroll
-          for (int s = 0; s < 2; ++s) {
-            const uint64_t bdesc = sw128_desc(a_addr + C::kA + s * 192 * BK * 2);
-#pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              umma_f16(tmem_base + s * 192, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
-          }
-          umma_commit(&empty[stage]);
-          if (++stage == 3) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (ok) umma_commit(&tfull[0]);
-      }
-      // the QKV GEMM, once h is in its tiles and the LayerNorm has read its rows out of TMEM
-      if (ok) ok = mbar_wait(h_ready, 0, abort_flag);
-      tc_fence_after();
-      int s2 = 0;
-      uint32_t ph2 = 0;
-      for (int u = 0; ok && u < 5; ++u) {
-        const int acc = u & 1;
-        if (u >= 2 && !(ok = mbar_wait(&tempty2[acc], ((u >> 1) - 1) & 1u, abort_flag))) break;
-        tc_fence_after();
-        const uint32_t idesc = u < 4 ? idesc_f16_f32(BM, 256, false) : idesc_f16_f32(BM, 128, false);
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * 256);
-        for (int kb = 0; kb < kHidden / BK; ++kb) {
-          if (!(ok = mbar_wait(&full2[s2], ph2, abort_flag))) break;
-          tc_fence_after();
-          const uint64_t adesc = sw128_desc(smem_u32(htile(kb)));
-          const uint64_t bdesc = sw128_desc(smem_u32(wstage(s2)));
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&empty2[s2]);
-          if (++s2 == 3) {
-            s2 = 0;
-            ph2 ^= 1u;
-          }
-        }
-        if (ok) umma_commit(&tfull2[acc]);
-      }
-      if (!ok) {
-        report(status, kErrMmaWait);
-        *abort_flag = 1;
-      }
-      umma_commit(mma_drain);  // every MMA issued has completed before TMEM is freed
-      mbar_drain(mma_drain, 0);
-    }
-  } else {
-    const int ew = warp - 2, q = warp & 3, half = ew >> 2;
-    const int r = q * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    EpiCtx ctx;
-    ctx.M = M;
-    ctx.half = half;
-    ctx.r = r;
-    ctx.lane = lane;
-    ctx.row = m0 + r;
-    ctx.row0 = m0 + q * 32;
-    ctx.smem = extra1;
-    ctx.staging = htile(3 * half) + q * EpiResidLN::kBlockBytes;
-    for (int b = 0; b < 3; ++b) ctx.blocks[b] = htile(3 * half + b) + q * EpiResidLN::kBlockBytes;
-    ctx.h_in_smem = true;
-    ctx.buf = 0;
-    ctx.nbuf = 1;
-    ctx.narrow = false;
-    ctx.split = 0;
-    ctx.out_map = &tmX;
-    ctx.ln_map = &tmX;  // unused: h stays in shared memory
-    ctx.in_bar = in_bars + 2 * ew;
-    ctx.iter = 0;
-    ctx.abort_flag = abort_flag;
-    ctx.failed = false;
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[0], 0, abort_flag));
-    {  // a warp without its accumulator still meets its partner at the LayerNorm's barrier
-      ctx.failed = !ok;
-      tc_fence_after();
-      EpiResidLN::Pre pre;
-      epi1.template run<192>(tmem_base + lane_base + static_cast<uint32_t>(half * 192), half * 192,
-                             ctx, pre);
-      ok = !ctx.failed;
-    }
-    // h written (generic proxy) and read by the MMAs (async proxy); TMEM rows read
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(h_ready);
-    EpiCtx c2 = ctx;
-    c2.smem = extra2;
-    c2.staging = staging2 + ew * kStageBlockBytes;
-    c2.out_map = &tmQ;
-    c2.h_in_smem = false;
-    EpiQkvRope::Pre pre2;
-    for (int u = 0; ok && u < 5; ++u) {
-      const int acc = u & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull2[acc], (u >> 1) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool narrow = u == 4;
-      c2.narrow = narrow;
-      const uint32_t col_off = narrow ? 0u : static_cast<uint32_t>(half * 128);
-      epi2.template run<128>(tmem_base + lane_base + static_cast<uint32_t>(acc * 256) + col_off,
-                             256 * u + (narrow ? 0 : half * 128), c2, pre2);
-      tc_fence_before();
-      mbar_arrive(&tempty2[acc]);
-    }
-    if (!ok && lane == 0) {
-      report(status, kErrEpilogueWait);
-      *abort_flag = 1;
-    }
-    if (lane == 0) bulk_wait<0>();  // stores done before the CTA retires
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0)  // x blocks requested but never consumed (after an abort) land first
-    for (int ew = 0; ew < *in_armed; ++ew) mbar_drain(&in_bars[2 * ew], 0);
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
-  }
-}
-
-bool make_down_qkv_maps(const void *act, uint32_t rows, const void *down_w, void *x,
-                        const void *qkv_w, void *qkv, DownQkvMaps *maps, std::string *err) {
-  return encode_map_f16(&maps->a, act, kMlp, rows, BK, BM, err) &&
-         encode_map_f16(&maps->b, down_w, kMlp, kHidden, BK, 192, err) &&
-         encode_map_f16_swizzled(&maps->x, x, kHidden, rows, 64, 32, 128, err) &&
-         encode_map_f16(&maps->w, qkv_w, kHidden, kQkv, BK, 128, err) &&
-         encode_map_f16_swizzled(&maps->qkv, qkv, kQkv, rows, 32, 32, 64, err);
-}
-
-cudaError_t launch_down_qkv(const DownQkvMaps &maps, uint32_t rows, const GemmArgs &down,
-                            const GemmArgs &qkv, uint32_t *status, cudaStream_t stream) {
-  if (rows == 0) return cudaSuccess;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint32_t m_tiles = (rows + BM - 1) / BM;
-  if (m_tiles > static_cast<uint32_t>(sm_count(dev)) || down.ln_out_f32) return cudaErrorInvalidValue;
-  static bool configured[64] = {};
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(down_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kDqSmem);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
-  return launch_pdl(down_qkv_kernel, dim3(m_tiles), dim3(kGemmThreads), kDqSmem, stream, maps.a,
-                    maps.b, maps.x, maps.w, maps.qkv, static_cast<int>(rows), kMlp / BK,
-                    EpiResidLN{down.bias, down.lambda, down.gamma, down.beta, false},
-                    EpiQkvRope{qkv.bias, qkv.rope_cos, qkv.rope_sin}, status);
-}
-
 // The residual GEMMs run on full 384-wide rows (one tile per CTA, A read once: about 0.56 us per
 // 64-deep k-block for three 128-column tiles' worth of MMAs, against 0.31 us per k-block for one
 // 128-wide tile; the LayerNorm fused) once the row tiles outnumber half the SMs, as long as they
@@ -1001,18 +536,31 @@ bool resid_wide(uint32_t rows) {
 }
 
 // Partial slabs of the no-alloc split-K entry point (dv3k_down_splitk_noalloc): a file-scope
-// device array, so that call needs no workspace from its caller and allocates nothing. Sized for
-// the largest splits x rows the plan uses (2 slices of 3015 rows at batch 15; 8 of 603 at 3).
+// device array, so that call needs no workspace from its caller and allocates nothing. Its size
+// is fixed when the library is built (6144 partial rows of 384 floats, 9 MiB on every device that
+// loads the library); it is not derived from splitk_splits, which may pick more slices on a GPU
+// with more SMs. 6144 covers the slices the model's plan takes on a 148-SM B200 (2 slices of 3015
+// rows at batch 15, 8 of 603 at batch 3); callers size splits x rows to fit it.
 constexpr size_t kSplitkScratchFloats = static_cast<size_t>(6144) * kHidden;
 static __device__ __align__(256) float g_splitk_scratch[kSplitkScratchFloats];
 
+// The array's device address is looked up once per device (with that device current) under a
+// lock, so concurrent first calls from several host threads are safe. The address belongs to the
+// device's primary context: a cudaDeviceReset of that device invalidates it, as it does every
+// other device resource of this library.
 float *splitk_scratch(size_t *capacity_floats) {
+  static std::mutex lock;
   static void *addr[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev] && cudaGetSymbolAddress(&addr[dev], g_splitk_scratch) != cudaSuccess) {
-    addr[dev] = nullptr;
-    return nullptr;
+  std::lock_guard<std::mutex> guard(lock);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_splitk_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    addr[dev] = p;
   }
   if (capacity_floats) *capacity_floats = kSplitkScratchFloats;
   return static_cast<float *>(addr[dev]);
@@ -1046,7 +594,6 @@ GemmShape gemm_shape(GemmOp op) {
     case GemmOp::ResidLN384: return {384, kHidden, kHidden};
     case GemmOp::ResidLN1536: return {384, kHidden, kMlp};
     case GemmOp::SplitK1536: return {128, kHidden, kMlp};
-    case GemmOp::PatchPixels: return {384, kHidden, kPatchK};
   }
   return {0, 0, 0};
 }
@@ -1061,7 +608,6 @@ const char *gemm_name(GemmOp op) {
     case GemmOp::ResidLN384: return "gemm_o_resid_layernorm";
     case GemmOp::ResidLN1536: return "gemm_down_resid_layernorm";
     case GemmOp::SplitK1536: return "gemm_down_splitk";
-    case GemmOp::PatchPixels: return "gemm_patch_pixels";
   }
   return "?";
 }
@@ -1091,10 +637,7 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
       (s.bn == 128 && (op == GemmOp::Resid384 || op == GemmOp::Resid1536 || op == GemmOp::Patch));
   const uint32_t b_rows = s.bn >= 256 || narrow_ops ? s.bn / 2 : s.bn;
   if (!encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err)) return false;
-  if (op == GemmOp::PatchPixels)
-    maps->a = maps->b;  // no A map: the epilogue warps build the A tiles from the images
-  else if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err))
-    return false;
+  if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err)) return false;
   maps->d = maps->a;  // unused unless the epilogue writes a LayerNorm output
   if (op == GemmOp::SplitK1536)  // f32 partial slabs [splits][rows][384], 32x32 blocks
     return encode_map_f32_slabs(&maps->c, out, kHidden, rows, splits, 32, err);
@@ -1156,13 +699,14 @@ template <int BN, class Epi>
 static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k, const Epi &epi,
                               uint32_t *status, cudaStream_t stream, const GemmArgs &args,
                               int k_splits = 1) {
-  static bool configured[64] = {};  // per template instance and device
+  static std::atomic<bool> configured[64] = {};  // per template instance and device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev >= 0 && dev < 64 && !configured[dev].load(std::memory_order_acquire)) {
+    // setting the attribute twice (two threads racing here) is harmless
     cudaError_t e = configure_one<BN, Epi>();
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   TileSched sched = tile_sched<BN, Epi>(rows, n, sm_count(dev), k_splits);
   sched.l2_next = args.l2_next;
@@ -1184,10 +728,6 @@ cudaError_t configure_gemm_kernels() {
   if ((e = configure_one<256, EpiSwiGLU>()) != cudaSuccess) return e;
   if ((e = configure_one<384, EpiResidLN>()) != cudaSuccess) return e;
   if ((e = configure_one<128, EpiPartialF32>()) != cudaSuccess) return e;
-  if ((e = configure_one<384, EpiPatchPixels>()) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(down_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kDqSmem)) != cudaSuccess)
-    return e;
   int dev = 0;
   cudaGetDevice(&dev);
   sm_count(dev);
@@ -1225,17 +765,6 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
       if (args.splits == 0 || (kMlp / BK) % args.splits != 0) return cudaErrorInvalidValue;
       return launch_one<128>(maps, rows, s.n, s.k, EpiPartialF32{}, status, stream, args,
                              static_cast<int>(args.splits));
-    case GemmOp::PatchPixels: {
-      // one tile per CTA: at most one wave of 128-row tiles (96 images on 148 SMs)
-      int dev = 0;
-      cudaGetDevice(&dev);
-      if (!args.images || !args.prefix || !args.out || rows % kPatches != 0 ||
-          (rows + BM - 1) / BM > static_cast<uint32_t>(sm_count(dev)))
-        return cudaErrorInvalidValue;
-      return launch_one<384>(maps, rows, s.n, s.k,
-                             EpiPatchPixels{args.bias, args.out, args.images, args.prefix},
-                             status, stream, args);
-    }
   }
   return cudaErrorInvalidValue;
 }

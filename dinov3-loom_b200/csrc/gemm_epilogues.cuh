@@ -63,7 +63,6 @@ struct EpiCtx {
   volatile int *abort_flag;
   bool failed;         // a bounded wait expired inside run()
   uint8_t *blocks[3];  // EpiResidLN: this warp's three 4 KB staging blocks
-  bool h_in_smem;      // EpiResidLN: h stays in the staging blocks (the fused QKV reads it)
 };
 
 struct NoPre {};
@@ -202,65 +201,6 @@ struct EpiPatch {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] += u2f(r[i]);
       if (ok) store_half32(x + static_cast<size_t>(token) * kHidden + n0 + k, v);
-    }
-  }
-};
-
-// ---------------------------------------------------------------------------------------------
-// Patch embedding with the patchify fused into the mainloop (GemmOp::PatchPixels, full 384-wide
-// rows, one tile per CTA): the epilogue warps build the A tiles from the images while the
-// producer loads the weights (pixel_a_tiles in gemm.cu), and the accumulator starts at the bias.
-// The epilogue writes x[(p/196)*201 + 5 + p%196] = f16(acc) for its row's 192 columns, and the
-// thread of each image's first patch row also writes that image's 5 prefix rows (CLS and
-// register tokens, f16 of the f32 weights: the prefix half of kernels/embed_scatter_f32.loom).
-// ---------------------------------------------------------------------------------------------
-struct EpiPatchPixels {
-  const float *bias;
-  __half *x;
-  const float *images;
-  const float *prefix;
-  static constexpr int kSmem = kHidden * 4;
-  static constexpr bool kTmaStore = false;
-  static constexpr bool kBiasInTmem = true;
-  static constexpr bool kAFromPixels = true;
-  using Pre = NoPre;
-  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
-  __device__ void init(uint8_t *smem, int tid, int n) const {
-    stage_floats(reinterpret_cast<float *>(smem), bias, kHidden, tid, n);
-  }
-  __device__ void fill_acc(uint32_t taddr, const uint8_t *smem, int half) const {
-    fill_acc_bias192(taddr, reinterpret_cast<const float *>(smem) + half * (kHidden / 2));
-  }
-  template <int COLS>
-  __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &) const {
-    static_assert(COLS == 192, "a column half of a full row");
-    const bool ok = c.row < c.M;
-    const int img = c.row / kPatches, pp = c.row % kPatches;
-    __half *dst = x + (static_cast<size_t>(img) * kTokens + kPrefix + pp) * kHidden + n0;
-    uint32_t ra[32], rb[32];
-    tmem_ld32(taddr, ra);
-#pragma unroll
-    for (int j = 0; j < COLS / 32; ++j) {
-      uint32_t(&r)[32] = (j & 1) ? rb : ra;
-      uint32_t(&rn)[32] = (j & 1) ? ra : rb;
-      tmem_wait_ld(r);
-      if (j + 1 < COLS / 32) tmem_ld32(taddr + 32 * (j + 1), rn);
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = u2f(r[i]);
-      if (ok) store_half32(dst + 32 * j, v);
-    }
-    if (ok && pp == 0) {
-      __half *pre_dst = x + static_cast<size_t>(img) * kTokens * kHidden + n0;
-#pragma unroll 1
-      for (int t = 0; t < kPrefix; ++t) {
-#pragma unroll
-        for (int j = 0; j < COLS / 32; ++j) {
-          float v[32];
-          ldg32(prefix + t * kHidden + n0 + 32 * j, v);
-          store_half32(pre_dst + t * kHidden + 32 * j, v);
-        }
-      }
     }
   }
 };
@@ -751,17 +691,14 @@ struct EpiResidLN {
       }
       if (!f32_out) {
         uint8_t *rowp = c.blocks[j >> 1] + c.lane * 128;
-        if (!(j & 1)) {  // with h kept in shared memory no h stores join the groups: wait for all
-          if (c.lane == 0) {
-            if (c.h_in_smem) bulk_wait_read<0>();
-            else bulk_wait_read<2>();
-          }
+        if (!(j & 1)) {
+          if (c.lane == 0) bulk_wait_read<2>();
           __syncwarp();
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           *reinterpret_cast<uint4 *>(rowp + ((((j & 1) * 4 + k) ^ sw) << 4)) = pack8(y, k);
-        if ((j & 1) && !c.h_in_smem) {
+        if (j & 1) {
           fence_proxy_async_smem();
           __syncwarp();
           if (c.lane == 0) {

@@ -51,11 +51,7 @@ bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uin
 // rows, followed in the same kernel by the LayerNorm of the updated row into ln_out (f16) or
 // ln_out_f32. SplitK1536: the down projection's K split into `splits` slices, each CTA writing
 // the f32 partial product of its slice (no bias) into slab s of partials [splits][rows][384]
-// (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it. PatchPixels: the patch
-// embedding with the patchify fused into its A operand: the epilogue warps build each A tile from
-// the f32 NCHW images (`images`, f16 rounding as patchify, non-finite pixels flagged in
-// status[1]) while the producer loads only the weights; full 384-wide rows, one tile per CTA; the
-// epilogue writes the patch rows and each image's prefix rows (`prefix`) of x.
+// (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it.
 enum class GemmOp {
   Patch,
   QkvRope,
@@ -64,8 +60,7 @@ enum class GemmOp {
   SwiGLU,
   ResidLN384,
   ResidLN1536,
-  SplitK1536,
-  PatchPixels
+  SplitK1536
 };
 
 struct GemmShape {
@@ -88,10 +83,9 @@ struct GemmMaps {
   CUtensorMap c;  // the epilogue's output, for epilogues that store through TMA
   CUtensorMap d;  // ResidLN*: the LayerNorm output (f16 h, or the f32 final output)
 };
-// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch and PatchPixels, which
-// write x through GemmArgs). PatchPixels takes no `a` (null): its A operand comes from the images.
-// ResidLN* also takes
-// the LayerNorm output: `ln_out` f16 [rows][384], or f32 when `ln_f32`.
+// `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch, which writes x through
+// GemmArgs). ResidLN* also takes the LayerNorm output: `ln_out` f16 [rows][384], or f32 when
+// `ln_f32`.
 // SplitK1536: `out` is the f32 partials [splits][rows][384].
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
                     GemmMaps *maps, std::string *err, const void *ln_out = nullptr,
@@ -108,27 +102,12 @@ struct GemmArgs {
   __half *ln_out = nullptr;      // ResidLN*: f16 LayerNorm output, or
   float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
   float *partials = nullptr;     // SplitK1536: [splits][rows][384] f32
-  const float *images = nullptr;  // PatchPixels: f32 NCHW images, rows / 196 of them
-  const float *prefix = nullptr;  // PatchPixels: the 5 prefix rows (CLS, registers) f32 [5][384]
   uint32_t splits = 1;           // SplitK1536: K slices (a divisor of 24, the 64-wide k-blocks)
   // Weights of a later kernel (16-byte aligned; no kernel writes them) that this launch starts
   // toward L2, so that kernel's first tiles do not wait for DRAM.
   const void *l2_next = nullptr;
   size_t l2_next_bytes = 0;
 };
-
-// The down projection of one layer with its residual update and the next layer's LN1, then that
-// layer's QKV GEMM with RoPE on the LayerNorm's rows, in one kernel (one 128-row tile per CTA,
-// h kept in shared memory; at most one wave of tiles). `down`: bias, lambda, gamma, beta of the
-// residual + LayerNorm (x updated in place); `qkv`: bias, rope_cos, rope_sin. Maps: act
-// [rows][1536], down_w [384][1536], x [rows][384], qkv_w [1152][384], qkv [rows][1152].
-struct DownQkvMaps {
-  CUtensorMap a, b, x, w, qkv;
-};
-bool make_down_qkv_maps(const void *act, uint32_t rows, const void *down_w, void *x,
-                        const void *qkv_w, void *qkv, DownQkvMaps *maps, std::string *err);
-cudaError_t launch_down_qkv(const DownQkvMaps &maps, uint32_t rows, const GemmArgs &down,
-                            const GemmArgs &qkv, uint32_t *status, cudaStream_t stream);
 
 // The K split of the down projection over `rows` rows in the model's plan: the most slices (at
 // most 8, a divisor of 24, so each CTA walks at least three 64-wide k-blocks) whose

@@ -170,9 +170,10 @@ Model::Model(const std::string &path, dv3_options options)
          "allocate pinned status");
     for (int i = 0; i < 4; ++i) slot_status_host_[i] = 0;
     cuda(cudaMemset(status_, 0, 256), "clear status");
-    cuda(cudaMallocHost(reinterpret_cast<void **>(&status_host_), 2 * sizeof(uint32_t)),
+    cuda(cudaMallocHost(reinterpret_cast<void **>(&status_host_), 4 * sizeof(uint32_t)),
          "allocate pinned status");
-    status_host_[0] = status_host_[1] = 0;
+    status_host_[0] = status_host_[1] = status_host_[2] = 0;
+    inject_host_ = status_host_ + 2;
   } catch (...) {
     release();
     throw;
@@ -201,6 +202,7 @@ void Model::release() {
   if (slot_status_host_) cudaFreeHost(slot_status_host_);
   slot_status_host_ = nullptr;
   if (status_host_) cudaFreeHost(status_host_);
+  inject_host_ = nullptr;
   if (act_blob_) cudaFree(act_blob_);
   if (weight_blob_) cudaFree(weight_blob_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -211,7 +213,7 @@ void Model::release() {
 }
 
 // The launch plan of one batch size (src/lib.rs:149-263): patchify, the patch GEMM (with the
-// embed scatter; or both in one launch, PatchPixels, with DV3_FUSE_PATCHIFY=1), LN1 of layer 0,
+// embed scatter), LN1 of layer 0,
 // then per layer QKV+RoPE, attention, o-proj+LS1+residual+LN2, gate/up+SwiGLU, and
 // down-proj+LS2+residual+(LN1 of the next layer | final LN). The reference launches each
 // LayerNorm separately (87 launches at b > 1); here each one after layer 0's first rides in the
@@ -231,28 +233,6 @@ uint32_t Model::down_splits(uint32_t rows) const {
 bool Model::fuse_layernorm(size_t b) const {
   if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
   return resid_wide(static_cast<uint32_t>(kTokens * b));
-}
-
-// Whether each down projection (layers 0-10, full-row plans only) also runs the next layer's QKV
-// GEMM on the LayerNorm rows it keeps in shared memory (launch_down_qkv: one launch instead of
-// two, h not written; bit for bit the same output). Off unless DV3_FUSE_QKV=1: its QKV phase
-// follows the LayerNorm serially on 101 CTAs with three 32 KB weight stages, and the batch-64
-// forward measured 1.246 against 1.189 ms.
-bool Model::fuse_qkv(size_t b) const {
-  if (!fuse_layernorm(b)) return false;
-  if (const char *v = std::getenv("DV3_FUSE_QKV")) return v[0] == '1';
-  return false;
-}
-
-// Whether the patch GEMM builds its A tiles from the images itself (GemmOp::PatchPixels: one
-// launch instead of patchify + patch GEMM, no f16 patch matrix in memory). Off unless
-// DV3_FUSE_PATCHIFY=1: its one full-row tile per CTA (98 CTAs at batch 64, 2 at batch 1) waits
-// on pixel reads that patchify streams at full bandwidth, and measured slower at every batch
-// size tried (batch 64: 1.189 against 1.184 ms per forward; batch 1: 0.400 against 0.382 ms).
-bool Model::fuse_patchify(size_t b) const {
-  if (const char *v = std::getenv("DV3_FUSE_PATCHIFY")) return v[0] == '1';
-  (void)b;
-  return false;
 }
 
 // Bytes of each projection's f16 weights. Each launch of the plan starts the weights of a GEMM
@@ -284,27 +264,22 @@ Plan &Model::prepare(size_t b, int slot) {
   float *image = image_slot_[slot], *out = out_slot_[slot];
   __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
 
-  const bool pix = fuse_patchify(b);
-  const GemmOp patch_op = pix ? GemmOp::PatchPixels : GemmOp::Patch;
   GemmMaps patch_maps;
-  need(make_gemm_maps(patch_op, patches, p, w.patch_w, x, &patch_maps, &err));
+  need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, x, &patch_maps, &err));
   AttentionMaps attn_map;
   need(make_attention_map(qkv, attn, r, &attn_map, &err));
 
-  if (!pix)
-    add("patchify", [=](cudaStream_t s) {
-      return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s,
-                             w.patch_w, size_t{kHidden} * kPatchK * 2);
-    });
-  add(gemm_name(patch_op), [=](cudaStream_t s) {
+  add("patchify", [=](cudaStream_t s) {
+    return launch_patchify(image, static_cast<uint32_t>(b), w.prefix, patches, x, st, s,
+                           w.patch_w, size_t{kHidden} * kPatchK * 2);
+  });
+  add(gemm_name(GemmOp::Patch), [=](cudaStream_t s) {
     GemmArgs g;
     g.l2_next = w.layer[0].qkv_w;
     g.l2_next_bytes = kQkvWBytes;
     g.bias = w.patch_b;
     g.out = x;
-    g.images = image;    // PatchPixels
-    g.prefix = w.prefix;
-    return launch_gemm(patch_op, patch_maps, p, g, st, s);
+    return launch_gemm(GemmOp::Patch, patch_maps, p, g, st, s);
   });
   add("layernorm_f16", [=](cudaStream_t s) {
     return launch_layernorm_f16(x, r, w.layer[0].norm1_w, w.layer[0].norm1_b, h, s);
@@ -317,13 +292,9 @@ Plan &Model::prepare(size_t b, int slot) {
   // reference splits K at batch 1, src/lib.rs:218-226).
   const uint32_t splits = fuse ? 1u : down_splits(r);
   float *partials = partials_;
-  const bool fqkv = fuse_qkv(b) && splits == 1;
   for (int i = 0; i < 12; ++i) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
-    DownQkvMaps dq_maps;
-    if (fqkv && i < 11)
-      need(make_down_qkv_maps(act, r, l.down_w, x, w.layer[i + 1].qkv_w, qkv, &dq_maps, &err));
     need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, qkv, &qkv_maps, &err));
     need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err, h));
     need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, act, &gu_maps, &err));
@@ -334,7 +305,6 @@ Plan &Model::prepare(size_t b, int slot) {
       need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err,
                           i == 11 ? static_cast<const void *>(out) : static_cast<const void *>(h),
                           i == 11));
-    if (!(fqkv && i > 0))  // else the previous layer's down projection ran this QKV
     add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;
@@ -390,21 +360,6 @@ Plan &Model::prepare(size_t b, int slot) {
       add("splitk_reduce_layernorm", [=](cudaStream_t s) {
         return launch_splitk_reduce(partials, r, splits, l.down_b, l.ls2, x, ng, nb,
                                     last ? nullptr : h, last ? out : nullptr, s);
-      });
-      continue;
-    }
-    if (fqkv && !last) {
-      const LayerWeights &n = w.layer[i + 1];
-      add("gemm_down_ln_qkv", [=](cudaStream_t s) {
-        GemmArgs d, q;
-        d.bias = l.down_b;
-        d.lambda = l.ls2;
-        d.gamma = ng;
-        d.beta = nb;
-        q.bias = n.qkv_b;
-        q.rope_cos = w.rope_cos;
-        q.rope_sin = w.rope_sin;
-        return launch_down_qkv(dq_maps, r, d, q, st, s);
       });
       continue;
     }
@@ -488,6 +443,7 @@ void Model::forward(const float *pixels, size_t n_floats, float *out, size_t out
                          cudaMemcpyHostToDevice, stream_),
          "upload input");
     cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+    apply_injection();
     if (readout == Readout::Full) {
       cuda(cudaMemcpyAsync(out + i * per, out_, b * per * sizeof(float), cudaMemcpyDeviceToHost,
                            stream_),
@@ -525,6 +481,7 @@ void Model::forward_device(const float *pixels, size_t n_floats, float *out, siz
                          cudaMemcpyDeviceToDevice, stream_),
          "copy input");
     cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+    apply_injection();
     cuda(cudaMemcpyAsync(out + i * per, out_, b * per * sizeof(float), cudaMemcpyDeviceToDevice, stream_),
          "copy output");
     status_pending_ = true;
@@ -563,6 +520,7 @@ uint64_t Model::submit(const float *pixels, size_t n_floats, float *out, size_t 
   cuda(cudaStreamWaitEvent(stream_, ev_out_[slot], 0), "order forward");
   cuda(cudaMemsetAsync(status_, 0, 2 * sizeof(uint32_t), stream_), "clear status");
   cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+  apply_injection();
   cuda(cudaMemcpyAsync(slot_status_host_ + 2 * slot, status_, 2 * sizeof(uint32_t),
                        cudaMemcpyDeviceToHost, stream_),
        "read status");
@@ -619,7 +577,24 @@ void Model::run(size_t batch) {
   activate();
   Plan &plan = prepare(batch);
   cuda(cudaGraphLaunch(plan.exec, stream_), "launch graph");
+  apply_injection();
   status_pending_ = true;
+}
+
+void Model::inject_fault(uint32_t bits) {
+  check_usable();
+  if (bits == 0) throw Error(DV3_INVALID_ARGUMENT, "inject at least one failure bit");
+  *inject_host_ = bits;
+  inject_pending_ = true;
+}
+
+// The injected bits land in the failure word on the compute stream after the forward's kernels
+// and before its status is read, exactly where a kernel's expired wait would have put them.
+void Model::apply_injection() {
+  if (!inject_pending_) return;
+  inject_pending_ = false;
+  cuda(cudaMemcpyAsync(status_, inject_host_, sizeof(uint32_t), cudaMemcpyHostToDevice, stream_),
+       "inject failure bits");
 }
 
 void Model::synchronize() {
@@ -728,6 +703,65 @@ std::vector<std::pair<const char *, double>> Model::profile_launches(size_t batc
   }
   for (auto &e : ev) cudaEventDestroy(e);
   check_status();
+  return result;
+}
+
+// Per-launch device time inside whole forwards, in the production plan's order and with its
+// cache state: each of `replays` forwards of the staged input is preceded by a write of
+// `flush_bytes` bytes to a scratch buffer (evicting L2 when larger than it, as between timed
+// steps), then its launches are enqueued directly on the model's stream with an event recorded
+// before the first and after each one; a launch's time is the interval between the events
+// around it, averaged over the replays. The flush gives the host a head start, so every kernel
+// is queued before the previous one ends. Between two events the next kernel cannot start its
+// set-up early (the graph lets it overlap the previous kernel's tail), so the sum of the launch
+// times slightly exceeds one graph replay. The scratch buffer is allocated for the call and
+// freed after it.
+std::vector<std::pair<const char *, double>> Model::profile_forward(size_t batch, size_t replays,
+                                                                    size_t flush_bytes) {
+  drain();
+  check_usable();
+  if (batch < 1 || batch > max_batch_)
+    throw Error(DV3_INVALID_ARGUMENT, "batch must be 1..=max_batch");
+  if (replays < 1) throw Error(DV3_INVALID_ARGUMENT, "replays must be >= 1");
+  activate();
+  Plan &plan = prepare(batch);
+  const size_t n = plan.launches.size();
+  std::vector<cudaEvent_t> ev(n + 1, nullptr);
+  void *flush = nullptr;
+  auto release_all = [&] {
+    for (auto &e : ev)
+      if (e) cudaEventDestroy(e);
+    if (flush) cudaFree(flush);
+    flush = nullptr;
+  };
+  std::vector<double> total(n, 0.0);
+  try {
+    for (auto &e : ev) cuda(cudaEventCreate(&e), "create event");
+    if (flush_bytes) cuda(cudaMalloc(&flush, flush_bytes), "allocate flush buffer");
+    for (size_t r = 0; r < replays; ++r) {
+      if (flush)
+        cuda(cudaMemsetAsync(flush, static_cast<int>(r & 0xff), flush_bytes, stream_), "flush L2");
+      cuda(cudaEventRecord(ev[0], stream_), "record event");
+      for (size_t j = 0; j < n; ++j) {
+        cuda(plan.launches[j].enqueue(stream_), plan.launches[j].name);
+        cuda(cudaEventRecord(ev[j + 1], stream_), "record event");
+      }
+      cuda(cudaEventSynchronize(ev[n]), "synchronize");
+      for (size_t j = 0; j < n; ++j) {
+        float ms = 0;
+        cuda(cudaEventElapsedTime(&ms, ev[j], ev[j + 1]), "elapsed time");
+        total[j] += ms;
+      }
+    }
+  } catch (...) {
+    release_all();
+    throw;
+  }
+  release_all();
+  check_status();
+  std::vector<std::pair<const char *, double>> result;
+  for (size_t j = 0; j < n; ++j)
+    result.emplace_back(plan.launches[j].name, total[j] / static_cast<double>(replays));
   return result;
 }
 

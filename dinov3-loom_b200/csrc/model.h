@@ -73,6 +73,13 @@ class Model {
   dv3_timings benchmark(const float *pixels, size_t n_floats, size_t samples);
   size_t launches_per_forward(size_t batch);
   std::vector<std::pair<const char *, double>> profile_launches(size_t batch, size_t iterations);
+  // Per-launch device time inside whole forwards (see model.cpp).
+  std::vector<std::pair<const char *, double>> profile_forward(size_t batch, size_t replays,
+                                                               size_t flush_bytes);
+  // Test hook (no reference counterpart): the next forward enqueued on this model (any path)
+  // writes `bits` into the device failure word after its kernels, as a kernel whose bounded wait
+  // expired would, so the host sees a device failure without one.
+  void inject_fault(uint32_t bits);
 
   float *input_buffer() const { return image_; }
   float *output_buffer() const { return out_; }
@@ -85,8 +92,6 @@ class Model {
   Plan &prepare(size_t batch, int slot = 0);    // build + capture once per batch size and slot
   void drain();                                  // finish every outstanding submission
   bool fuse_layernorm(size_t batch) const;      // plan variant for this batch size
-  bool fuse_patchify(size_t batch) const;       // patchify inside the patch GEMM
-  bool fuse_qkv(size_t batch) const;            // next QKV inside the down projection
   uint32_t down_splits(uint32_t rows) const;    // split-K slices of the down projection
   void check_status();                          // read the device status words (synchronous)
   void activate() const;
@@ -117,6 +122,9 @@ class Model {
   uint32_t *status_ = nullptr;       // device: [0] failure bits, [1] non-finite input
   uint32_t *status_host_ = nullptr;  // pinned mirror
   bool status_pending_ = false;      // work enqueued since the last status check
+  uint32_t *inject_host_ = nullptr;  // pinned: the failure bits inject_fault asked for
+  bool inject_pending_ = false;
+  void apply_injection();            // enqueue the injected failure bits (if any) on stream_
   std::map<std::pair<size_t, int>, Plan> plans_;
 };
 

@@ -228,6 +228,21 @@ class DINOv3:
                                                 ctypes.byref(count)))
         return [(names[i].decode(), ms[i]) for i in range(min(count.value, cap))]
 
+    def profile_forward(self, batch: int, replays: int = 10, flush_bytes: int = 256 << 20):
+        """[(kernel name, average device ms)] for every launch of one forward, in order, timed
+        inside whole forwards with an L2 flush of `flush_bytes` before each (dv3_profile_forward)."""
+        cap = 256
+        ms = (ctypes.c_double * cap)()
+        names = (ctypes.c_char_p * cap)()
+        count = ctypes.c_size_t()
+        _check(_lib.load().dv3_profile_forward(self._h, batch, replays, flush_bytes, ms, names,
+                                               cap, ctypes.byref(count)))
+        return [(names[i].decode(), ms[i]) for i in range(min(count.value, cap))]
+
+    def debug_inject_fault(self, bits: int = 1 << 30) -> None:
+        """Test hook: the next forward reports a device failure (DV3_POISONED) without one."""
+        _check(_lib.load().dv3_debug_inject_fault(self._h, bits))
+
 
 def pack_f16(name: str, values) -> np.ndarray:
     """The packer's f32 -> f16 narrowing (src/weights.rs:6-17); raises DINOv3Error on the first

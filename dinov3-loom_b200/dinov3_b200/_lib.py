@@ -70,20 +70,20 @@ SIGNATURES = {
     "dv3_wait": ([_P, ctypes.c_uint64], _I),
     "dv3_launches_per_forward": ([_P, _SZ, ctypes.POINTER(_SZ)], _I),
     "dv3_profile_launches": ([_P, _SZ, _SZ, _P, _P, _SZ, ctypes.POINTER(_SZ)], _I),
+    "dv3_profile_forward": ([_P, _SZ, _SZ, _SZ, _P, _P, _SZ, ctypes.POINTER(_SZ)], _I),
+    "dv3_debug_inject_fault": ([_P, _U32], _I),
     "dv3_pack_f16": ([ctypes.c_char_p, _P, _SZ, _P, ctypes.POINTER(_SZ)], _I),
     "dv3_hub_weights": ([_I, ctypes.c_char_p, _SZ], _I),
     "dv3_from_pretrained": ([Options, ctypes.POINTER(_P)], _I),
     # dinov3_kernels.h
     "dv3k_patchify": ([_P, _U32, _P, _P, _P, _P, _P], _I),
     "dv3k_patch_embed": ([_P, _U32, _P, _P, _P, _P, _P], _I),
-    "dv3k_patch_embed_pixels": ([_P, _U32, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_layernorm_f16": ([_P, _U32, _P, _P, _P, _P], _I),
     "dv3k_layernorm_f32out": ([_P, _U32, _P, _P, _P, _P], _I),
     "dv3k_qkv_rope": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_attention": ([_P, _U32, _P, _P, _P], _I),
     "dv3k_matmul_resid": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_resid_layernorm": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
-    "dv3k_down_layernorm_qkv": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_swiglu": ([_P, _U32, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_splitk": ([_P, _U32, _P, _U32, _P, _P, _P], _I),
     "dv3k_splitk_reduce": ([_P, _U32, _U32, _P, _P, _P, _P], _I),

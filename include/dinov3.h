@@ -80,8 +80,10 @@ int dv3_from_pretrained(dv3_options options, dv3_model **out);
 /* DINOv3::forward (src/lib.rs:90-114). `pixels` holds n_floats = k*DV3_IMAGE_ELEMENTS floats
  * (k >= 0); `out` must have room for k*201*384 floats (out_floats). Synchronous. Inputs larger
  * than max_batch are processed in chunks of max_batch. Non-finite input is an error; it is
- * detected on the device while the input is read, so `out` is unspecified on that error.
- * Host buffers may be pageable; pinned buffers transfer faster. */
+ * detected on the device while each chunk is read. On any error `out` is unspecified: the
+ * chunks before the failing one, and the failing chunk itself, may already have been written
+ * (the reference returns a fresh vector instead, src/lib.rs:90-114). Host buffers may be
+ * pageable; pinned buffers transfer faster. */
 int dv3_forward(dv3_model *m, const float *pixels, size_t n_floats, float *out, size_t out_floats);
 
 /* DINOv3::cls (src/lib.rs:126-132): the CLS token of each image, k*384 floats. Only those
@@ -164,6 +166,25 @@ int dv3_launches_per_forward(dv3_model *m, size_t batch, size_t *out);
  * next forward recomputes them). */
 int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *ms,
                          const char **names, size_t capacity, size_t *count);
+
+/* Per-launch device time of the launches of whole forwards of `batch` staged images, in the
+ * plan's order and cache state: each of `replays` forwards is preceded by a write of
+ * `flush_bytes` bytes to a scratch buffer the call allocates (evicting L2 when larger than it;
+ * 0: no flush), its launches are enqueued on the model's stream with an event after each, and a
+ * launch's time is the interval between the events around it, averaged over the replays. Writes
+ * up to `capacity` entries (launch order) of milliseconds and static kernel names, and the
+ * count to *count. The events stop each kernel's set-up from overlapping the previous kernel,
+ * so the sum slightly exceeds one graph replay. */
+int dv3_profile_forward(dv3_model *m, size_t batch, size_t replays, size_t flush_bytes,
+                        double *ms, const char **names, size_t capacity, size_t *count);
+
+/* Test hook (no reference counterpart): the next forward enqueued on `m` (dv3_forward, dv3_cls,
+ * dv3_patch_mean, dv3_run, dv3_submit, dv3_forward_device) writes the nonzero `bits` into the
+ * model's device failure word after its kernels, where a kernel whose bounded wait expired
+ * records its bit, so that forward reports DV3_POISONED and the model stays poisoned
+ * (src/engine.rs:93,168-171), without faulting the GPU. Returns DV3_POISONED on a model that is
+ * already poisoned. */
+int dv3_debug_inject_fault(dv3_model *m, uint32_t bits);
 
 /* ---- Pinned weights in the Hugging Face cache (src/hub.rs), usable without a GPU. ---- */
 

@@ -15,8 +15,8 @@
  *     rows == 0 launches nothing and returns 0.
  *   - `status` is an optional device array of two uint32_t words (NULL allowed). Word 0
  *     collects device-side failure bits (a bounded wait that expired; the kernel then exits
- *     without finishing). Word 1 is set nonzero by dv3k_patchify and dv3k_patch_embed_pixels
- *     when an input value is not finite. The caller clears and reads them.
+ *     without finishing). Word 1 is set nonzero by dv3k_patchify when an input value is not
+ *     finite. The caller clears and reads them.
  *   - `stream` is a cudaStream_t (NULL: the legacy default stream). Launches are asynchronous.
  *   - Return value: 0, DV3_INVALID_ARGUMENT (shape/alignment) or DV3_DEVICE (launch failed),
  *     with the message in dv3_last_error().
@@ -59,15 +59,6 @@ int dv3k_patchify(const float *images, uint32_t n_images, const float *prefix, u
  * with f32 accumulation, for p < n_patches. */
 int dv3k_patch_embed(const uint16_t *patches, uint32_t n_patches, const uint16_t *w,
                      const float *bias, uint16_t *x, uint32_t *status, void *stream);
-
-/* dv3k_patchify and dv3k_patch_embed in one kernel (the device patchify fused into the patch
- * GEMM's A loader): the same x rows, bit for bit, including the prefix rows, and the same
- * status[1] flag for non-finite pixels, without the f16 patch matrix in memory. Full 384-wide
- * rows, one 128-patch tile per CTA: n_images * 196 patch rows must fit one wave of tiles
- * (n_images <= 96 on a 148-SM B200). */
-int dv3k_patch_embed_pixels(const float *images, uint32_t n_images, const uint16_t *w,
-                            const float *bias, const float *prefix, uint16_t *x, uint32_t *status,
-                            void *stream);
 
 /* LayerNorm over 384 channels, eps 1e-5, f16 -> f16. Replaces
  * kernels/layernorm_rowwave_f16.loom. */
@@ -115,16 +106,6 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
                                 const float *gamma, const float *beta, uint16_t *h,
                                 float *out_f32, uint32_t *status, void *stream);
 
-/* dv3k_matmul_resid_layernorm (k = 1536, f16 h) followed by dv3k_qkv_rope on its h, in one
- * kernel: each 128-row tile's LayerNorm rows stay in shared memory as the QKV GEMM's A operand
- * (h is not written to memory). x and qkv are bit for bit those of the two calls. rows: a
- * multiple of 201, at most one 128-row tile per SM. */
-int dv3k_down_layernorm_qkv(const uint16_t *act, uint32_t rows, const uint16_t *down_w,
-                            const float *down_b, const float *lambda, uint16_t *x,
-                            const float *gamma, const float *beta, const uint16_t *qkv_w,
-                            const float *qkv_b, const float *rope_cos, const float *rope_sin,
-                            uint16_t *qkv, uint32_t *status, void *stream);
-
 /* Down projection split over K (kernels/matmul_splitk_f16_wmma.loom, launched at batch 1 by
  * src/lib.rs:218-224 with the specialisation of :297): for each slice s < splits of the 1536-long
  * reduction, partials[s][row][n] = sum over k in slice s of a[row][k] * w[n][k], f32, no bias.
@@ -149,10 +130,20 @@ int dv3k_splitk_reduce_layernorm(const float *partials, uint32_t rows, uint32_t 
                                  float *out_f32, void *stream);
 
 /* dv3k_matmul_splitk followed by dv3k_splitk_reduce (x[row][n] = f16(x + lambda[n] * (sum of
- * the slices + bias[n])), in place) without a workspace argument: the partial slabs live in a
- * file-scope device array of the library (6144 x 384 floats, so splits x rows <= 6144), and the
- * call allocates nothing. Two launches on `stream`; calls on different streams must not overlap,
- * since they share that array. */
+ * the slices + bias[n])), in place) without a workspace argument, for callers that may not
+ * allocate device memory themselves (an allocator-free embedding, a caller inside a region
+ * where cudaMalloc would synchronise or is forbidden). No counterpart in the reference.
+ *   - The partial slabs live in a file-scope device array of the library whose size is fixed
+ *     when the library is built: 6144 partial rows of 384 floats (9 MiB, held on every device
+ *     that loads the library until the process exits). It is not derived from any SM count;
+ *     the caller sizes splits x rows <= 6144, and larger requests return DV3_INVALID_ARGUMENT.
+ *   - The call allocates nothing (no cudaMalloc, cudaFree or allocating library routine). The
+ *     first call on a device looks up the array's device address once (cudaGetSymbolAddress,
+ *     with that device current); make that first call before any stream capture.
+ *   - Two launches on `stream`. Every call shares the one array and overwrites the slabs it
+ *     uses (no clearing is needed: each slab is fully written before it is read), so calls
+ *     that overlap on the GPU race: calls on different streams of one device must be ordered by
+ *     the caller. Calls in sequence on one stream are ordered by the stream. */
 int dv3k_down_splitk_noalloc(const uint16_t *a, uint32_t rows, const uint16_t *w, uint32_t splits,
                              const float *bias, const float *lambda, uint16_t *x, uint32_t *status,
                              void *stream);

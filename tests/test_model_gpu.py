@@ -31,6 +31,9 @@ import dinov3_b200 as dv  # noqa: E402
 # Largest |gpu - float64| over every output element allowed in these tests (outputs are
 # LayerNorm-normalised, O(1)); f16 weights and activations with f32 accumulation.
 MAX_ABS = 0.08
+# The same bound for the full-batch tests of the benchmark's configurations (every image of a
+# batch of 32 or 64 against the float64 oracle).
+MAX_ABS_FULL = 0.03
 
 
 @pytest.fixture(scope="module")
@@ -192,6 +195,109 @@ def test_full_size_batch_properties(models, oracles, source):
     np.testing.assert_array_equal(model.forward(images), out)
 
 
+@pytest.mark.parametrize("flavor,batch,source", [
+    ("baseline", 32, "seeded"), ("baseline", 32, "reference"),
+    ("baseline", 64, "seeded"), ("baseline", 64, "reference"), ("stress", 64, "seeded")])
+def test_every_image_of_full_batches_against_oracle(models, oracles, flavor, batch, source):
+    """BASELINE config 1 (batch 32 with the default Options, resident capacity 32) and config 2
+    (batch 64, capacity 64, the benchmark's plan): every image of the batch against the float64
+    oracle, all-token and CLS cosine > 0.9999 each, and every output element within
+    MAX_ABS_FULL, as tests/model.rs:75-94 checks every image of its batch."""
+    model = models(flavor, max_batch=batch)
+    if batch == 32:
+        assert model.launches_per_forward(32) == 3 + 12 * 7  # 128-wide residual tiles
+    else:
+        assert model.launches_per_forward(64) == 3 + 12 * 5  # full-row residual + LayerNorm
+    images = synth.images(5000 + batch, batch) if source == "seeded" else \
+        synth.reference_test_images(batch)
+    out = model.forward(images)
+    want = oracles(flavor).forward(images, threads=0)
+    worst = []
+    for i in range(batch):
+        c_all, c_cls = cos(out[i], want[i]), cos(out[i, 0], want[i, 0])
+        worst.append((c_all, c_cls, float(np.abs(out[i] - want[i]).max())))
+        assert c_all > 0.9999, f"image {i}: all-token cosine {c_all}"
+        assert c_cls > 0.9999, f"image {i}: CLS cosine {c_cls}"
+    err = max(w[2] for w in worst)
+    print(f"{flavor} b={batch} {source}: min all-token cosine {min(w[0] for w in worst):.8f}, "
+          f"min CLS cosine {min(w[1] for w in worst):.8f}, max |err| {err:.5f}")
+    assert err < MAX_ABS_FULL
+
+
+def test_injected_device_failure_poisons_the_session(weights_file):
+    """A device failure poisons the model (src/engine.rs:93,168-171,198-200): the forward that
+    saw it returns DV3_POISONED with the reference's message, and so does every later call. The
+    failure is injected on the host (dv3_debug_inject_fault writes the failure bits an expired
+    device wait would record), so no GPU fault is made."""
+    path = weights_file(1, "stress")
+    images = synth.images(61, 2)
+    pin_in = torch.from_numpy(images).pin_memory()
+    pin_out = torch.empty((2, 201, 384), dtype=torch.float32).pin_memory()
+
+    def poisoned(call):
+        with pytest.raises(dv.DINOv3Error) as e:
+            call()
+        assert e.value.code == dv.POISONED, str(e.value)
+        assert "session is unusable after a GPU failure" in str(e.value)
+
+    # synchronous forward
+    with dv.DINOv3.load(path, dv.Options(0, 4)) as model:
+        want = model.forward(images)
+        model.debug_inject_fault(1 << 30)
+        poisoned(lambda: model.forward(images))
+        poisoned(lambda: model.forward(images))
+        poisoned(lambda: model.cls(images))
+        poisoned(lambda: model.patch_mean(images))
+        poisoned(lambda: model.run(2))
+        poisoned(lambda: model.submit(pin_in, pin_out))
+        poisoned(lambda: model.debug_inject_fault(1))
+    # device-resident replay: the failure is reported by the next synchronize
+    with dv.DINOv3.load(path, dv.Options(0, 4)) as model:
+        np.testing.assert_array_equal(model.forward(images), want)  # stages the input
+        model.run(2)
+        model.synchronize()
+        model.debug_inject_fault(1 << 30)
+        model.run(2)
+        poisoned(model.synchronize)
+        poisoned(lambda: model.run(2))
+        poisoned(lambda: model.forward(images))
+    # serving path: a non-finite submission is an argument error and does not poison; the
+    # faulted submission reports DV3_POISONED and the model stays poisoned
+    with dv.DINOv3.load(path, dv.Options(0, 4)) as model:
+        bad = images.copy()
+        bad[1, 2, 3, 4] = np.nan
+        bad_in = torch.from_numpy(bad).pin_memory()
+        outs = [torch.empty((2, 201, 384), dtype=torch.float32).pin_memory() for _ in range(3)]
+        tb = model.submit(bad_in, outs[0])
+        with pytest.raises(dv.DINOv3Error) as e:
+            model.wait(tb)
+        assert e.value.code == dv.INVALID_ARGUMENT and "input must be finite" in str(e.value)
+        tg = model.submit(pin_in, outs[1])
+        model.wait(tg)
+        np.testing.assert_array_equal(outs[1].numpy(), want)
+        model.debug_inject_fault(1 << 30)
+        tf = model.submit(pin_in, outs[2])
+        poisoned(lambda: model.wait(tf))
+        poisoned(lambda: model.submit(pin_in, outs[2]))
+        poisoned(lambda: model.forward(images))
+
+
+def test_profile_forward_in_plan_order(models):
+    """dv3_profile_forward times every launch inside whole forwards (L2 flushed before each):
+    the plan's launches in order, each positive, and their sum close to one graph replay."""
+    model = models("baseline", max_batch=64)
+    images = synth.images(17, 64)
+    model.forward(images)  # stages the input
+    prof = model.profile_forward(64, 3, 256 << 20)
+    assert len(prof) == model.launches_per_forward(64)
+    assert [n for n, _ in prof][:3] == ["patchify", "gemm_patch_embed", "layernorm_f16"]
+    assert all(ms > 0 for _, ms in prof)
+    total = sum(ms for _, ms in prof)
+    assert 0.3 < total < 5.0, total  # ms for a batch-64 forward
+    with pytest.raises(dv.DINOv3Error):
+        model.profile_forward(65, 1)
+
+
 @pytest.mark.parametrize("b", [12, 40])
 def test_mid_size_batch_plans(models, oracles, b):
     """Batch sizes between the batch-1 and batch-64 plans: 12 images run the down projection as 2
@@ -302,51 +408,6 @@ def test_split_k_plan(weights_file, monkeypatch):
         plain = model.forward(images)
     for i in range(3):
         assert cos(split[i], plain[i]) > 0.99999
-
-
-@pytest.mark.parametrize("b", [1, 64])
-def test_fused_patchify_plan(weights_file, monkeypatch, b):
-    """The default plan runs patchify and the patch GEMM as two launches; DV3_FUSE_PATCHIFY=1
-    (read when a batch size's graph is built) makes the patch GEMM build its A tiles from the
-    images in one launch. Both give the same result within the bias's position in the f32 sum,
-    and the fused launch flags a non-finite pixel like patchify."""
-    path = weights_file(1, "stress")
-    images = synth.images(44, b)
-    with dv.DINOv3.load(path, dv.Options(0, b)) as model:
-        names = [n for n, _ in model.profile_launches(b, 1)]
-        assert names[:2] == ["patchify", "gemm_patch_embed"]
-        plain = model.forward(images)
-    monkeypatch.setenv("DV3_FUSE_PATCHIFY", "1")
-    with dv.DINOv3.load(path, dv.Options(0, b)) as model:
-        names = [n for n, _ in model.profile_launches(b, 1)]
-        assert names[0] == "gemm_patch_pixels" and "patchify" not in names
-        fused = model.forward(images)
-        bad = images.copy()
-        bad[b - 1, 0, 17, 200] = np.inf
-        with pytest.raises(dv.DINOv3Error, match="finite"):
-            model.forward(bad)
-        np.testing.assert_array_equal(model.forward(images), fused)  # still usable, bitwise
-    for i in range(b):
-        assert cos(fused[i], plain[i]) > 0.99999
-
-
-def test_fused_down_qkv_plan(weights_file, monkeypatch):
-    """DV3_FUSE_QKV=1 (read when a batch size's graph is built; full-row plans only) runs each
-    down projection of layers 0-10 together with the next layer's QKV GEMM (h kept in shared
-    memory): 11 launches fewer, and bit for bit the default plan's output."""
-    path = weights_file(1, "stress")
-    images = synth.images(55, 64)
-    with dv.DINOv3.load(path, dv.Options(0, 64)) as model:
-        n_default = model.launches_per_forward(64)
-        want = model.forward(images)
-    monkeypatch.setenv("DV3_FUSE_QKV", "1")
-    with dv.DINOv3.load(path, dv.Options(0, 64)) as model:
-        assert model.launches_per_forward(64) == n_default - 11
-        names = [n for n, _ in model.profile_launches(64, 1)]
-        assert names.count("gemm_down_ln_qkv") == 11 and names.count("gemm_qkv_rope") == 1
-        got = model.forward(images)
-        assert model.launches_per_forward(16) == 3 + 12 * 7  # small batches: unchanged
-    np.testing.assert_array_equal(got, want)
 
 
 def test_submit_wait_serving_path(models):
