@@ -17,9 +17,11 @@ barrier and the max-over-ranks of the timings).
           step (upload, forward and download in series), CUDA events on the model's stream.
   roofline the dominant kernel (gate/up GEMM + SwiGLU, 46.5 % of the FLOPs): its algorithmic FLOPs
           per launch / its average launch time, measured inside whole forwards after the timed
-          region (dv3_profile_forward: `--profile-iters` forwards of the same staged batch, the
-          L2 flushed before each, every launch enqueued on the model's stream between two CUDA
-          events), against the measured burst bf16/f16 dense peak (MEASURED_PEAKS.json
+          region (dv3_profile_forward: CUDA events on the model's stream around graphs of the
+          first j launches of the plan, `--profile-iters` replays each with the L2 flushed
+          before each; launch j takes T(j) - T(j-1), so the launch times add up to a forward and
+          keep the production graph's overlap of each kernel's set-up with the previous
+          kernel's tail), against the measured burst bf16/f16 dense peak (MEASURED_PEAKS.json
           bf16_tflops; `frac_of_sustained` beside it). `per_kernel` lists every kernel of the
           plan the same way: FLOPs and algorithmic bytes per launch, the measured time, the
           floor max(FLOPs / tensor peak, bytes / HBM bandwidth) and floor / time. `traffic` comes
@@ -509,9 +511,12 @@ def run_ours(args):
                          "traffic": committed_traffic("gemm_gateup_swiglu"),
                          "algorithmic_flops": gate["gflop"] * 1e9,
                          "algorithmic_bytes": gate["mbytes"] * 1e6, "avg_launch_ms": gate_ms,
-                         "timing": f"dv3_profile_forward: {args.profile_iters} forwards, L2 "
-                                   "flushed before each, CUDA events around every launch on "
-                                   "the model's stream",
+                         "timing": f"dv3_profile_forward: CUDA events on the model's stream "
+                                   f"around graphs of the plan's first j launches, "
+                                   f"{args.profile_iters} replays each, L2 flushed before each; "
+                                   "launch j = T(j) - T(j-1)",
+                         "profiled_forward_ms": sum(e["us"] * e["launches"]
+                                                    for e in per_kernel) / 1e3,
                          "per_kernel": per_kernel},
             "cpu_baseline": cpu,
             "cpu_baseline_single": cpu_single,

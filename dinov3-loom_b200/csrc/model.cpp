@@ -706,16 +706,15 @@ std::vector<std::pair<const char *, double>> Model::profile_launches(size_t batc
   return result;
 }
 
-// Per-launch device time inside whole forwards, in the production plan's order and with its
-// cache state: each of `replays` forwards of the staged input is preceded by a write of
-// `flush_bytes` bytes to a scratch buffer (evicting L2 when larger than it, as between timed
-// steps), then its launches are enqueued directly on the model's stream with an event recorded
-// before the first and after each one; a launch's time is the interval between the events
-// around it, averaged over the replays. The flush gives the host a head start, so every kernel
-// is queued before the previous one ends. Between two events the next kernel cannot start its
-// set-up early (the graph lets it overlap the previous kernel's tail), so the sum of the launch
-// times slightly exceeds one graph replay. The scratch buffer is allocated for the call and
-// freed after it.
+// Per-launch device time inside whole forwards, in the production plan's order, cache state and
+// overlap: for every j the first j launches of the plan are captured into a CUDA graph (kernel
+// nodes joined by programmatic dependencies, as in the production graph), and each prefix graph
+// is replayed `replays` times between two CUDA events on the model's stream, each replay after
+// a write of `flush_bytes` bytes to a scratch buffer outside the events (evicting L2 when larger
+// than it, as between timed steps). T(j) is the mean replay time of the first j launches, and
+// launch j's time is T(j) - T(j-1): what that launch adds to the forward, including the part of
+// its set-up that overlaps the previous kernel's tail. The times add up to a whole forward. The
+// scratch buffer and the graphs are made for the call and released after it.
 std::vector<std::pair<const char *, double>> Model::profile_forward(size_t batch, size_t replays,
                                                                     size_t flush_bytes) {
   drain();
@@ -726,32 +725,49 @@ std::vector<std::pair<const char *, double>> Model::profile_forward(size_t batch
   activate();
   Plan &plan = prepare(batch);
   const size_t n = plan.launches.size();
-  std::vector<cudaEvent_t> ev(n + 1, nullptr);
+  cudaEvent_t ev[2] = {nullptr, nullptr};
   void *flush = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  auto release_graph = [&] {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    exec = nullptr;
+    graph = nullptr;
+  };
   auto release_all = [&] {
+    release_graph();
     for (auto &e : ev)
       if (e) cudaEventDestroy(e);
     if (flush) cudaFree(flush);
     flush = nullptr;
   };
-  std::vector<double> total(n, 0.0);
+  std::vector<double> prefix(n + 1, 0.0);  // T(j), ms
   try {
     for (auto &e : ev) cuda(cudaEventCreate(&e), "create event");
     if (flush_bytes) cuda(cudaMalloc(&flush, flush_bytes), "allocate flush buffer");
-    for (size_t r = 0; r < replays; ++r) {
-      if (flush)
-        cuda(cudaMemsetAsync(flush, static_cast<int>(r & 0xff), flush_bytes, stream_), "flush L2");
-      cuda(cudaEventRecord(ev[0], stream_), "record event");
-      for (size_t j = 0; j < n; ++j) {
-        cuda(plan.launches[j].enqueue(stream_), plan.launches[j].name);
-        cuda(cudaEventRecord(ev[j + 1], stream_), "record event");
-      }
-      cuda(cudaEventSynchronize(ev[n]), "synchronize");
-      for (size_t j = 0; j < n; ++j) {
+    for (size_t j = 1; j <= n; ++j) {
+      cuda(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+      cudaError_t e = cudaSuccess;
+      for (size_t k = 0; k < j && e == cudaSuccess; ++k) e = plan.launches[k].enqueue(stream_);
+      const cudaError_t e2 = cudaStreamEndCapture(stream_, &graph);
+      cuda(e != cudaSuccess ? e : e2, "capture profiling graph");
+      cuda(cudaGraphInstantiate(&exec, graph, 0), "instantiate profiling graph");
+      cuda(cudaGraphLaunch(exec, stream_), "launch profiling graph");  // warm-up
+      double sum = 0.0;
+      for (size_t r = 0; r < replays; ++r) {
+        if (flush) cuda(cudaMemsetAsync(flush, static_cast<int>(r & 0xff), flush_bytes, stream_),
+                        "flush L2");
+        cuda(cudaEventRecord(ev[0], stream_), "record event");
+        cuda(cudaGraphLaunch(exec, stream_), "launch profiling graph");
+        cuda(cudaEventRecord(ev[1], stream_), "record event");
+        cuda(cudaEventSynchronize(ev[1]), "synchronize");
         float ms = 0;
-        cuda(cudaEventElapsedTime(&ms, ev[j], ev[j + 1]), "elapsed time");
-        total[j] += ms;
+        cuda(cudaEventElapsedTime(&ms, ev[0], ev[1]), "elapsed time");
+        sum += ms;
       }
+      prefix[j] = sum / static_cast<double>(replays);
+      release_graph();
     }
   } catch (...) {
     release_all();
@@ -760,8 +776,7 @@ std::vector<std::pair<const char *, double>> Model::profile_forward(size_t batch
   release_all();
   check_status();
   std::vector<std::pair<const char *, double>> result;
-  for (size_t j = 0; j < n; ++j)
-    result.emplace_back(plan.launches[j].name, total[j] / static_cast<double>(replays));
+  for (size_t j = 0; j < n; ++j) result.emplace_back(plan.launches[j].name, prefix[j + 1] - prefix[j]);
   return result;
 }
 

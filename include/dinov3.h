@@ -168,13 +168,13 @@ int dv3_profile_launches(dv3_model *m, size_t batch, size_t iterations, double *
                          const char **names, size_t capacity, size_t *count);
 
 /* Per-launch device time of the launches of whole forwards of `batch` staged images, in the
- * plan's order and cache state: each of `replays` forwards is preceded by a write of
- * `flush_bytes` bytes to a scratch buffer the call allocates (evicting L2 when larger than it;
- * 0: no flush), its launches are enqueued on the model's stream with an event after each, and a
- * launch's time is the interval between the events around it, averaged over the replays. Writes
- * up to `capacity` entries (launch order) of milliseconds and static kernel names, and the
- * count to *count. The events stop each kernel's set-up from overlapping the previous kernel,
- * so the sum slightly exceeds one graph replay. */
+ * plan's order, cache state and overlap: for every j the first j launches are captured into a
+ * CUDA graph (programmatic dependencies between kernels, as in the forward's graph) and replayed
+ * `replays` times between two CUDA events on the model's stream, each replay after a write of
+ * `flush_bytes` bytes to a scratch buffer the call allocates (outside the events; evicts L2 when
+ * larger than it; 0: no flush). With T(j) the mean time of the first j launches, launch j takes
+ * T(j) - T(j-1), so the times add up to one forward. Writes up to `capacity` entries (launch
+ * order) of milliseconds and static kernel names, and the count to *count. */
 int dv3_profile_forward(dv3_model *m, size_t batch, size_t replays, size_t flush_bytes,
                         double *ms, const char **names, size_t capacity, size_t *count);
 

@@ -256,43 +256,6 @@ def test_matmul_resid_layernorm(k, b, f32_out):
         assert_close16(h, ref_ln)
 
 
-@pytest.mark.parametrize("b", [1, 3, 64])
-def test_down_layernorm_qkv_matches_two_calls(b):
-    """The fused down projection + residual + LayerNorm + QKV GEMM gives bit for bit the x of
-    dv3k_matmul_resid_layernorm and the qkv of dv3k_qkv_rope on its h (the same LayerNorm rows,
-    read from shared memory instead of memory, and the same MMA order)."""
-    rng = np.random.default_rng(90 + b)
-    r = rows_of(b)
-    act = t16(f16(rng.standard_normal((r, 1536))))
-    down_w = t16(f16(rng.standard_normal((384, 1536)) / np.sqrt(1536)))
-    down_b, lam = t32(rng.standard_normal(384) * 0.1), t32(rng.random(384) * 0.2 + 0.05)
-    gamma, beta = t32(rng.standard_normal(384) * 0.3 + 1), t32(rng.standard_normal(384) * 0.1)
-    qkv_w = t16(f16(rng.standard_normal((1152, 384)) / np.sqrt(384)))
-    qkv_b = t32(rng.standard_normal(1152) * 0.1)
-    cos, sin = (t32(v) for v in ref_numpy.rope_tables())
-    x0 = f16(rng.standard_normal((r, 384)) + rng.standard_normal((r, 1)))
-    x_two, x_one = t16(x0), t16(x0)
-    h = torch.empty((r, 384), dtype=torch.float16, device=DEV)
-    qkv_two = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
-    qkv_one = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
-    st = status()
-    check_rc(lib().dv3k_matmul_resid_layernorm(ptr(act), r, 1536, ptr(down_w), ptr(down_b),
-                                               ptr(lam), ptr(x_two), ptr(gamma), ptr(beta),
-                                               ptr(h), None, ptr(st), stream()))
-    check_rc(lib().dv3k_qkv_rope(ptr(h), r, ptr(qkv_w), ptr(qkv_b), ptr(cos), ptr(sin),
-                                 ptr(qkv_two), ptr(st), stream()))
-    check_rc(lib().dv3k_down_layernorm_qkv(ptr(act), r, ptr(down_w), ptr(down_b), ptr(lam),
-                                           ptr(x_one), ptr(gamma), ptr(beta), ptr(qkv_w),
-                                           ptr(qkv_b), ptr(cos), ptr(sin), ptr(qkv_one), ptr(st),
-                                           stream()))
-    torch.cuda.synchronize()
-    assert st.cpu().tolist() == [0, 0]
-    np.testing.assert_array_equal(x_one.cpu().numpy().view(np.uint16),
-                                  x_two.cpu().numpy().view(np.uint16))
-    np.testing.assert_array_equal(qkv_one.cpu().numpy().view(np.uint16),
-                                  qkv_two.cpu().numpy().view(np.uint16))
-
-
 def splitk_reduce_ref(partials, bias, lam, x):
     """kernels/splitk_reduce_f16.loom in float32 with its own rounding order: the slabs onto
     zero in order, + bias, * lambda, + the f16 residual, rounded to f16."""

@@ -29,11 +29,11 @@ if not torch.cuda.is_available():
 import dinov3_b200 as dv  # noqa: E402
 
 # Largest |gpu - float64| over every output element allowed in these tests (outputs are
-# LayerNorm-normalised, O(1)); f16 weights and activations with f32 accumulation.
-MAX_ABS = 0.08
-# The same bound for the full-batch tests of the benchmark's configurations (every image of a
-# batch of 32 or 64 against the float64 oracle).
-MAX_ABS_FULL = 0.03
+# LayerNorm-normalised, O(1)); f16 weights and activations with f32 accumulation. The largest
+# error seen over every image of batches of 32 and 64 is 0.020 (stress weights) and 0.018
+# (baseline weights).
+MAX_ABS = 0.03
+MAX_ABS_FULL = MAX_ABS
 
 
 @pytest.fixture(scope="module")
@@ -283,15 +283,17 @@ def test_injected_device_failure_poisons_the_session(weights_file):
 
 
 def test_profile_forward_in_plan_order(models):
-    """dv3_profile_forward times every launch inside whole forwards (L2 flushed before each):
-    the plan's launches in order, each positive, and their sum close to one graph replay."""
+    """dv3_profile_forward times every launch inside whole forwards (L2 flushed before each)
+    as the differences of timed graphs of the plan's first j launches: the plan's launches in
+    order, and their sum is one forward."""
     model = models("baseline", max_batch=64)
     images = synth.images(17, 64)
     model.forward(images)  # stages the input
     prof = model.profile_forward(64, 3, 256 << 20)
     assert len(prof) == model.launches_per_forward(64)
     assert [n for n, _ in prof][:3] == ["patchify", "gemm_patch_embed", "layernorm_f16"]
-    assert all(ms > 0 for _, ms in prof)
+    gemms = [ms for n, ms in prof if n.startswith("gemm_gateup")]
+    assert len(gemms) == 12 and all(ms > 0.005 for ms in gemms)
     total = sum(ms for _, ms in prof)
     assert 0.3 < total < 5.0, total  # ms for a batch-64 forward
     with pytest.raises(dv.DINOv3Error):
