@@ -226,8 +226,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();  // the QKV rows of the previous kernel are complete from here on
-  pdl_trigger();
+  // Programmatic dependent launch: only the TMA producer reads what the previous kernel wrote,
+  // so only it waits for that kernel (before its first load); the other roles start on the data
+  // it brings. Their entry code overlaps the previous kernel's tail.
   // the producer warp's idle lane starts a later kernel's weights toward L2
   if (warp == kProducerWarp && lane == 1 && l2_next) l2_prefetch_share(l2_next, l2_next_bytes);
 
@@ -241,6 +242,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           report(status, kErrAttentionWait);
           *abort_flag = 1;
           break;
+        }
+        if (k == 0) {
+          pdl_wait();  // the QKV rows of the previous kernel are complete from here on
+          pdl_trigger();
         }
         const int item = item_of(k);
         const int img = item / kHeads, head = item % kHeads;

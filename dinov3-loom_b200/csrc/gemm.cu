@@ -244,6 +244,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  // The scalar launch parameters are read here, in the set-up that overlaps the previous kernel:
+  // a first read from the parameter bank misses the constant cache (hundreds of cycles), and
+  // the roles would otherwise take those misses after their dependency wait.
+  asm volatile("" ::"r"(M), "r"(sched.m_tiles), "r"(sched.full_n), "r"(sched.split_from),
+               "r"(sched.num_units), "r"(sched.k_splits), "r"(k_blocks));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -286,8 +291,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     tc_fence_after();
   }
-  pdl_wait();  // activations of the previous kernel are complete from here on
-  pdl_trigger();
+  // Programmatic dependent launch: only the roles that touch what earlier kernels wrote or read
+  // wait for the previous kernel (griddepcontrol.wait): the TMA producer right before its first
+  // load, and the epilogue warps before their first input request or store. The MMA issuer reads
+  // only shared memory that the producer filled after its wait. Each role's entry code (and the
+  // fetch of its instructions) thus overlaps the previous kernel's tail.
   // an epilogue thread, idle until the first accumulator, starts the next weights toward L2
   if (threadIdx.x == 64 && sched.l2_next) l2_prefetch_share(sched.l2_next, sched.l2_next_bytes);
   const uint32_t tmem_base = *tmem_slot;
@@ -322,6 +330,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             *abort_flag = 1;
             ok = false;
             break;
+          }
+          if (tile == static_cast<int>(blockIdx.x) && kb == 0) {
+            pdl_wait();  // activations of the previous kernel are complete from here on
+            pdl_trigger();
           }
           uint8_t *a = tiles + stage * C::kStage;
           mbar_arrive_expect_tx(&full[stage], C::kA + b_boxes * C::kBBox * BK * 2);
@@ -424,6 +436,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
+    pdl_wait();  // before the first input request or store (see above)
+    pdl_trigger();
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;       // which half of the tile's columns
     constexpr int kCols = BN / 2;

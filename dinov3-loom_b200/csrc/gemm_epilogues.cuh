@@ -224,7 +224,9 @@ struct EpiQkvRope {
   static constexpr int kSmem = kRopeBytes + kQkv * 4;       // + bias
   static constexpr bool kTmaStore = true;
   // One staging block per warp: the 16 KB saved let a fourth 48 KB mainloop stage fit beside
-  // the RoPE tables and the bias (the epilogue has slack to wait for each store's read).
+  // the RoPE tables and the bias. Measured no faster: the two 16-column halves of that block
+  // used in turn (twice the TMA store instructions delayed the producer's loads), and the
+  // second head's accumulator loaded from TMEM during the first head's stores.
   static constexpr int kStagingBufs = 1;
   using Pre = NoPre;
   __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
