@@ -30,6 +30,8 @@ barrier and the max-over-ranks of the timings).
           tests/support/reference.rs) on this host, OpenMP over images, rank 0 at N = 1 only.
 Reference arm (--impl reference): the same CPU oracle with all host threads, rank 0 only; a
 step is one forward of as many images as host threads (a bounded sample of the batch-64 step).
+--copies: the end-to-end step's host<->device transfers alone (no forward), per rank, to show how
+much copy bandwidth the host gives N GPUs at once.
 --ops: BASELINE config 3, every kernel entry point (include/dinov3_kernels.h) alone at batch 64
 (12,864 token rows), inputs N(0,1) and weights N(0,1)/sqrt(K), with cold L2: each timed graph
 cycles over enough copies of the operands to exceed twice the L2, so no launch finds its inputs
@@ -118,6 +120,10 @@ def parse_args():
                          "1..64 from pinned host memory, synchronous and two-deep pipelined")
     ap.add_argument("--serve-images", type=int, default=8192,
                     help="images over all GPUs in the serving measurement")
+    ap.add_argument("--copies", action="store_true",
+                    help="the end-to-end step's host<->device copies alone (38.5 MB up, 19.8 MB "
+                         "down per GPU per step, pinned buffers, both directions at once): the "
+                         "bandwidth the host side gives every rank")
     ap.add_argument("--ops", action="store_true",
                     help="per-op microbenchmark (BASELINE config 3): every kernel entry point "
                          "alone at batch 64, cold and warm L2")
@@ -747,12 +753,62 @@ def run_ops(args):
     print(json.dumps(line), flush=True)
 
 
+def run_copies(args):
+    """The transfers of one end-to-end step without the forward: every rank copies a batch-64
+    input (pinned, 38.5 MB) to the GPU and a batch-64 output (19.8 MB) back to pinned memory,
+    on two streams so both directions run at once, `--steps` times; host clock between device
+    synchronisations, max over ranks. Rank 0 prints the aggregate and per-rank GB/s."""
+    import torch
+
+    from dinov3_b200.replicas import Replicas
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    reps = Replicas("nccl", timeout_s=120)
+    up_h = torch.empty(BATCH * 3 * 224 * 224, dtype=torch.float32).pin_memory()
+    down_h = torch.empty(BATCH * 201 * 384, dtype=torch.float32).pin_memory()
+    up_d = torch.empty_like(up_h, device="cuda")
+    down_d = torch.zeros_like(down_h, device="cuda")
+    s_up, s_down = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def step():
+        with torch.cuda.stream(s_up):
+            up_d.copy_(up_h, non_blocking=True)
+        with torch.cuda.stream(s_down):
+            down_h.copy_(down_d, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    reps.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    dt = reps.max(time.perf_counter() - t0)
+    reps.barrier()
+    per_step = up_h.numel() * 4 + down_h.numel() * 4
+    if rank == 0:
+        print(json.dumps({
+            "metric": "host<->device copy bandwidth of the end-to-end step's transfers",
+            "value": world * per_step * args.steps / dt / 1e9, "unit": "GB/s", "n_gpus": world,
+            "per_gpu_gbs": per_step * args.steps / dt / 1e9, "steps": args.steps,
+            "bytes_per_step_per_gpu": per_step,
+            "equivalent_images_per_s": world * BATCH * args.steps / dt,
+            "config": {"workload": "batch-64 input up and output down per step, pinned host "
+                                   "buffers, both directions concurrently, no forward",
+                       "parallelism": f"replicas{world}"}}), flush=True)
+    reps.close()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.ops:
         run_ops(args)
+    elif args.copies:
+        run_copies(args)
     else:
         run_ours(args)
 
