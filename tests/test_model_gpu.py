@@ -131,6 +131,37 @@ def test_chunking_matches_single_images(models):
         assert cos(out[i], model.forward(images[i:i + 1])[0]) > 0.99999
 
 
+def test_chunked_full_capacity_against_oracle(models, oracles):
+    """130 images through the full resident capacity (max_batch 64: chunks of 64, 64 and 2,
+    so two plans): the chunks equal their own forwards bitwise, cls and patch_mean read the same
+    tokens, and images from every chunk (first and last of each) match the float64 oracle."""
+    model = models("baseline", max_batch=64)
+    images = synth.images(9000, 130)
+    out = model.forward(images)
+    assert out.shape == (130, 201, 384) and np.isfinite(out).all()
+    np.testing.assert_array_equal(out[128:], model.forward(images[128:]))
+    np.testing.assert_array_equal(out[64:128], model.forward(images[64:128]))
+    np.testing.assert_array_equal(model.cls(images), out[:, 0])
+    pm = model.patch_mean(images)
+    want_pm = np.zeros((130, 384), np.float32)
+    for r in range(5, 201):  # src/lib.rs:134-148 accumulation order
+        want_pm += out[:, r] / np.float32(196.0)
+    np.testing.assert_array_equal(pm, want_pm)
+    picks = [0, 63, 64, 127, 128, 129]
+    want = oracles("baseline").forward(images[picks], threads=0)
+    for got, ref in zip(out[picks], want):
+        assert cos(got, ref) > 0.9999 and cos(got[0], ref[0]) > 0.9999
+        assert np.abs(got - ref).max() < MAX_ABS
+    # a non-finite pixel in the second chunk is an argument error (the earlier chunk has run;
+    # the output is unspecified on error) and the model stays usable
+    bad = images.copy()
+    bad[100, 2, 50, 60] = np.inf
+    with pytest.raises(dv.DINOv3Error) as e:
+        model.forward(bad)
+    assert e.value.code == dv.INVALID_ARGUMENT and "input must be finite" in str(e.value)
+    np.testing.assert_array_equal(model.forward(images[128:]), out[128:])
+
+
 def test_cls_and_patch_mean(models):
     """cls reads back only row 0 of each image and patch_mean reduces on the device; both equal
     the reference's host arithmetic on the full output bit for bit, also across chunks."""
