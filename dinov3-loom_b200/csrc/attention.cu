@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmq,
                      const __grid_constant__ CUtensorMap tmkv,
                      const __grid_constant__ CUtensorMap tmo, int n_items, int tile_split,
-                     const void *l2_next, size_t l2_next_bytes, uint32_t *status) {
+                     const void *l2_next, size_t l2_next_bytes, const void *discard,
+                     size_t discard_bytes, uint32_t *status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t *smem = smem_raw + pad;
@@ -231,6 +232,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // it brings. Their entry code overlaps the previous kernel's tail.
   // the producer warp's idle lane starts a later kernel's weights toward L2
   if (warp == kProducerWarp && lane == 1 && l2_next) l2_prefetch_share(l2_next, l2_next_bytes);
+  // its other idle lanes drop a dead intermediate from L2 once the previous kernel is complete
+  if (warp == kProducerWarp && lane >= 2 && discard) {
+    pdl_wait();
+    l2_discard_share(discard, discard_bytes, lane - 2, 30);
+  }
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -389,7 +395,8 @@ cudaError_t configure_attention_kernel() {
 }
 
 cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
-                             cudaStream_t stream, const void *l2_next, size_t l2_next_bytes) {
+                             cudaStream_t stream, const void *l2_next, size_t l2_next_bytes,
+                             const void *discard, size_t discard_bytes) {
   if (rows == 0) return cudaSuccess;
   static std::atomic<bool> configured[64] = {};
   int dev = 0;
@@ -404,9 +411,12 @@ cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t 
   // Small batches (every query tile fits its own SM): one CTA per query tile.
   const int tile_split = 2 * n_items <= sm_count(dev) ? 1 : 0;
   const int grid = tile_split ? 2 * n_items : (n_items < sm_count(dev) ? n_items : sm_count(dev));
+  const void *dp;
+  size_t db;
+  discard_range(discard, discard_bytes, &dp, &db);
   return launch_pdl(attention_kernel, dim3(grid), dim3(kAttnThreads), kAttnSmem, stream, maps.q,
                     maps.kv, maps.out, n_items, tile_split, l2_next,
-                    l2_next_bytes & ~static_cast<size_t>(15), status);
+                    l2_next_bytes & ~static_cast<size_t>(15), dp, db, status);
 }
 
 }  // namespace dv3

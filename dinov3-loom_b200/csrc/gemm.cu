@@ -188,6 +188,8 @@ struct TileSched {
   int k_splits;    // split-K: the full tiles repeat for each K slice (slice-major); else 1
   const void *l2_next;    // weights of a later kernel to prefetch into L2 (or null)
   size_t l2_next_bytes;
+  const void *discard;    // a dead intermediate to drop from L2 after the dependency wait
+  size_t discard_bytes;
 };
 
 template <int BN>
@@ -438,6 +440,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     pdl_wait();  // before the first input request or store (see above)
     pdl_trigger();
+    if (sched.discard)  // idle until the first accumulator
+      l2_discard_share(sched.discard, sched.discard_bytes, threadIdx.x - 64, kEpilogueThreads);
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;       // which half of the tile's columns
     constexpr int kCols = BN / 2;
@@ -706,6 +710,8 @@ static TileSched tile_sched(uint32_t rows, int n, int sms, int k_splits = 1) {
   if (k_splits > 1) t.num_units = full * k_splits;  // full tiles only, repeated per K slice
   t.l2_next = nullptr;
   t.l2_next_bytes = 0;
+  t.discard = nullptr;
+  t.discard_bytes = 0;
   return t;
 }
 
@@ -725,6 +731,7 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
   TileSched sched = tile_sched<BN, Epi>(rows, n, sm_count(dev), k_splits);
   sched.l2_next = args.l2_next;
   sched.l2_next_bytes = args.l2_next_bytes & ~static_cast<size_t>(15);
+  discard_range(args.discard, args.discard_bytes, &sched.discard, &sched.discard_bytes);
   const int grid = sched.num_units < sm_count(dev) ? sched.num_units : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
                     gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,

@@ -107,7 +107,25 @@ struct GemmArgs {
   // toward L2, so that kernel's first tiles do not wait for DRAM.
   const void *l2_next = nullptr;
   size_t l2_next_bytes = 0;
+  // An intermediate that earlier kernels wrote and read and that nothing reads any more (and this
+  // launch does not write): its whole 128-byte lines are dropped from L2 without a write-back
+  // after this launch's dependency wait (see discard_range).
+  const void *discard = nullptr;
+  size_t discard_bytes = 0;
 };
+
+// The whole 128-byte lines inside [p, p + bytes), as the (pointer, bytes) pair that the kernels'
+// L2 discard takes (null when none).
+inline void discard_range(const void *p, size_t bytes, const void **out, size_t *out_bytes) {
+  *out = nullptr;
+  *out_bytes = 0;
+  if (!p) return;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p), lo = (a + 127) & ~uintptr_t{127},
+                  hi = (a + bytes) & ~uintptr_t{127};
+  if (hi <= lo) return;
+  *out = reinterpret_cast<const void *>(lo);
+  *out_bytes = hi - lo;
+}
 
 // The K split of the down projection over `rows` rows in the model's plan: the most slices (at
 // most 8, a divisor of 24, so each CTA walks at least three 64-wide k-blocks) whose
@@ -132,10 +150,12 @@ struct AttentionMaps {
 };
 bool make_attention_map(const void *qkv, const void *out, uint32_t rows, AttentionMaps *maps,
                         std::string *err);
-// l2_next/l2_next_bytes: weights of a later kernel to prefetch into L2 (see GemmArgs).
+// l2_next/l2_next_bytes: weights of a later kernel to prefetch into L2; discard/discard_bytes: a
+// dead intermediate to drop from L2 (see GemmArgs).
 cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t *status,
                              cudaStream_t stream, const void *l2_next = nullptr,
-                             size_t l2_next_bytes = 0);
+                             size_t l2_next_bytes = 0, const void *discard = nullptr,
+                             size_t discard_bytes = 0);
 
 // ---- bandwidth kernels (elementwise.cu) ----
 // l2_next/l2_next_bytes: weights of a later kernel to prefetch into L2 (see GemmArgs).

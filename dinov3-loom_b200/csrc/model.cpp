@@ -292,6 +292,13 @@ Plan &Model::prepare(size_t b, int slot) {
   // reference splits K at batch 1, src/lib.rs:218-226).
   const uint32_t splits = fuse ? 1u : down_splits(r);
   float *partials = partials_;
+  // Each intermediate is dropped from L2 (GemmArgs::discard) by the launch after the one that
+  // last reads it, once that reader is complete: its lines neither cost a DRAM write-back when
+  // they are evicted nor hold L2 space until the next layer rewrites them. The dropping launch
+  // never touches the buffer itself.
+  const size_t patches_bytes = size_t{p} * kPatchK * 2, h_bytes = size_t{r} * kHidden * 2,
+               qkv_bytes = size_t{r} * kQkv * 2, attn_bytes = h_bytes,
+               act_bytes = size_t{r} * kMlp * 2;
   for (int i = 0; i < 12; ++i) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
@@ -313,10 +320,13 @@ Plan &Model::prepare(size_t b, int slot) {
       g.out = qkv;
       g.l2_next = l.o_w;
       g.l2_next_bytes = kOWBytes;
+      // the patch GEMM's input (layer 0), or the previous layer's down-projection input
+      g.discard = i == 0 ? static_cast<const void *>(patches) : static_cast<const void *>(act);
+      g.discard_bytes = i == 0 ? patches_bytes : act_bytes;
       return launch_gemm(GemmOp::QkvRope, qkv_maps, r, g, st, s);
     });
-    add("attention", [=](cudaStream_t s) {
-      return launch_attention(attn_map, r, st, s, l.gateup_w, kGateUpWBytes);
+    add("attention", [=](cudaStream_t s) {  // h: the QKV GEMM's input
+      return launch_attention(attn_map, r, st, s, l.gateup_w, kGateUpWBytes, h, h_bytes);
     });
     // o-proj + LayerScale 1 + residual, and LN2 of this layer (fused or separate): x -> x, h
     add(gemm_name(o_op), [=](cudaStream_t s) {
@@ -329,6 +339,8 @@ Plan &Model::prepare(size_t b, int slot) {
       g.ln_out = h;
       g.l2_next = l.down_w;
       g.l2_next_bytes = kDownWBytes;
+      g.discard = qkv;  // the attention's input
+      g.discard_bytes = qkv_bytes;
       return launch_gemm(o_op, o_maps, r, g, st, s);
     });
     if (!fuse)
@@ -339,6 +351,8 @@ Plan &Model::prepare(size_t b, int slot) {
       GemmArgs g;
       g.bias = l.gateup_b;
       g.out = act;
+      g.discard = attn;  // the o-projection's input
+      g.discard_bytes = attn_bytes;
       if (i < 11) {
         g.l2_next = w.layer[i + 1].qkv_w;
         g.l2_next_bytes = kQkvWBytes;

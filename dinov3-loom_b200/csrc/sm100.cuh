@@ -141,6 +141,20 @@ __device__ __forceinline__ void l2_prefetch_share(const void *p, size_t bytes) {
   }
 }
 
+// Drop this CTA's share (thread t of nt) of a dead buffer from L2 without writing it back
+// (discard.global.L2: afterwards the lines read as indeterminate until written again), so that
+// an intermediate no kernel reads any more neither costs a DRAM write-back nor holds L2 space.
+// [p, p + bytes) is whole 128-byte lines. Only for a buffer whose readers have completed (after
+// griddepcontrol.wait) and that this kernel does not write.
+__device__ __forceinline__ void l2_discard_share(const void *p, size_t bytes, int t, int nt) {
+  const size_t lines = bytes >> 7;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * nt + t; i < lines;
+       i += static_cast<size_t>(gridDim.x) * nt)
+    asm volatile("discard.global.L2 [%0], 128;" ::"l"(
+                     reinterpret_cast<uint64_t>(static_cast<const uint8_t *>(p) + (i << 7)))
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
