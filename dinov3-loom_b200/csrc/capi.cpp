@@ -427,6 +427,61 @@ int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_
   return gemm_entry(dv3::GemmOp::SwiGLU, h, rows, gateup_w, g, status, stream);
 }
 
+int dv3k_matmul_resid_rowstat(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
+                              const float *bias, const float *lambda, uint16_t *x, float *rowstat,
+                              uint32_t *status, void *stream) {
+  if (!all_aligned(a, w, bias, lambda, x, rowstat))
+    return bad_args("pointers must be 16-byte aligned");
+  if (k != 384 && k != 1536) return bad_args("k must be 384 or 1536");
+  if (rowstat == nullptr) return bad_args("rowstat is required");
+  if (rows > 128u * static_cast<uint32_t>(dv3::sm_count(current_device())))
+    return bad_args("rows must fit one 128-row tile per SM");
+  dv3::GemmArgs g;
+  g.bias = bias;
+  g.lambda = lambda;
+  g.out = reinterpret_cast<__half *>(x);
+  g.rowstat = reinterpret_cast<float2 *>(rowstat);
+  return gemm_entry(k == 384 ? dv3::GemmOp::ResidStats384 : dv3::GemmOp::ResidStats1536, a, rows,
+                    w, g, status, stream);
+}
+
+int dv3k_layernorm_rowstat(const uint16_t *x, uint32_t rows, float *rowstat, void *stream) {
+  if (!all_aligned(x, rowstat)) return bad_args("pointers must be 16-byte aligned");
+  if (rowstat == nullptr) return bad_args("rowstat is required");
+  return launch_status(dv3::launch_layernorm_rowstat(reinterpret_cast<const __half *>(x), rows,
+                                                     reinterpret_cast<float2 *>(rowstat),
+                                                     static_cast<cudaStream_t>(stream)),
+                       "layernorm_rowstat");
+}
+
+int dv3k_qkv_rope_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf, const float *cs,
+                         const float *rowstat, const float *rope_cos, const float *rope_sin,
+                         uint16_t *qkv, uint32_t *status, void *stream) {
+  if (!all_aligned(x, wf, cs, rowstat, rope_cos, rope_sin, qkv))
+    return bad_args("pointers must be 16-byte aligned");
+  if (cs == nullptr || rowstat == nullptr) return bad_args("cs and rowstat are required");
+  dv3::GemmArgs g;
+  g.fold_cs = cs;
+  g.rowstat = reinterpret_cast<float2 *>(const_cast<float *>(rowstat));
+  g.rope_cos = rope_cos;
+  g.rope_sin = rope_sin;
+  g.out = reinterpret_cast<__half *>(qkv);
+  return gemm_entry(dv3::GemmOp::QkvRopeFold, x, rows, wf, g, status, stream);
+}
+
+int dv3k_matmul_swiglu_folded(const uint16_t *x, uint32_t rows, const uint16_t *gateup_wf,
+                              const float *cs, const float *rowstat, uint16_t *act,
+                              uint32_t *status, void *stream) {
+  if (!all_aligned(x, gateup_wf, cs, rowstat, act))
+    return bad_args("pointers must be 16-byte aligned");
+  if (cs == nullptr || rowstat == nullptr) return bad_args("cs and rowstat are required");
+  dv3::GemmArgs g;
+  g.fold_cs = cs;
+  g.rowstat = reinterpret_cast<float2 *>(const_cast<float *>(rowstat));
+  g.out = reinterpret_cast<__half *>(act);
+  return gemm_entry(dv3::GemmOp::SwiGLUFold, x, rows, gateup_wf, g, status, stream);
+}
+
 uint32_t dv3k_gateup_source_row(uint32_t packed_row) { return dv3::gateup_source_row(packed_row); }
 
 }  // extern "C"

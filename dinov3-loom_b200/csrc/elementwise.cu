@@ -151,6 +151,47 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The statistics of the LayerNorm only (folded LayerNorm, GemmOp::QkvRopeFold): rowstat[r] =
+// (rstd, -mean rstd) of row r, computed as layernorm_kernel computes them. One row per warp.
+__global__ void __launch_bounds__(256)
+    layernorm_rowstat_kernel(const __half *__restrict__ x, int rows, float2 *__restrict__ rowstat) {
+  pdl_wait();  // the rows written by the previous kernel are complete from here on
+  pdl_trigger();
+  const int row = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;  // whole warp leaves together
+  const __half *xr = x + static_cast<int64_t>(row) * kHidden;
+  const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xr) + lane);
+  const uint2 b = __ldg(reinterpret_cast<const uint2 *>(xr + 256) + lane);
+  const uint32_t w[6] = {a.x, a.y, a.z, a.w, b.x, b.y};
+  float v[12];
+#pragma unroll
+  for (int e = 0; e < 6; ++e) {
+    const float2 f = unpack_half2(w[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 12; ++e) s += v[e];
+  const float mean = warp_sum(s) * (1.0f / kHidden);
+  float d = 0.f;
+#pragma unroll
+  for (int e = 0; e < 12; ++e) {
+    const float t = v[e] - mean;
+    d += t * t;
+  }
+  const float rstd = rsqrtf(warp_sum(d) * (1.0f / kHidden) + 1e-5f);
+  if (lane == 0) rowstat[row] = make_float2(rstd, -mean * rstd);
+}
+
+cudaError_t launch_layernorm_rowstat(const __half *x, uint32_t rows, float2 *rowstat,
+                                     cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  return launch_pdl(layernorm_rowstat_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, x,
+                    static_cast<int>(rows), rowstat);
+}
+
 cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,
                             __half *patches, __half *x, uint32_t *status, cudaStream_t stream,
                             const void *l2_next, size_t l2_next_bytes) {

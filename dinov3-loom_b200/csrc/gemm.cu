@@ -612,6 +612,10 @@ GemmShape gemm_shape(GemmOp op) {
     case GemmOp::ResidLN384: return {384, kHidden, kHidden};
     case GemmOp::ResidLN1536: return {384, kHidden, kMlp};
     case GemmOp::SplitK1536: return {128, kHidden, kMlp};
+    case GemmOp::ResidStats384: return {384, kHidden, kHidden};
+    case GemmOp::ResidStats1536: return {384, kHidden, kMlp};
+    case GemmOp::QkvRopeFold: return {256, kQkv, kHidden};
+    case GemmOp::SwiGLUFold: return {256, kGateUp, kHidden};
   }
   return {0, 0, 0};
 }
@@ -626,6 +630,10 @@ const char *gemm_name(GemmOp op) {
     case GemmOp::ResidLN384: return "gemm_o_resid_layernorm";
     case GemmOp::ResidLN1536: return "gemm_down_resid_layernorm";
     case GemmOp::SplitK1536: return "gemm_down_splitk";
+    case GemmOp::ResidStats384: return "gemm_o_resid_rowstat";
+    case GemmOp::ResidStats1536: return "gemm_down_resid_rowstat";
+    case GemmOp::QkvRopeFold: return "gemm_qkv_rope_folded";
+    case GemmOp::SwiGLUFold: return "gemm_gateup_swiglu_folded";
   }
   return "?";
 }
@@ -633,12 +641,16 @@ const char *gemm_name(GemmOp op) {
 // Width of the tensor the epilogue stores by TMA (0: it writes rows itself).
 static uint32_t tma_store_cols(GemmOp op) {
   switch (op) {
-    case GemmOp::QkvRope: return kQkv;
-    case GemmOp::SwiGLU: return kMlp;
+    case GemmOp::QkvRope:
+    case GemmOp::QkvRopeFold: return kQkv;
+    case GemmOp::SwiGLU:
+    case GemmOp::SwiGLUFold: return kMlp;
     case GemmOp::Resid384:
     case GemmOp::Resid1536:
     case GemmOp::ResidLN384:
-    case GemmOp::ResidLN1536: return kHidden;
+    case GemmOp::ResidLN1536:
+    case GemmOp::ResidStats384:
+    case GemmOp::ResidStats1536: return kHidden;
     default: return 0;
   }
 }
@@ -665,8 +677,11 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
     return true;
   }
   const bool ln = op == GemmOp::ResidLN384 || op == GemmOp::ResidLN1536;
-  // the LayerNorm epilogue moves 64-column blocks (128-byte rows), the others 32-column blocks
-  if (!encode_map_f16_swizzled(&maps->c, out, c_cols, rows, ln ? 64 : 32, 32, ln ? 128 : 64, err))
+  const bool full_row = ln || op == GemmOp::ResidStats384 || op == GemmOp::ResidStats1536;
+  // the full-row residual epilogue moves 64-column blocks (128-byte rows), the others 32-column
+  // blocks
+  if (!encode_map_f16_swizzled(&maps->c, out, c_cols, rows, full_row ? 64 : 32, 32,
+                               full_row ? 128 : 64, err))
     return false;
   if (ln) {
     if (ln_out == nullptr) {
@@ -747,6 +762,8 @@ cudaError_t configure_gemm_kernels() {
   if ((e = configure_one<128, EpiResid>()) != cudaSuccess) return e;
   if ((e = configure_one<384, EpiResidWide>()) != cudaSuccess) return e;
   if ((e = configure_one<256, EpiSwiGLU>()) != cudaSuccess) return e;
+  if ((e = configure_one<256, EpiSwiGLUFold>()) != cudaSuccess) return e;
+  if ((e = configure_one<256, EpiQkvRopeFold>()) != cudaSuccess) return e;
   if ((e = configure_one<384, EpiResidLN>()) != cudaSuccess) return e;
   if ((e = configure_one<128, EpiPartialF32>()) != cudaSuccess) return e;
   int dev = 0;
@@ -781,6 +798,23 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
       return launch_one<384>(maps, rows, s.n, s.k,
                              EpiResidLN{args.bias, args.lambda, args.gamma, args.beta,
                                         args.ln_out_f32 != nullptr},
+                             status, stream, args);
+    case GemmOp::ResidStats384:
+    case GemmOp::ResidStats1536:
+      if (args.rowstat == nullptr) return cudaErrorInvalidValue;
+      return launch_one<384>(maps, rows, s.n, s.k,
+                             EpiResidLN{args.bias, args.lambda, nullptr, nullptr, false,
+                                        args.rowstat},
+                             status, stream, args);
+    case GemmOp::QkvRopeFold:
+      if (args.rowstat == nullptr || args.fold_cs == nullptr) return cudaErrorInvalidValue;
+      return launch_one<256>(maps, rows, s.n, s.k,
+                             EpiQkvRopeFold{args.fold_cs, args.rope_cos, args.rope_sin,
+                                            args.rowstat},
+                             status, stream, args);
+    case GemmOp::SwiGLUFold:
+      if (args.rowstat == nullptr || args.fold_cs == nullptr) return cudaErrorInvalidValue;
+      return launch_one<256>(maps, rows, s.n, s.k, EpiSwiGLUFold{args.fold_cs, args.rowstat},
                              status, stream, args);
     case GemmOp::SplitK1536:
       if (args.splits == 0 || (kMlp / BK) % args.splits != 0) return cudaErrorInvalidValue;

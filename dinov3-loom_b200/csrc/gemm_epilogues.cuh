@@ -101,6 +101,36 @@ __device__ __forceinline__ void ldg32(const float *s, float (&v)[32]) {
   }
 }
 
+// The folded LayerNorm's output for 32 consecutive columns of one row, y = a acc + (c + b s)
+// with a = rstd and b = -mean rstd of the row, in two steps so that the accumulator's TMEM load
+// can be in flight during the first: fold_cs32 forms c + b s from the per-column terms, stored by
+// column pairs (c[2j], c[2j+1], s[2j], s[2j+1]) and read 16 bytes at a time from global memory
+// through L1 (a broadcast, like ldg32) or from shared memory; fold_acc32 adds a acc (raw f32
+// bits from TMEM).
+template <bool kShared>
+__device__ __forceinline__ void fold_cs32(const float *cs, float b, float (&v)[32]) {
+  const float4 *p = reinterpret_cast<const float4 *>(cs);
+  const float2 b2 = make_float2(b, b);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float4 q = kShared ? p[j] : __ldg(p + j);
+    const float2 t = __ffma2_rn(b2, make_float2(q.z, q.w), make_float2(q.x, q.y));
+    v[2 * j] = t.x;
+    v[2 * j + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void fold_acc32(float a, const uint32_t (&acc)[32], float (&v)[32]) {
+  const float2 a2 = make_float2(a, a);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float2 t = __ffma2_rn(a2, make_float2(u2f(acc[2 * j]), u2f(acc[2 * j + 1])),
+                                make_float2(v[2 * j], v[2 * j + 1]));
+    v[2 * j] = t.x;
+    v[2 * j + 1] = t.y;
+  }
+}
+
 __device__ __forceinline__ void ldg_half32(const __half *src, uint4 (&q)[4]) {
   const uint4 *p = reinterpret_cast<const uint4 *>(src);
 #pragma unroll
@@ -213,23 +243,39 @@ struct EpiPatch {
 // the packed [196][64] table (rows padded to 17 floats so the 32 rows of a warp fall in distinct
 // banks); the packed entries for channels c and c+32 are equal. Columns >= 1152 (the zero-filled
 // tail of the last 256-wide tile) are neither computed nor stored.
+// Folded form (kFold): A is x instead of LN(x), and the projection before RoPE is
+// rstd acc - mean rstd s + c, from the row's (rstd, -mean rstd) and the folded vectors.
 // ---------------------------------------------------------------------------------------------
-struct EpiQkvRope {
+template <bool kFold>
+struct EpiQkvRopeT {
+  // kFold (the LayerNorm before the projection folded in, GemmOp::QkvRopeFold): the pairs (c, s)
+  // of each output column, c = b + W beta, s = the row sum of W'
   const float *bias;
   const float *cosv;
   const float *sinv;
+  const float2 *rowstat = nullptr;  // kFold: each row's (rstd, -mean rstd)
   static constexpr int kPad = 17;
   static constexpr int kTab = 14 * kPad;                   // floats per (axis, function)
   static constexpr int kRopeBytes = ((4 * kTab * 4 + 15) / 16) * 16;
-  static constexpr int kSmem = kRopeBytes + kQkv * 4;       // + bias
+  static constexpr int kSmem = kRopeBytes + (kFold ? 2 : 1) * kQkv * 4;  // + bias, or (c, s)
   static constexpr bool kTmaStore = true;
   // One staging block per warp: the 16 KB saved let a fourth 48 KB mainloop stage fit beside
   // the RoPE tables and the bias. Measured no faster: the two 16-column halves of that block
   // used in turn (twice the TMA store instructions delayed the producer's loads), and the
   // second head's accumulator loaded from TMEM during the first head's stores.
   static constexpr int kStagingBufs = 1;
-  using Pre = NoPre;
-  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
+  struct Pre {
+    float a, b;  // kFold: this row's rstd and -mean rstd
+  };
+  __device__ Pre prefetch(int, const EpiCtx &c) const {
+    if constexpr (kFold) {
+      if (c.row < c.M) {
+        const float2 v = __ldg(rowstat + c.row);
+        return {v.x, v.y};
+      }
+    }
+    return {1.f, 0.f};
+  }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     float *t = reinterpret_cast<float *>(smem);
     for (int i = tid; i < 4 * 14 * 16; i += n) {
@@ -238,7 +284,8 @@ struct EpiQkvRope {
       const int src = (which < 2) ? (pos * 14) * 64 + j : pos * 64 + 16 + j;
       t[which * kTab + pos * kPad + j] = __ldg(((which & 1) ? sinv : cosv) + src);
     }
-    stage_floats(reinterpret_cast<float *>(smem + kRopeBytes), bias, kQkv, tid, n);
+    stage_floats(reinterpret_cast<float *>(smem + kRopeBytes), bias, (kFold ? 2 : 1) * kQkv, tid,
+                 n);
   }
   template <int COLS>
   __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
@@ -256,15 +303,27 @@ struct EpiQkvRope {
     for (int h = h0; h < h1; h += 64) {
       const int col = n0 + h;  // first column of this 64-wide head
       if (col >= kQkv) break;  // warp-uniform
-      uint32_t ra[32], rb[32];
-      tmem_load32x2(taddr + h, ra, taddr + h + 32, rb);
       float lo[32], hi[32];
-      lds32(sb + col, lo);
-      lds32(sb + col + 32, hi);
+      if constexpr (kFold) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + h, ra);  // in flight while c + b s is formed
+        tmem_ld32(taddr + h + 32, rb);
+        fold_cs32<true>(sb + 2 * col, pre.b, lo);
+        fold_cs32<true>(sb + 2 * (col + 32), pre.b, hi);
+        tmem_wait_ld(ra);
+        tmem_regs_ready(rb);
+        fold_acc32(pre.a, ra, lo);
+        fold_acc32(pre.a, rb, hi);
+      } else {
+        uint32_t ra[32], rb[32];
+        tmem_load32x2(taddr + h, ra, taddr + h + 32, rb);
+        lds32(sb + col, lo);
+        lds32(sb + col + 32, hi);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        lo[i] += u2f(ra[i]);
-        hi[i] += u2f(rb[i]);
+        for (int i = 0; i < 32; ++i) {
+          lo[i] += u2f(ra[i]);
+          hi[i] += u2f(rb[i]);
+        }
       }
       if (patch_row && col < 2 * kHidden) {  // q and k columns of patch tokens rotate
 #pragma unroll
@@ -281,6 +340,8 @@ struct EpiQkvRope {
     }
   }
 };
+using EpiQkvRope = EpiQkvRopeT<false>;
+using EpiQkvRopeFold = EpiQkvRopeT<true>;
 
 // ---------------------------------------------------------------------------------------------
 // Split-K partial product (kernels/matmul_splitk_f16_wmma.loom): the f32 accumulator of this
@@ -475,15 +536,33 @@ struct EpiResidWide {
 // ---------------------------------------------------------------------------------------------
 // Gate/up with SwiGLU: the weight rows are packed 64 gate rows, the matching 64 up rows, ...;
 // act[row][j] = f16(silu(g + bg) (u + bu)), silu through the hardware tanh (one MUFU op).
+// Folded form (kFold): A is x instead of LN(x), g = rstd acc_g - mean rstd s_g + c_g (and u the
+// same), from the row's (rstd, -mean rstd) and the folded vectors.
 // ---------------------------------------------------------------------------------------------
-struct EpiSwiGLU {
-  const float *bias;  // packed like the weight rows
-  // The bias is read through L1 (every lane of a warp reads the same 32 floats) rather than staged
-  // in shared memory: without it four 48 KB stages fit beside the TMA-store staging (three with).
+template <bool kFold>
+struct EpiSwiGLUT {
+  // packed like the weight rows; kFold (the LayerNorm before the projection folded in,
+  // GemmOp::SwiGLUFold): the pairs (c, s) of each output column, c = b + W beta, s = the row sum
+  // of W'
+  const float *bias;
+  const float2 *rowstat = nullptr;  // kFold: each row's (rstd, -mean rstd)
+  // The vectors are read through L1 (every lane of a warp reads the same 32 floats) rather than
+  // staged in shared memory: without them four 48 KB stages fit beside the TMA-store staging
+  // (three with).
   static constexpr int kSmem = 0;
   static constexpr bool kTmaStore = true;
-  using Pre = NoPre;
-  __device__ Pre prefetch(int, const EpiCtx &) const { return {}; }
+  struct Pre {
+    float a, b;  // kFold: this row's rstd and -mean rstd
+  };
+  __device__ Pre prefetch(int, const EpiCtx &c) const {
+    if constexpr (kFold) {
+      if (c.row < c.M) {
+        const float2 v = __ldg(rowstat + c.row);
+        return {v.x, v.y};
+      }
+    }
+    return {1.f, 0.f};
+  }
   __device__ void init(uint8_t *, int, int) const {}
   template <int COLS>
   __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
@@ -496,18 +575,34 @@ struct EpiSwiGLU {
     for (int g = 0; g < g1; g += 128) {
 #pragma unroll 1
       for (int sub = s0; sub < s1; sub += 32) {
-        uint32_t rg[32], ru[32];
-        tmem_load32x2(taddr + g + sub, rg, taddr + g + 64 + sub, ru);
         float gv[32], uv[32];
-        ldg32(sb + n0 + g + sub, gv);
-        ldg32(sb + n0 + g + 64 + sub, uv);
+        if constexpr (kFold) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(taddr + g + sub, rg);  // in flight while c + b s is formed
+          tmem_ld32(taddr + g + 64 + sub, ru);
+          fold_cs32<false>(sb + 2 * (n0 + g + sub), pre.b, gv);
+          fold_cs32<false>(sb + 2 * (n0 + g + 64 + sub), pre.b, uv);
+          tmem_wait_ld(rg);
+          tmem_regs_ready(ru);
+          fold_acc32(pre.a, rg, gv);
+          fold_acc32(pre.a, ru, uv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i] + u2f(rg[i])) * (uv[i] + u2f(ru[i]));
+          for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i]) * uv[i];
+        } else {
+          uint32_t rg[32], ru[32];
+          tmem_load32x2(taddr + g + sub, rg, taddr + g + 64 + sub, ru);
+          ldg32(sb + n0 + g + sub, gv);
+          ldg32(sb + n0 + g + 64 + sub, uv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i] + u2f(rg[i])) * (uv[i] + u2f(ru[i]));
+        }
         tma_emit32(c, gv, (n0 + g) / 2 + sub);
       }
     }
   }
 };
+using EpiSwiGLU = EpiSwiGLUT<false>;
+using EpiSwiGLUFold = EpiSwiGLUT<true>;
 
 // ---------------------------------------------------------------------------------------------
 // Residual update fused with the following LayerNorm, on full-row tiles (BN = 384, one tile per
@@ -526,7 +621,9 @@ struct EpiSwiGLU {
 // of squares of its 192 values, and the two warps of a row merge them through shared memory
 // (Chan et al.: M2 = M2a + M2b + d^2 n_a n_b / n), eps 1e-5, f32. The normalised blocks reuse
 // the staging region once the x stores have read it: three f16 blocks, or (f32 output) two
-// rounds of three 32-row x 32-column f32 blocks.
+// rounds of three 32-row x 32-column f32 blocks. With `rowstat` set (GemmOp::ResidStats*, the
+// LayerNorm folded into the next GEMM) the epilogue stops after the statistics and leaves
+// (rstd, -mean rstd) of each row instead of normalising it.
 // ---------------------------------------------------------------------------------------------
 struct EpiResidLN {
   const float *bias;
@@ -534,6 +631,9 @@ struct EpiResidLN {
   const float *gamma;
   const float *beta;
   bool f32_out;
+  // GemmOp::ResidStats*: the LayerNorm is folded into the next GEMM, so instead of normalising
+  // the row this epilogue leaves rowstat[row] = (rstd, -mean rstd) (gamma and beta unused).
+  float2 *rowstat = nullptr;
   static constexpr int kVecs = 4 * kHidden;  // bias, lambda, gamma, beta
   static constexpr int kSmem = kVecs * 4 + 4 * 128 * 4;  // + [mean|M2][2 halves][128 rows]
   static constexpr bool kTmaStore = true;
@@ -551,6 +651,7 @@ struct EpiResidLN {
     float *s = reinterpret_cast<float *>(smem);
     stage_floats(s, bias, kHidden, tid, n);
     stage_floats(s + kHidden, lambda, kHidden, tid, n);
+    if (rowstat) return;
     stage_floats(s + 2 * kHidden, gamma, kHidden, tid, n);
     stage_floats(s + 3 * kHidden, beta, kHidden, tid, n);
   }
@@ -662,6 +763,10 @@ struct EpiResidLN {
     mean = 0.5f * (m0 + m1);
     m2 = red[256 + c.r] + red[384 + c.r] + d * d * (kHidden / 4);
     const float rstd = rsqrtf(m2 * (1.0f / kHidden) + 1e-5f);
+    if (rowstat) {  // folded LayerNorm: the consumer normalises
+      if (c.half == 0 && c.row < c.M) rowstat[c.row] = make_float2(rstd, -mean * rstd);
+      return;
+    }
     // h = (x rstd - mean rstd) gamma + beta, staged where the x blocks were. Each output block
     // overwrites a block whose store was committed three groups earlier (an x block, or for f32
     // output the first round of f32 blocks), so waiting until at most two groups are still

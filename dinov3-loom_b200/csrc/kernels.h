@@ -52,6 +52,11 @@ bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uin
 // ln_out_f32. SplitK1536: the down projection's K split into `splits` slices, each CTA writing
 // the f32 partial product of its slice (no bias) into slab s of partials [splits][rows][384]
 // (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it.
+// Folded LayerNorm (no counterpart in the reference; the weights in weights.cpp): ResidStats*
+// update x like ResidLN* but leave only rowstat[row] = (rstd, -mean rstd) of the updated row;
+// QkvRopeFold and SwiGLUFold then read x itself and apply the LayerNorm in their epilogues,
+// acc' = x W'^T, y = rstd acc' - mean rstd s + c (W' = f16(W gamma), s its row sums,
+// c = b + W beta), before RoPE or SwiGLU.
 enum class GemmOp {
   Patch,
   QkvRope,
@@ -60,7 +65,11 @@ enum class GemmOp {
   SwiGLU,
   ResidLN384,
   ResidLN1536,
-  SplitK1536
+  SplitK1536,
+  ResidStats384,
+  ResidStats1536,
+  QkvRopeFold,
+  SwiGLUFold
 };
 
 struct GemmShape {
@@ -103,6 +112,10 @@ struct GemmArgs {
   float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
   float *partials = nullptr;     // SplitK1536: [splits][rows][384] f32
   uint32_t splits = 1;           // SplitK1536: K slices (a divisor of 24, the 64-wide k-blocks)
+  // Folded LayerNorm: ResidStats* write and QkvRopeFold / SwiGLUFold read (rstd, -mean rstd)
+  // per row; the folded GEMMs take (c, s) per output column in `fold_cs` (`bias` unused).
+  float2 *rowstat = nullptr;
+  const float *fold_cs = nullptr;
   // Weights of a later kernel (16-byte aligned; no kernel writes them) that this launch starts
   // toward L2, so that kernel's first tiles do not wait for DRAM.
   const void *l2_next = nullptr;
@@ -166,6 +179,10 @@ cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *ga
                                  const float *beta, __half *out, cudaStream_t stream);
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, float *out, cudaStream_t stream);
+// The statistics of the LayerNorm only: rowstat[r] = (rstd, -mean rstd) of row r of x (the
+// folded LayerNorm of the QKV GEMM after the patch embedding).
+cudaError_t launch_layernorm_rowstat(const __half *x, uint32_t rows, float2 *rowstat,
+                                     cudaStream_t stream);
 
 // Split-K completion (kernels/splitk_reduce_f16.loom): x[r][n] = f16(x + lambda[n] (sum over
 // s = 0..splits-1 in that order of partials[s][r][n] + b[n])), one warp per row. With gamma and

@@ -14,6 +14,8 @@
 //   out     f32 [201B][384]        final LayerNorm output
 //   status  u32 [2]                device failure bits, non-finite input flag (sticky until read)
 //   pmean   f32 [B][384]           patch-token means (patch_mean readout)
+//   rowstat f32 [201B][2]          (rstd, -mean rstd) of each token row: the LayerNorm that the
+//                                  QKV and gate/up GEMMs apply themselves (folded plan)
 //   image1, out1                   the second serving slot's input and output (slot 0 uses
 //                                  image and out)
 // The QKV buffer needs no headroom rows: attention reads through TMA, whose out-of-bounds rows
@@ -129,6 +131,10 @@ Model::Model(const std::string &path, dv3_options options)
       l.norm2_b = fp(s + "norm2_b");
       l.ls1 = fp(s + "ls1");
       l.ls2 = fp(s + "ls2");
+      l.qkv_wf = hp(s + "qkv_wf");
+      l.gateup_wf = hp(s + "gateup_wf");
+      l.qkv_cs = fp(s + "qkv_cs");
+      l.gateup_cs = fp(s + "gateup_cs");
     }
 
     // Activations for max_batch images.
@@ -139,13 +145,13 @@ Model::Model(const std::string &path, dv3_options options)
       const uint32_t r = static_cast<uint32_t>(kTokens * b);
       partial_floats = std::max(partial_floats, static_cast<size_t>(splitk_splits(r)) * r * kHidden);
     }
-    const size_t sizes[13] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
+    const size_t sizes[14] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
                               R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
                               R * kMlp * 2,           R * kHidden * 4, 256,
                               B * kHidden * 4,        B * kImageElements * 4, R * kHidden * 4,
-                              partial_floats * 4};
-    size_t at[13], act_total = 0;
-    for (int i = 0; i < 13; ++i) {
+                              partial_floats * 4,     R * 8};
+    size_t at[14], act_total = 0;
+    for (int i = 0; i < 14; ++i) {
       at[i] = act_total;
       act_total += align256(sizes[i]);
     }
@@ -153,6 +159,7 @@ Model::Model(const std::string &path, dv3_options options)
     uint8_t *a = static_cast<uint8_t *>(act_blob_);
     image_ = reinterpret_cast<float *>(a + at[0]);
     partials_ = reinterpret_cast<float *>(a + at[12]);
+    rowstat_ = reinterpret_cast<float2 *>(a + at[13]);
     patches_ = reinterpret_cast<__half *>(a + at[1]);
     x_ = reinterpret_cast<__half *>(a + at[2]);
     h_ = reinterpret_cast<__half *>(a + at[3]);
@@ -219,7 +226,10 @@ void Model::release() {
 // LayerNorm separately (87 launches at b > 1); here each one after layer 0's first rides in the
 // epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches), whenever the
 // residual GEMMs run on full rows (large batches; see resid_wide); small batches keep 128-wide
-// residual tiles and separate LayerNorm launches (3 + 12*7 = 87).
+// residual tiles and separate LayerNorm launches (3 + 12*7 = 87). With the full-row residual
+// GEMMs, the LayerNorms before QKV and gate/up are further folded into those GEMMs
+// (fold_layernorm): the residual GEMM (and, for layer 0, layernorm_rowstat) leaves only each
+// row's statistics and QKV / gate/up read x.
 // DV3_FUSE_LAYERNORM=0 in the environment restores the separate LayerNorm launches (the
 // reference's plan) for comparison; =1 forces fusion.
 // K slices of the down projection at this batch size (1: unsplit). DV3_SPLITK=0 in the
@@ -233,6 +243,18 @@ uint32_t Model::down_splits(uint32_t rows) const {
 bool Model::fuse_layernorm(size_t b) const {
   if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
   return resid_wide(static_cast<uint32_t>(kTokens * b));
+}
+
+// With the LayerNorms fused into the full-row residual GEMMs, each of them except the final one
+// is folded one step further into the GEMM that consumes it: the residual GEMM leaves only
+// (rstd, -mean rstd) per row instead of normalising the row, and the QKV and gate/up GEMMs read
+// x with the folded weights (weights.cpp). Returns which LayerNorms are folded: bit 0 LN1
+// (into QKV), bit 1 LN2 (into gate/up). DV3_FOLD_LAYERNORM in the environment picks them for
+// comparison (0: none, keeping the normalised h; 1: LN1; 2: LN2; 3: both).
+int Model::fold_layernorm(size_t b) const {
+  if (!fuse_layernorm(b)) return 0;
+  if (const char *v = std::getenv("DV3_FOLD_LAYERNORM")) return (v[0] - '0') & 3;
+  return 3;
 }
 
 // Bytes of each projection's f16 weights. Each launch of the plan starts the weights of a GEMM
@@ -263,6 +285,9 @@ Plan &Model::prepare(size_t b, int slot) {
   const DeviceWeights w = w_;
   float *image = image_slot_[slot], *out = out_slot_[slot];
   __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
+  float2 *rowstat = rowstat_;
+  const int fold_mask = fold_layernorm(b);
+  const bool fold = fold_mask & 1, fold2 = (fold_mask & 2) != 0;  // LN1 into QKV, LN2 into gate/up
 
   GemmMaps patch_maps;
   need(make_gemm_maps(GemmOp::Patch, patches, p, w.patch_w, x, &patch_maps, &err));
@@ -275,15 +300,20 @@ Plan &Model::prepare(size_t b, int slot) {
   });
   add(gemm_name(GemmOp::Patch), [=](cudaStream_t s) {
     GemmArgs g;
-    g.l2_next = w.layer[0].qkv_w;
+    g.l2_next = fold ? w.layer[0].qkv_wf : w.layer[0].qkv_w;
     g.l2_next_bytes = kQkvWBytes;
     g.bias = w.patch_b;
     g.out = x;
     return launch_gemm(GemmOp::Patch, patch_maps, p, g, st, s);
   });
-  add("layernorm_f16", [=](cudaStream_t s) {
-    return launch_layernorm_f16(x, r, w.layer[0].norm1_w, w.layer[0].norm1_b, h, s);
-  });
+  if (fold)
+    add("layernorm_rowstat", [=](cudaStream_t s) {
+      return launch_layernorm_rowstat(x, r, rowstat, s);
+    });
+  else
+    add("layernorm_f16", [=](cudaStream_t s) {
+      return launch_layernorm_f16(x, r, w.layer[0].norm1_w, w.layer[0].norm1_b, h, s);
+    });
   const bool fuse = fuse_layernorm(b);
   const GemmOp o_op = fuse ? GemmOp::ResidLN384 : GemmOp::Resid384;
   const GemmOp down_op = fuse ? GemmOp::ResidLN1536 : GemmOp::Resid1536;
@@ -302,19 +332,27 @@ Plan &Model::prepare(size_t b, int slot) {
   for (int i = 0; i < 12; ++i) {
     const LayerWeights &l = w.layer[i];
     GemmMaps qkv_maps, o_maps, gu_maps, down_maps;
-    need(make_gemm_maps(GemmOp::QkvRope, h, r, l.qkv_w, qkv, &qkv_maps, &err));
-    need(make_gemm_maps(o_op, attn, r, l.o_w, x, &o_maps, &err, h));
-    need(make_gemm_maps(GemmOp::SwiGLU, h, r, l.gateup_w, act, &gu_maps, &err));
+    // folded: QKV and gate/up read x, the residual GEMMs leave row statistics
+    const GemmOp qkv_op = fold ? GemmOp::QkvRopeFold : GemmOp::QkvRope;
+    const GemmOp gu_op = fold2 ? GemmOp::SwiGLUFold : GemmOp::SwiGLU;
+    const GemmOp o_op_l = fold2 ? GemmOp::ResidStats384 : o_op;
+    const GemmOp down_op_l = fold && i < 11 ? GemmOp::ResidStats1536 : down_op;
+    need(make_gemm_maps(qkv_op, fold ? x : h, r, fold ? l.qkv_wf : l.qkv_w, qkv, &qkv_maps, &err));
+    need(make_gemm_maps(o_op_l, attn, r, l.o_w, x, &o_maps, &err, h));
+    need(make_gemm_maps(gu_op, fold2 ? x : h, r, fold2 ? l.gateup_wf : l.gateup_w, act, &gu_maps,
+                        &err));
     if (splits > 1)
       need(make_gemm_maps(GemmOp::SplitK1536, act, r, l.down_w, partials, &down_maps, &err,
                           nullptr, false, splits));
     else
-      need(make_gemm_maps(down_op, act, r, l.down_w, x, &down_maps, &err,
+      need(make_gemm_maps(down_op_l, act, r, l.down_w, x, &down_maps, &err,
                           i == 11 ? static_cast<const void *>(out) : static_cast<const void *>(h),
                           i == 11));
-    add(gemm_name(GemmOp::QkvRope), [=](cudaStream_t s) {
+    add(gemm_name(qkv_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;
+      g.fold_cs = l.qkv_cs;
+      g.rowstat = rowstat;
       g.rope_cos = w.rope_cos;
       g.rope_sin = w.rope_sin;
       g.out = qkv;
@@ -323,13 +361,14 @@ Plan &Model::prepare(size_t b, int slot) {
       // the patch GEMM's input (layer 0), or the previous layer's down-projection input
       g.discard = i == 0 ? static_cast<const void *>(patches) : static_cast<const void *>(act);
       g.discard_bytes = i == 0 ? patches_bytes : act_bytes;
-      return launch_gemm(GemmOp::QkvRope, qkv_maps, r, g, st, s);
+      return launch_gemm(qkv_op, qkv_maps, r, g, st, s);
     });
-    add("attention", [=](cudaStream_t s) {  // h: the QKV GEMM's input
-      return launch_attention(attn_map, r, st, s, l.gateup_w, kGateUpWBytes, h, h_bytes);
+    add("attention", [=](cudaStream_t s) {  // h: the QKV GEMM's input (x, still live, if folded)
+      return launch_attention(attn_map, r, st, s, fold2 ? l.gateup_wf : l.gateup_w, kGateUpWBytes,
+                              fold ? nullptr : h, fold ? 0 : h_bytes);
     });
     // o-proj + LayerScale 1 + residual, and LN2 of this layer (fused or separate): x -> x, h
-    add(gemm_name(o_op), [=](cudaStream_t s) {
+    add(gemm_name(o_op_l), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.o_b;
       g.lambda = l.ls1;
@@ -337,27 +376,30 @@ Plan &Model::prepare(size_t b, int slot) {
       g.gamma = l.norm2_w;
       g.beta = l.norm2_b;
       g.ln_out = h;
+      g.rowstat = rowstat;
       g.l2_next = l.down_w;
       g.l2_next_bytes = kDownWBytes;
       g.discard = qkv;  // the attention's input
       g.discard_bytes = qkv_bytes;
-      return launch_gemm(o_op, o_maps, r, g, st, s);
+      return launch_gemm(o_op_l, o_maps, r, g, st, s);
     });
     if (!fuse)
       add("layernorm_f16", [=](cudaStream_t s) {
         return launch_layernorm_f16(x, r, l.norm2_w, l.norm2_b, h, s);
       });
-    add(gemm_name(GemmOp::SwiGLU), [=](cudaStream_t s) {
+    add(gemm_name(gu_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.gateup_b;
+      g.fold_cs = l.gateup_cs;
+      g.rowstat = rowstat;
       g.out = act;
       g.discard = attn;  // the o-projection's input
       g.discard_bytes = attn_bytes;
       if (i < 11) {
-        g.l2_next = w.layer[i + 1].qkv_w;
+        g.l2_next = fold ? w.layer[i + 1].qkv_wf : w.layer[i + 1].qkv_w;
         g.l2_next_bytes = kQkvWBytes;
       }
-      return launch_gemm(GemmOp::SwiGLU, gu_maps, r, g, st, s);
+      return launch_gemm(gu_op, gu_maps, r, g, st, s);
     });
     // down-proj + LayerScale 2 + residual, fused with LN1 of the next layer (f16 h) or, after
     // the last layer, with the final LayerNorm (f32 output)
@@ -377,7 +419,7 @@ Plan &Model::prepare(size_t b, int slot) {
       });
       continue;
     }
-    add(gemm_name(down_op), [=](cudaStream_t s) {
+    add(gemm_name(down_op_l), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.down_b;
       g.lambda = l.ls2;
@@ -386,7 +428,8 @@ Plan &Model::prepare(size_t b, int slot) {
       g.beta = nb;
       g.ln_out = last ? nullptr : h;
       g.ln_out_f32 = last ? out : nullptr;
-      return launch_gemm(down_op, down_maps, r, g, st, s);
+      g.rowstat = rowstat;
+      return launch_gemm(down_op_l, down_maps, r, g, st, s);
     });
     if (!fuse) {
       if (last)

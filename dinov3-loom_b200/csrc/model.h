@@ -25,6 +25,10 @@ struct LayerWeights {
   const __half *qkv_w, *gateup_w, *o_w, *down_w;
   const float *qkv_b, *gateup_b, *o_b, *down_b;
   const float *norm1_w, *norm1_b, *norm2_w, *norm2_b, *ls1, *ls2;
+  // The QKV and gate/up projections with the LayerNorm before them folded in (weights.cpp):
+  // W' = f16(W gamma), and per output column the pair (c, s): c = b + W beta, s = row sum of W'.
+  const __half *qkv_wf, *gateup_wf;
+  const float *qkv_cs, *gateup_cs;
 };
 
 struct DeviceWeights {
@@ -92,6 +96,7 @@ class Model {
   Plan &prepare(size_t batch, int slot = 0);    // build + capture once per batch size and slot
   void drain();                                  // finish every outstanding submission
   bool fuse_layernorm(size_t batch) const;      // plan variant for this batch size
+  int fold_layernorm(size_t batch) const;       // LayerNorms folded into QKV (1), gate/up (2)
   uint32_t down_splits(uint32_t rows) const;    // split-K slices of the down projection
   void check_status();                          // read the device status words (synchronous)
   void activate() const;
@@ -110,6 +115,7 @@ class Model {
          *patches_ = nullptr;
   float *image_ = nullptr, *out_ = nullptr, *pmean_ = nullptr;
   float *partials_ = nullptr;  // split-K partial slabs of the down projection
+  float2 *rowstat_ = nullptr;  // per token row (rstd, -mean rstd) of the folded LayerNorm
   float *image_slot_[2] = {}, *out_slot_[2] = {};  // slot 0 aliases image_ / out_
   // Per slot: upload done, forward done (input consumed, output ready), download done.
   cudaEvent_t ev_in_[2] = {}, ev_done_[2] = {}, ev_out_[2] = {};

@@ -410,6 +410,46 @@ std::map<std::string, Packed> load_weights(const std::string &path) {
     w.h = std::move(wp);
     b.f = std::move(bp);
   }
+  // LayerNorm folded into the GEMM that consumes it (no counterpart in the reference). With
+  // h = (x - mu) rstd gamma + beta and W the packed f16 weights,
+  //   h W^T + b = rstd (x W'^T) - mu rstd s + c,  W' = f16(W gamma),  s[n] = sum_k W'[n][k],
+  //   c[n] = b[n] + sum_k W[n][k] beta[k],
+  // so the kernel that updates x leaves only (rstd, -mu rstd) per row and the QKV and gate/up
+  // GEMMs read x itself. s sums the rounded W', so rstd (x W'^T - mu s) = rstd ((x - mu) W'^T)
+  // up to the f32 accumulation. c and s are stored by column pairs, (c[2j], c[2j+1], s[2j],
+  // s[2j+1]), so one 16-byte load gives a kernel both terms of two columns. Emitted after every
+  // reference tensor, so the reference's first error is still the one reported.
+  auto fold = [&](const std::string &s, const std::string &mat, const std::string &norm) {
+    const Packed &w = out.at(s + mat + "_w");
+    const Packed &b = out.at(s + mat + "_b");
+    const std::vector<float> &g = out.at(s + norm + "_w").f, &be = out.at(s + norm + "_b").f;
+    const size_t n = b.f.size();
+    std::vector<float> wf(w.h.size()), cv(n);
+    for (size_t r = 0; r < n; ++r) {
+      double c = b.f[r];
+      for (size_t k = 0; k < H; ++k) {
+        const float v = f16_to_f32(w.h[r * H + k]);
+        wf[r * H + k] = v * g[k];
+        c += static_cast<double>(v) * be[k];
+      }
+      cv[r] = static_cast<float>(c);
+    }
+    emit(s + mat + "_wf", wf, true);
+    const std::vector<uint16_t> &packed = out.at(s + mat + "_wf").h;
+    std::vector<float> cs(2 * n);  // per column pair: c[2j], c[2j+1], s[2j], s[2j+1]
+    for (size_t r = 0; r < n; ++r) {
+      double acc = 0.0;
+      for (size_t k = 0; k < H; ++k) acc += f16_to_f32(packed[r * H + k]);
+      cs[4 * (r / 2) + r % 2] = cv[r];
+      cs[4 * (r / 2) + 2 + r % 2] = static_cast<float>(acc);
+    }
+    emit(s + mat + "_cs", cs, false);
+  };
+  for (int i = 0; i < 12; ++i) {
+    const std::string s = "l" + std::to_string(i) + "_";
+    fold(s, "qkv", "norm1");
+    fold(s, "gateup", "norm2");
+  }
   return out;
 }
 

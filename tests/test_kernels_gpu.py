@@ -359,6 +359,152 @@ def test_matmul_swiglu(b):
     assert_close16(act, ref)
 
 
+# Folded LayerNorm (no counterpart in the reference): the residual GEMM leaves (rstd, -mean rstd)
+# per row and the QKV and gate/up GEMMs read x with W' = f16(W gamma), s = row sums of W',
+# c = b + W beta (weights.cpp). References: the unrounded float64 LayerNorm of x, then the op;
+# the folded kernels are held to the accuracy of the unfolded kernels on h = f16(LN(x)).
+def ln_stats(x):
+    mean = x.mean(axis=1)
+    var = ((x - mean[:, None]) ** 2).mean(axis=1)
+    rstd = 1.0 / np.sqrt(var + 1e-5)
+    return rstd, -mean * rstd
+
+
+def fold(w, b, g, be):
+    """The folded weights of weights.cpp from f16 weights w [n][384], bias b, LayerNorm g, be:
+    wf = f16(w g), and c and s by output column pairs (c[2j], c[2j+1], s[2j], s[2j+1])."""
+    g32, be32 = g.astype(np.float32), be.astype(np.float32)
+    wf = (w.astype(np.float32) * g32).astype(np.float16)
+    s = wf.astype(np.float64).sum(axis=1)
+    c = b.astype(np.float32).astype(np.float64) + w @ be32.astype(np.float64)
+    return wf, np.stack([c.reshape(-1, 2), s.reshape(-1, 2)], axis=1).ravel()
+
+
+def ln64(x, g, be):
+    rstd, nm = ln_stats(x)
+    return (x * rstd[:, None] + nm[:, None]) * g.astype(np.float32) + be.astype(np.float32)
+
+
+def rowstat_of(x):
+    rstd, nm = ln_stats(x)
+    return np.stack([rstd, nm], axis=1).astype(np.float32)
+
+
+def scaled_err(got, ref):
+    got = got.float().cpu().numpy().astype(np.float64)
+    return np.abs(got - ref) / np.maximum(1.0, np.abs(ref))
+
+
+def assert_as_accurate(folded, plain, ref):
+    """The folded GEMM rounds W gamma to f16 where the unfolded one rounds LN(x) to f16 (h), so
+    both carry one f16 rounding of their inputs: against the unrounded float64 reference the
+    folded output must be about as accurate as the unfolded kernel on h = f16(LN(x))."""
+    ef, ep = scaled_err(folded, ref), scaled_err(plain, ref)
+    rms_f, rms_p = np.sqrt((ef ** 2).mean()), np.sqrt((ep ** 2).mean())
+    assert ef.max() <= max(4e-3, 2.0 * ep.max()), f"max {ef.max():.3e} vs unfolded {ep.max():.3e}"
+    assert rms_f <= 1.5 * rms_p + 1e-6, f"rms {rms_f:.3e} vs unfolded {rms_p:.3e}"
+
+
+@pytest.mark.parametrize("b", [1, 64])
+def test_layernorm_rowstat(b):
+    rng = np.random.default_rng(80 + b)
+    r = rows_of(b)
+    x = f16(rng.standard_normal((r, 384)) * 3 + rng.standard_normal((r, 1)))
+    out = torch.empty((r, 2), dtype=torch.float32, device=DEV)
+    check_rc(lib().dv3k_layernorm_rowstat(ptr(t16(x)), r, ptr(out), stream()))
+    torch.cuda.synchronize()
+    want = rowstat_of(x)
+    got = out.cpu().numpy()
+    assert np.abs(got[:, 0] / want[:, 0] - 1).max() < 1e-5
+    assert np.abs(got[:, 1] - want[:, 1]).max() < 1e-5 * np.abs(want[:, 1]).max() + 1e-6
+
+
+@pytest.mark.parametrize("k", [384, 1536])
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_matmul_resid_rowstat(k, b):
+    """x is updated bit for bit as by dv3k_matmul_resid_layernorm; rowstat holds the statistics
+    of the stored f16 rows."""
+    rng = np.random.default_rng(90 + b + k)
+    r = rows_of(b)
+    a = f16(rng.standard_normal((r, k)))
+    w = f16(rng.standard_normal((384, k)) / np.sqrt(k))
+    bias = rng.standard_normal(384) * 0.1
+    lam = rng.random(384) * 0.2 + 0.05
+    x0 = f16(rng.standard_normal((r, 384)) + rng.standard_normal((r, 1)))
+    g = rng.standard_normal(384) * 0.3 + 1
+    be = rng.standard_normal(384) * 0.1
+    x_ln, x_st = t16(x0), t16(x0)
+    h = torch.empty((r, 384), dtype=torch.float16, device=DEV)
+    rs = torch.empty((r, 2), dtype=torch.float32, device=DEV)
+    st = status()
+    ad, wd, bd, ld = t16(a), t16(w), t32(bias), t32(lam)
+    check_rc(lib().dv3k_matmul_resid_layernorm(ptr(ad), r, k, ptr(wd), ptr(bd), ptr(ld), ptr(x_ln),
+                                               ptr(t32(g)), ptr(t32(be)), ptr(h), None, ptr(st),
+                                               stream()))
+    check_rc(lib().dv3k_matmul_resid_rowstat(ptr(ad), r, k, ptr(wd), ptr(bd), ptr(ld), ptr(x_st),
+                                             ptr(rs), ptr(st), stream()))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist() == [0, 0]
+    np.testing.assert_array_equal(x_st.cpu().numpy().view(np.uint16), x_ln.cpu().numpy().view(np.uint16))
+    want = rowstat_of(x_st.float().cpu().numpy().astype(np.float64))
+    got = rs.cpu().numpy()
+    assert np.abs(got[:, 0] / want[:, 0] - 1).max() < 1e-5
+    assert np.abs(got[:, 1] - want[:, 1]).max() < 1e-5 * np.abs(want[:, 1]).max() + 1e-6
+
+
+@pytest.mark.parametrize("b", [1, 3, 64])
+def test_qkv_rope_folded(b):
+    rng = np.random.default_rng(100 + b)
+    r = rows_of(b)
+    x = f16(rng.standard_normal((r, 384)) * 2 + rng.standard_normal((r, 1)))
+    g = rng.standard_normal(384) * 0.3 + 1
+    be = rng.standard_normal(384) * 0.1
+    w = f16(rng.standard_normal((1152, 384)) / np.sqrt(384))
+    bias = rng.standard_normal(1152) * 0.1
+    bias[384:768] = 0
+    ref = rope_ref(ln64(x, g, be) @ w.T + bias.astype(np.float32), r)
+    wf, cs = fold(w, bias, g, be)
+    cos, sin = ref_numpy.rope_tables()
+    out = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
+    plain = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
+    check_rc(lib().dv3k_qkv_rope_folded(ptr(t16(x)), r, ptr(t16(wf)), ptr(t32(cs)),
+                                        ptr(t32(rowstat_of(x))), ptr(t32(cos)), ptr(t32(sin)),
+                                        ptr(out), ptr(status()), stream()))
+    check_rc(lib().dv3k_qkv_rope(ptr(t16(ln64(x, g, be))), r, ptr(t16(w)), ptr(t32(bias)),
+                                 ptr(t32(cos)), ptr(t32(sin)), ptr(plain), ptr(status()), stream()))
+    torch.cuda.synchronize()
+    assert_as_accurate(out, plain, ref)
+
+
+@pytest.mark.parametrize("b", [1, 3, 50, 64])
+def test_matmul_swiglu_folded(b):
+    rng = np.random.default_rng(110 + b)
+    r = rows_of(b)
+    x = f16(rng.standard_normal((r, 384)) * 2 + rng.standard_normal((r, 1)))
+    gam = rng.standard_normal(384) * 0.3 + 1
+    be = rng.standard_normal(384) * 0.1
+    wg = f16(rng.standard_normal((1536, 384)) / np.sqrt(384) * 2)
+    wu = f16(rng.standard_normal((1536, 384)) / np.sqrt(384))
+    bg = rng.standard_normal(1536) * 0.1
+    bu = rng.standard_normal(1536) * 0.1
+    h = ln64(x, gam, be)
+    gv = h @ wg.T + bg.astype(np.float32)
+    uv = h @ wu.T + bu.astype(np.float32)
+    ref = gv / (1 + np.exp(-gv)) * uv
+    src = np.array([lib().dv3k_gateup_source_row(i) for i in range(3072)])
+    w_packed, b_packed = np.concatenate([wg, wu])[src], np.concatenate([bg, bu])[src]
+    wf, cs = fold(w_packed, b_packed, gam, be)
+    act = torch.empty((r, 1536), dtype=torch.float16, device=DEV)
+    plain = torch.empty((r, 1536), dtype=torch.float16, device=DEV)
+    check_rc(lib().dv3k_matmul_swiglu_folded(ptr(t16(x)), r, ptr(t16(wf)), ptr(t32(cs)),
+                                             ptr(t32(rowstat_of(x))), ptr(act), ptr(status()),
+                                             stream()))
+    check_rc(lib().dv3k_matmul_swiglu(ptr(t16(h)), r, ptr(t16(w_packed)), ptr(t32(b_packed)),
+                                      ptr(plain), ptr(status()), stream()))
+    torch.cuda.synchronize()
+    assert_as_accurate(act, plain, ref)
+
+
 def test_bounded_wait_expires_and_context_survives():
     """The failure path every kernel uses, made to run out on the device without a fault: a wait
     on an mbarrier that nothing arrives at expires after its limit and records its bit, the

@@ -322,7 +322,8 @@ def test_profile_forward_in_plan_order(models):
     model.forward(images)  # stages the input
     prof = model.profile_forward(64, 3, 256 << 20)
     assert len(prof) == model.launches_per_forward(64)
-    assert [n for n, _ in prof][:3] == ["patchify", "gemm_patch_embed", "layernorm_f16"]
+    # batch 64 folds the first LayerNorm into the QKV GEMM: only its row statistics
+    assert [n for n, _ in prof][:3] == ["patchify", "gemm_patch_embed", "layernorm_rowstat"]
     gemms = [ms for n, ms in prof if n.startswith("gemm_gateup")]
     assert len(gemms) == 12 and all(ms > 0.005 for ms in gemms)
     total = sum(ms for _, ms in prof)
@@ -406,22 +407,38 @@ def test_benchmark_and_profile(models):
 
 def test_fused_layernorm_plan(weights_file, monkeypatch):
     """Large batches ride each LayerNorm after the first in the preceding residual GEMM
-    (3 + 12*5 launches); small ones keep separate LayerNorm launches (3 + 12*7, the reference's
-    plan). At 16 images the default is the split plan; DV3_FUSE_LAYERNORM=1 (read when a batch
-    size's graph is built) forces fusion, which gives the same result within f16 rounding."""
+    (3 + 12*5 launches) and fold all but the final one further into the QKV and gate/up GEMMs
+    (the residual GEMM leaves only the row statistics); small ones keep separate LayerNorm
+    launches (3 + 12*7, the reference's plan). At 16 images the default is the split plan;
+    DV3_FUSE_LAYERNORM=1 (read when a batch size's graph is built) forces fusion and folding,
+    DV3_FOLD_LAYERNORM=0 keeps the fused LayerNorms unfolded. All three give the same result
+    within f16 rounding."""
     path = weights_file(1, "stress")
     images = synth.images(31, 16)
     with dv.DINOv3.load(path, dv.Options(0, 16)) as model:
         assert model.launches_per_forward(16) == 3 + 12 * 7
         split = model.forward(images)
     monkeypatch.setenv("DV3_FUSE_LAYERNORM", "1")
+    monkeypatch.setenv("DV3_FOLD_LAYERNORM", "0")
     with dv.DINOv3.load(path, dv.Options(0, 16)) as model:
         assert model.launches_per_forward(16) == 3 + 12 * 5
         fused = model.forward(images)
-        prof = model.profile_launches(16, 1)
-    assert [n for n, _ in prof].count("gemm_down_resid_layernorm") == 12
+        names = [n for n, _ in model.profile_launches(16, 1)]
+    assert names.count("gemm_down_resid_layernorm") == 12
+    assert names.count("gemm_o_resid_layernorm") == 12 and names[2] == "layernorm_f16"
+    monkeypatch.delenv("DV3_FOLD_LAYERNORM")
+    with dv.DINOv3.load(path, dv.Options(0, 16)) as model:
+        assert model.launches_per_forward(16) == 3 + 12 * 5
+        folded = model.forward(images)
+        names = [n for n, _ in model.profile_launches(16, 1)]
+    assert names[2] == "layernorm_rowstat"
+    assert names.count("gemm_qkv_rope_folded") == names.count("gemm_o_resid_rowstat") == 12
+    assert names.count("gemm_gateup_swiglu_folded") == 12
+    assert names.count("gemm_down_resid_rowstat") == 11  # the final LayerNorm is not folded
+    assert names[-1] == "gemm_down_resid_layernorm"
     for i in range(16):
         assert cos(fused[i], split[i]) > 0.99999
+        assert cos(folded[i], split[i]) > 0.99999
 
 
 def test_split_k_plan(weights_file, monkeypatch):
