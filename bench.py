@@ -75,26 +75,26 @@ def kernel_work(name: str, b: int = BATCH, last: bool = False):
         return 2.0 * p * 768 * d, (p * 768 + d * 768 + p * d) * f16 + d * f32
     if name in ("layernorm_f16", "layernorm_f32out"):
         return 0.0, r * d * f16 + r * d * (f32 if name == "layernorm_f32out" else f16) + 2 * d * f32
-    if name == "layernorm_rowstat":  # folded LayerNorm: (rstd, -mean rstd) per row
-        return 0.0, r * d * f16 + r * 2 * f32
+    if name == "layernorm_rowstat":  # folded LayerNorm: (rstd, -mean rstd) and aux row per row
+        return 0.0, r * d * f16 + r * (2 * f32 + 16 * f16)
     if name in ("gemm_qkv_rope", "gemm_qkv_rope_folded"):
-        fold = (r * 2 + 1152) * f32 if name.endswith("folded") else 0
+        fold = r * 2 * f32 + (r + 1152) * 16 * f16 if name.endswith("folded") else 0
         return 2.0 * r * d * 1152, ((r * d + 1152 * d + r * 1152) * f16 + (1152 + 2 * 196 * 64) * f32
                                     + fold)
     if name == "attention":
         return 4.0 * 201 * 201 * 64 * 6 * b, (r * 1152 + r * d) * f16
     if name in ("gemm_o_resid", "gemm_o_resid_layernorm", "gemm_o_resid_rowstat"):
         ln = name.endswith("layernorm")
-        stats = r * 2 * f32 if name.endswith("rowstat") else 0
+        stats = r * (2 * f32 + 16 * f16) if name.endswith("rowstat") else 0
         return 2.0 * r * d * d, ((r * d + d * d + 2 * r * d + (r * d if ln else 0)) * f16
                                  + 4 * d * f32 + stats)
     if name in ("gemm_gateup_swiglu", "gemm_gateup_swiglu_folded"):
-        fold = (r * 2 + 3072) * f32 if name.endswith("folded") else 0
+        fold = r * 2 * f32 + (r + 3072) * 16 * f16 if name.endswith("folded") else 0
         return 2.0 * r * d * 3072, (r * d + 3072 * d + r * 1536) * f16 + 3072 * f32 + fold
     if name in ("gemm_down_resid", "gemm_down_resid_layernorm", "gemm_down_resid_rowstat"):
         ln = name.endswith("layernorm")
         out = (r * d * (f32 if last else f16)) if ln else 0
-        stats = r * 2 * f32 if name.endswith("rowstat") else 0
+        stats = r * (2 * f32 + 16 * f16) if name.endswith("rowstat") else 0
         return 2.0 * r * 1536 * d, (r * 1536 + d * 1536 + 2 * r * d) * f16 + out + 4 * d * f32 + stats
     return 0.0, 0.0
 
@@ -741,33 +741,38 @@ def run_ops(args):
         lambda o, s: lib.dv3k_matmul_swiglu(ptr(o[0]), r, ptr(w["gateup"]), ptr(v["bias"]),
                                             ptr(o[1]), ptr(st), s),
         *kernel_work("gemm_gateup_swiglu"), r * (d + 1536) * f16b))
-    # the folded-LayerNorm forms the plan uses at this batch size: the residual GEMMs leave
-    # (rstd, -mean rstd) per row, QKV and gate/up read x and take (c, s) per output column
-    cs = {"qkv": vec(2 * 1152, -1, 1), "gateup": vec(2 * 3072, -1, 1)}
-    stats = lambda: torch.stack([vec(r, 0.5, 1.5), vec(r)], 1).contiguous()  # noqa: E731
+    # the folded-LayerNorm forms the plan uses at this batch size: the residual GEMMs leave the
+    # row statistics (rstd, -mean rstd) and an f16 aux row; QKV and gate/up read x and add the
+    # rank-2 correction in one more K=16 step from the weight aux rows
+    waux = {"qkv": randn((1152, 16), 0.1), "gateup": randn((3072, 16), 0.1)}
+    stats = lambda: (torch.stack([vec(r, 0.5, 1.5), vec(r)], 1).contiguous(),  # noqa: E731
+                     randn((r, 16), 0.1))
     results.append(time_op(
-        "layernorm_rowstat", lambda: (randn((r, d)), empty((r, 2), torch.float32)),
-        lambda o, s: lib.dv3k_layernorm_rowstat(ptr(o[0]), r, ptr(o[1]), s),
-        *kernel_work("layernorm_rowstat"), r * d * f16b + r * 2 * f32b))
+        "layernorm_rowstat",
+        lambda: (randn((r, d)), empty((r, 2), torch.float32), empty((r, 16))),
+        lambda o, s: lib.dv3k_layernorm_rowstat(ptr(o[0]), r, ptr(o[1]), ptr(o[2]), s),
+        *kernel_work("layernorm_rowstat"), r * d * f16b + r * (2 * f32b + 16 * f16b)))
     results.append(time_op(
-        "gemm_qkv_rope_folded", lambda: (randn((r, d)), stats(), empty((r, 1152))),
-        lambda o, s: lib.dv3k_qkv_rope_folded(ptr(o[0]), r, ptr(w["qkv"]), ptr(cs["qkv"]), ptr(o[1]),
-                                              ptr(v["cos"]), ptr(v["sin"]), ptr(o[2]), ptr(st), s),
-        *kernel_work("gemm_qkv_rope_folded"), r * (d + 1152) * f16b + r * 2 * f32b))
+        "gemm_qkv_rope_folded", lambda: (randn((r, d)), *stats(), empty((r, 1152))),
+        lambda o, s: lib.dv3k_qkv_rope_folded(ptr(o[0]), r, ptr(w["qkv"]), ptr(waux["qkv"]),
+                                              ptr(o[1]), ptr(o[2]), ptr(v["cos"]), ptr(v["sin"]),
+                                              ptr(o[3]), ptr(st), s),
+        *kernel_work("gemm_qkv_rope_folded"), r * (d + 1152 + 16) * f16b + r * 2 * f32b))
     for k, wname in ((384, "o"), (1536, "down")):
         name = ("gemm_o_resid" if k == 384 else "gemm_down_resid") + "_rowstat"
         results.append(time_op(
-            name, lambda k=k: (randn((r, k)), randn((r, d)), empty((r, 2), torch.float32)),
+            name, lambda k=k: (randn((r, k)), randn((r, d)), empty((r, 2), torch.float32),
+                               empty((r, 16))),
             lambda o, s, k=k, wname=wname: lib.dv3k_matmul_resid_rowstat(
                 ptr(o[0]), r, k, ptr(w[wname]), ptr(v["bias"]), ptr(v["lam"]), ptr(o[1]),
-                ptr(o[2]), ptr(st), s),
-            *kernel_work(name), r * (k + d) * f16b + r * 2 * f32b))
+                ptr(o[2]), ptr(o[3]), ptr(st), s),
+            *kernel_work(name), r * (k + d + 16) * f16b + r * 2 * f32b))
     results.append(time_op(
-        "gemm_gateup_swiglu_folded", lambda: (randn((r, d)), stats(), empty((r, 1536))),
+        "gemm_gateup_swiglu_folded", lambda: (randn((r, d)), *stats(), empty((r, 1536))),
         lambda o, s: lib.dv3k_matmul_swiglu_folded(ptr(o[0]), r, ptr(w["gateup"]),
-                                                   ptr(cs["gateup"]), ptr(o[1]), ptr(o[2]),
-                                                   ptr(st), s),
-        *kernel_work("gemm_gateup_swiglu_folded"), r * (d + 1536) * f16b + r * 2 * f32b))
+                                                   ptr(waux["gateup"]), ptr(o[1]), ptr(o[2]),
+                                                   ptr(o[3]), ptr(st), s),
+        *kernel_work("gemm_gateup_swiglu_folded"), r * (d + 1536 + 16) * f16b + r * 2 * f32b))
 
     def splitk_pair(o, s, splits=2):
         rc = lib.dv3k_matmul_splitk(ptr(o[0]), r, ptr(w["down"]), splits, ptr(o[2]), ptr(st), s)

@@ -223,7 +223,8 @@ int current_device() {
 }
 
 int gemm_entry(dv3::GemmOp op, const void *a, uint32_t rows, const void *w,
-               const dv3::GemmArgs &args, uint32_t *status, void *stream) {
+               const dv3::GemmArgs &args, uint32_t *status, void *stream,
+               const void *w_aux = nullptr) {
   if (rows == 0) return DV3_OK;
   dv3::GemmMaps maps;
   std::string err;
@@ -232,6 +233,8 @@ int gemm_entry(dv3::GemmOp op, const void *a, uint32_t rows, const void *w,
                                        : static_cast<const void *>(args.ln_out);
   if (!dv3::make_gemm_maps(op, a, rows, w, args.out, &maps, &err, ln ? ln_out : nullptr,
                            args.ln_out_f32 != nullptr))
+    return bad_args(err.c_str());
+  if (w_aux && !dv3::make_fold_maps(op, args.row_aux, rows, w_aux, &maps, &err))
     return bad_args(err.c_str());
   return launch_status(dv3::launch_gemm(op, maps, rows, args, status, static_cast<cudaStream_t>(stream)),
                        dv3::gemm_name(op));
@@ -429,11 +432,11 @@ int dv3k_matmul_swiglu(const uint16_t *h, uint32_t rows, const uint16_t *gateup_
 
 int dv3k_matmul_resid_rowstat(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
                               const float *bias, const float *lambda, uint16_t *x, float *rowstat,
-                              uint32_t *status, void *stream) {
-  if (!all_aligned(a, w, bias, lambda, x, rowstat))
+                              uint16_t *row_aux, uint32_t *status, void *stream) {
+  if (!all_aligned(a, w, bias, lambda, x, rowstat, row_aux))
     return bad_args("pointers must be 16-byte aligned");
   if (k != 384 && k != 1536) return bad_args("k must be 384 or 1536");
-  if (rowstat == nullptr) return bad_args("rowstat is required");
+  if (rowstat == nullptr || row_aux == nullptr) return bad_args("rowstat and row_aux are required");
   if (rows > 128u * static_cast<uint32_t>(dv3::sm_count(current_device())))
     return bad_args("rows must fit one 128-row tile per SM");
   dv3::GemmArgs g;
@@ -441,45 +444,52 @@ int dv3k_matmul_resid_rowstat(const uint16_t *a, uint32_t rows, uint32_t k, cons
   g.lambda = lambda;
   g.out = reinterpret_cast<__half *>(x);
   g.rowstat = reinterpret_cast<float2 *>(rowstat);
+  g.row_aux = reinterpret_cast<__half *>(row_aux);
   return gemm_entry(k == 384 ? dv3::GemmOp::ResidStats384 : dv3::GemmOp::ResidStats1536, a, rows,
                     w, g, status, stream);
 }
 
-int dv3k_layernorm_rowstat(const uint16_t *x, uint32_t rows, float *rowstat, void *stream) {
-  if (!all_aligned(x, rowstat)) return bad_args("pointers must be 16-byte aligned");
-  if (rowstat == nullptr) return bad_args("rowstat is required");
+int dv3k_layernorm_rowstat(const uint16_t *x, uint32_t rows, float *rowstat, uint16_t *row_aux,
+                           void *stream) {
+  if (!all_aligned(x, rowstat, row_aux)) return bad_args("pointers must be 16-byte aligned");
+  if (rowstat == nullptr || row_aux == nullptr) return bad_args("rowstat and row_aux are required");
   return launch_status(dv3::launch_layernorm_rowstat(reinterpret_cast<const __half *>(x), rows,
                                                      reinterpret_cast<float2 *>(rowstat),
+                                                     reinterpret_cast<__half *>(row_aux),
                                                      static_cast<cudaStream_t>(stream)),
                        "layernorm_rowstat");
 }
 
-int dv3k_qkv_rope_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf, const float *cs,
-                         const float *rowstat, const float *rope_cos, const float *rope_sin,
-                         uint16_t *qkv, uint32_t *status, void *stream) {
-  if (!all_aligned(x, wf, cs, rowstat, rope_cos, rope_sin, qkv))
+int dv3k_qkv_rope_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf,
+                         const uint16_t *w_aux, const float *rowstat, const uint16_t *row_aux,
+                         const float *rope_cos, const float *rope_sin, uint16_t *qkv,
+                         uint32_t *status, void *stream) {
+  if (!all_aligned(x, wf, w_aux, rowstat, row_aux, rope_cos, rope_sin, qkv))
     return bad_args("pointers must be 16-byte aligned");
-  if (cs == nullptr || rowstat == nullptr) return bad_args("cs and rowstat are required");
+  if (w_aux == nullptr || rowstat == nullptr || row_aux == nullptr)
+    return bad_args("w_aux, rowstat and row_aux are required");
   dv3::GemmArgs g;
-  g.fold_cs = cs;
   g.rowstat = reinterpret_cast<float2 *>(const_cast<float *>(rowstat));
+  g.row_aux = reinterpret_cast<__half *>(const_cast<uint16_t *>(row_aux));
   g.rope_cos = rope_cos;
   g.rope_sin = rope_sin;
   g.out = reinterpret_cast<__half *>(qkv);
-  return gemm_entry(dv3::GemmOp::QkvRopeFold, x, rows, wf, g, status, stream);
+  return gemm_entry(dv3::GemmOp::QkvRopeFold, x, rows, wf, g, status, stream, w_aux);
 }
 
 int dv3k_matmul_swiglu_folded(const uint16_t *x, uint32_t rows, const uint16_t *gateup_wf,
-                              const float *cs, const float *rowstat, uint16_t *act,
-                              uint32_t *status, void *stream) {
-  if (!all_aligned(x, gateup_wf, cs, rowstat, act))
+                              const uint16_t *w_aux, const float *rowstat,
+                              const uint16_t *row_aux, uint16_t *act, uint32_t *status,
+                              void *stream) {
+  if (!all_aligned(x, gateup_wf, w_aux, rowstat, row_aux, act))
     return bad_args("pointers must be 16-byte aligned");
-  if (cs == nullptr || rowstat == nullptr) return bad_args("cs and rowstat are required");
+  if (w_aux == nullptr || rowstat == nullptr || row_aux == nullptr)
+    return bad_args("w_aux, rowstat and row_aux are required");
   dv3::GemmArgs g;
-  g.fold_cs = cs;
   g.rowstat = reinterpret_cast<float2 *>(const_cast<float *>(rowstat));
+  g.row_aux = reinterpret_cast<__half *>(const_cast<uint16_t *>(row_aux));
   g.out = reinterpret_cast<__half *>(act);
-  return gemm_entry(dv3::GemmOp::SwiGLUFold, x, rows, gateup_wf, g, status, stream);
+  return gemm_entry(dv3::GemmOp::SwiGLUFold, x, rows, gateup_wf, g, status, stream, w_aux);
 }
 
 uint32_t dv3k_gateup_source_row(uint32_t packed_row) { return dv3::gateup_source_row(packed_row); }

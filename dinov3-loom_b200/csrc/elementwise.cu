@@ -152,9 +152,11 @@ __global__ void __launch_bounds__(256)
 }
 
 // The statistics of the LayerNorm only (folded LayerNorm, GemmOp::QkvRopeFold): rowstat[r] =
-// (rstd, -mean rstd) of row r, computed as layernorm_kernel computes them. One row per warp.
+// (rstd, -mean rstd) and the aux row (store_row_aux) of row r, computed as layernorm_kernel
+// computes them. One row per warp.
 __global__ void __launch_bounds__(256)
-    layernorm_rowstat_kernel(const __half *__restrict__ x, int rows, float2 *__restrict__ rowstat) {
+    layernorm_rowstat_kernel(const __half *__restrict__ x, int rows, float2 *__restrict__ rowstat,
+                             __half *__restrict__ row_aux) {
   pdl_wait();  // the rows written by the previous kernel are complete from here on
   pdl_trigger();
   const int row = blockIdx.x * 8 + threadIdx.x / 32;
@@ -183,13 +185,14 @@ __global__ void __launch_bounds__(256)
   }
   const float rstd = rsqrtf(warp_sum(d) * (1.0f / kHidden) + 1e-5f);
   if (lane == 0) rowstat[row] = make_float2(rstd, -mean * rstd);
+  if (lane == 1) store_row_aux(row_aux + static_cast<size_t>(row) * 16, mean, rstd);
 }
 
 cudaError_t launch_layernorm_rowstat(const __half *x, uint32_t rows, float2 *rowstat,
-                                     cudaStream_t stream) {
+                                     __half *row_aux, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
   return launch_pdl(layernorm_rowstat_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, x,
-                    static_cast<int>(rows), rowstat);
+                    static_cast<int>(rows), rowstat, row_aux);
 }
 
 cudaError_t launch_patchify(const float *images, uint32_t n_images, const float *prefix,

@@ -121,6 +121,18 @@ struct EpiWarpStaging<Epi, decltype(void(Epi::kWarpStaging))> {
   static constexpr int value = Epi::kWarpStaging;
 };
 
+// Whether the GEMM runs one more K=16 step per unit after its k-blocks (Epi::kAuxK, the folded
+// LayerNorm): A from the row aux [rows][16] (map tmD) and B from the weight aux [n][16] (map
+// tmE), 32-byte rows with the 32-byte swizzle, loaded into the next stage buffer of the ring.
+template <class Epi, class = void>
+struct AuxK {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct AuxK<Epi, decltype(void(Epi::kAuxK))> {
+  static constexpr bool value = Epi::kAuxK;
+};
+
 template <int BN, class Epi>
 struct GemmCfg {
   static constexpr int kSplit = BN > 256 ? 2 : 1;    // MMAs per K step
@@ -140,6 +152,8 @@ struct GemmCfg {
   static constexpr bool kInput = TmaInput<Epi>::value;
   static constexpr bool kEarly = EarlyInput<Epi>::value;
   static constexpr bool kBiasInit = BiasInTmem<Epi>::value;
+  static constexpr bool kAux = AuxK<Epi>::value;
+  static constexpr int kAuxA = BM * 32;  // bytes of the aux A tile (128 rows x 16 f16)
   // configurations whose launches have exactly one tile per CTA
   static constexpr bool kOneTile = kInTiles || kBiasInit;
   static_assert(!kBiasInit || BN == 384, "bias fill: one full-row tile per CTA");
@@ -227,7 +241,8 @@ template <int BN, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
-                int M, TileSched sched, int k_blocks, Epi epi, uint32_t *status) {
+                const __grid_constant__ CUtensorMap tmE, int M, TileSched sched, int k_blocks,
+                Epi epi, uint32_t *status) {
   using C = GemmCfg<BN, Epi>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -269,7 +284,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
     if (Epi::kTmaStore) tma_prefetch_map(&tmC);
-    if (std::is_same<Epi, EpiResidLN>::value) tma_prefetch_map(&tmD);
+    if (std::is_same<Epi, EpiResidLN>::value || C::kAux) tma_prefetch_map(&tmD);
+    if (C::kAux) tma_prefetch_map(&tmE);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -350,6 +366,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             phase ^= 1u;
           }
         }
+        if constexpr (C::kAux) {
+          // the extra K=16 step: the unit's 128 aux rows (A) and its columns' aux rows (B)
+          if (ok && !mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            report(status, kErrProducerWait);
+            *abort_flag = 1;
+            ok = false;
+          }
+          if (ok) {
+            uint8_t *a = tiles + stage * C::kStage;
+            mbar_arrive_expect_tx(&full[stage], C::kAuxA + b_boxes * C::kBBox * 32);
+            tma_load_2d(a, &tmD, &full[stage], 0, m0);
+            for (int s = 0; s < b_boxes; ++s)
+              tma_load_2d(a + C::kA + s * C::kBBox * 32, &tmE, &full[stage], 0,
+                          n0 + s * C::kBBox);
+            armed |= 1u << stage;
+            last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == C::kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
         if constexpr (C::kEarly) {
           // The epilogue's x blocks go into the stages of the last-but-two and last-but-one
           // k-blocks (one tile per CTA) once their MMAs have completed: epilogue warps 0..kEarlyA-1
@@ -427,6 +465,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
+          }
+        }
+        if constexpr (C::kAux) {  // the extra K=16 step (see the producer)
+          if (ok && !mbar_wait(&full[stage], phase, abort_flag)) {
+            report(status, kErrMmaWait);
+            *abort_flag = 1;
+            ok = false;
+          }
+          if (ok) {
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(tiles + stage * C::kStage);
+            umma_f16(d, sw32_desc(a_addr), sw32_desc(a_addr + C::kA), idesc, 1u);
+            umma_commit(&empty[stage]);
+            if (++stage == C::kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
         if (!ok) break;
@@ -668,7 +723,8 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
   const uint32_t b_rows = s.bn >= 256 || narrow_ops ? s.bn / 2 : s.bn;
   if (!encode_map_f16(&maps->b, w, s.k, s.n, BK, b_rows, err)) return false;
   if (!encode_map_f16(&maps->a, a, s.k, rows, BK, BM, err)) return false;
-  maps->d = maps->a;  // unused unless the epilogue writes a LayerNorm output
+  maps->d = maps->a;  // unused unless the epilogue writes a LayerNorm output (or the fold's aux)
+  maps->e = maps->a;  // unused unless the fold's aux
   if (op == GemmOp::SplitK1536)  // f32 partial slabs [splits][rows][384], 32x32 blocks
     return encode_map_f32_slabs(&maps->c, out, kHidden, rows, splits, 32, err);
   const uint32_t c_cols = tma_store_cols(op);
@@ -692,6 +748,19 @@ bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void
                   : encode_map_f16_swizzled(&maps->d, ln_out, kHidden, rows, 64, 32, 128, err);
   }
   return true;
+}
+
+bool make_fold_maps(GemmOp op, const void *row_aux, uint32_t rows, const void *w_aux,
+                    GemmMaps *maps, std::string *err) {
+  if (op != GemmOp::QkvRopeFold && op != GemmOp::SwiGLUFold) {
+    if (err) *err = "no folded LayerNorm in this GEMM";
+    return false;
+  }
+  const GemmShape s = gemm_shape(op, rows);
+  // 16-column boxes: 128 rows of the unit (A), and the weight boxes' rows (B: BN/2 rows, two per
+  // full tile and one per narrow unit, as for the weights)
+  return encode_map_f16_swizzled(&maps->d, row_aux, 16, rows, 16, BM, 32, err) &&
+         encode_map_f16_swizzled(&maps->e, w_aux, 16, s.n, 16, s.bn / 2, 32, err);
 }
 
 template <int BN, class Epi>
@@ -749,7 +818,7 @@ static cudaError_t launch_one(const GemmMaps &maps, uint32_t rows, int n, int k,
   discard_range(args.discard, args.discard_bytes, &sched.discard, &sched.discard_bytes);
   const int grid = sched.num_units < sm_count(dev) ? sched.num_units : sm_count(dev);
   return launch_pdl(gemm_kernel<BN, Epi>, dim3(grid), dim3(kGemmThreads),
-                    gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d,
+                    gemm_smem_bytes<BN, Epi>(), stream, maps.a, maps.b, maps.c, maps.d, maps.e,
                     static_cast<int>(rows), sched, k / BK / k_splits, epi, status);
 }
 
@@ -801,21 +870,20 @@ cudaError_t launch_gemm(GemmOp op, const GemmMaps &maps, uint32_t rows, const Ge
                              status, stream, args);
     case GemmOp::ResidStats384:
     case GemmOp::ResidStats1536:
-      if (args.rowstat == nullptr) return cudaErrorInvalidValue;
+      if (args.rowstat == nullptr || args.row_aux == nullptr) return cudaErrorInvalidValue;
       return launch_one<384>(maps, rows, s.n, s.k,
                              EpiResidLN{args.bias, args.lambda, nullptr, nullptr, false,
-                                        args.rowstat},
+                                        args.rowstat, args.row_aux},
                              status, stream, args);
     case GemmOp::QkvRopeFold:
-      if (args.rowstat == nullptr || args.fold_cs == nullptr) return cudaErrorInvalidValue;
+      if (args.rowstat == nullptr) return cudaErrorInvalidValue;
       return launch_one<256>(maps, rows, s.n, s.k,
-                             EpiQkvRopeFold{args.fold_cs, args.rope_cos, args.rope_sin,
-                                            args.rowstat},
+                             EpiQkvRopeFold{nullptr, args.rope_cos, args.rope_sin, args.rowstat},
                              status, stream, args);
     case GemmOp::SwiGLUFold:
-      if (args.rowstat == nullptr || args.fold_cs == nullptr) return cudaErrorInvalidValue;
-      return launch_one<256>(maps, rows, s.n, s.k, EpiSwiGLUFold{args.fold_cs, args.rowstat},
-                             status, stream, args);
+      if (args.rowstat == nullptr) return cudaErrorInvalidValue;
+      return launch_one<256>(maps, rows, s.n, s.k, EpiSwiGLUFold{nullptr, args.rowstat}, status,
+                             stream, args);
     case GemmOp::SplitK1536:
       if (args.splits == 0 || (kMlp / BK) % args.splits != 0) return cudaErrorInvalidValue;
       return launch_one<128>(maps, rows, s.n, s.k, EpiPartialF32{}, status, stream, args,

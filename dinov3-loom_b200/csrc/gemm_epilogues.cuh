@@ -101,36 +101,6 @@ __device__ __forceinline__ void ldg32(const float *s, float (&v)[32]) {
   }
 }
 
-// The folded LayerNorm's output for 32 consecutive columns of one row, y = a acc + (c + b s)
-// with a = rstd and b = -mean rstd of the row, in two steps so that the accumulator's TMEM load
-// can be in flight during the first: fold_cs32 forms c + b s from the per-column terms, stored by
-// column pairs (c[2j], c[2j+1], s[2j], s[2j+1]) and read 16 bytes at a time from global memory
-// through L1 (a broadcast, like ldg32) or from shared memory; fold_acc32 adds a acc (raw f32
-// bits from TMEM).
-template <bool kShared>
-__device__ __forceinline__ void fold_cs32(const float *cs, float b, float (&v)[32]) {
-  const float4 *p = reinterpret_cast<const float4 *>(cs);
-  const float2 b2 = make_float2(b, b);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float4 q = kShared ? p[j] : __ldg(p + j);
-    const float2 t = __ffma2_rn(b2, make_float2(q.z, q.w), make_float2(q.x, q.y));
-    v[2 * j] = t.x;
-    v[2 * j + 1] = t.y;
-  }
-}
-
-__device__ __forceinline__ void fold_acc32(float a, const uint32_t (&acc)[32], float (&v)[32]) {
-  const float2 a2 = make_float2(a, a);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float2 t = __ffma2_rn(a2, make_float2(u2f(acc[2 * j]), u2f(acc[2 * j + 1])),
-                                make_float2(v[2 * j], v[2 * j + 1]));
-    v[2 * j] = t.x;
-    v[2 * j + 1] = t.y;
-  }
-}
-
 __device__ __forceinline__ void ldg_half32(const __half *src, uint4 (&q)[4]) {
   const uint4 *p = reinterpret_cast<const uint4 *>(src);
 #pragma unroll
@@ -243,38 +213,34 @@ struct EpiPatch {
 // the packed [196][64] table (rows padded to 17 floats so the 32 rows of a warp fall in distinct
 // banks); the packed entries for channels c and c+32 are equal. Columns >= 1152 (the zero-filled
 // tail of the last 256-wide tile) are neither computed nor stored.
-// Folded form (kFold): A is x instead of LN(x), and the projection before RoPE is
-// rstd acc - mean rstd s + c, from the row's (rstd, -mean rstd) and the folded vectors.
+// Folded form (kFold): A is x instead of LN(x) and the kernel's extra K=16 step adds the row's
+// -mean s + c / rstd (weights.cpp), so the projection before RoPE is rstd acc.
 // ---------------------------------------------------------------------------------------------
 template <bool kFold>
 struct EpiQkvRopeT {
-  // kFold (the LayerNorm before the projection folded in, GemmOp::QkvRopeFold): the pairs (c, s)
-  // of each output column, c = b + W beta, s = the row sum of W'
-  const float *bias;
+  const float *bias;  // unused when kFold (the bias is in the weight aux)
   const float *cosv;
   const float *sinv;
   const float2 *rowstat = nullptr;  // kFold: each row's (rstd, -mean rstd)
   static constexpr int kPad = 17;
   static constexpr int kTab = 14 * kPad;                   // floats per (axis, function)
   static constexpr int kRopeBytes = ((4 * kTab * 4 + 15) / 16) * 16;
-  static constexpr int kSmem = kRopeBytes + (kFold ? 2 : 1) * kQkv * 4;  // + bias, or (c, s)
+  static constexpr int kSmem = kRopeBytes + (kFold ? 0 : kQkv * 4);  // + bias
   static constexpr bool kTmaStore = true;
   // One staging block per warp: the 16 KB saved let a fourth 48 KB mainloop stage fit beside
   // the RoPE tables and the bias. Measured no faster: the two 16-column halves of that block
   // used in turn (twice the TMA store instructions delayed the producer's loads), and the
   // second head's accumulator loaded from TMEM during the first head's stores.
   static constexpr int kStagingBufs = 1;
+  static constexpr bool kAuxK = kFold;  // one more K=16 step: the aux rows (gemm_kernel)
   struct Pre {
-    float a, b;  // kFold: this row's rstd and -mean rstd
+    float a;  // kFold: this row's rstd
   };
   __device__ Pre prefetch(int, const EpiCtx &c) const {
     if constexpr (kFold) {
-      if (c.row < c.M) {
-        const float2 v = __ldg(rowstat + c.row);
-        return {v.x, v.y};
-      }
+      if (c.row < c.M) return {__ldg(&rowstat[c.row].x)};
     }
-    return {1.f, 0.f};
+    return {1.f};
   }
   __device__ void init(uint8_t *smem, int tid, int n) const {
     float *t = reinterpret_cast<float *>(smem);
@@ -284,8 +250,7 @@ struct EpiQkvRopeT {
       const int src = (which < 2) ? (pos * 14) * 64 + j : pos * 64 + 16 + j;
       t[which * kTab + pos * kPad + j] = __ldg(((which & 1) ? sinv : cosv) + src);
     }
-    stage_floats(reinterpret_cast<float *>(smem + kRopeBytes), bias, (kFold ? 2 : 1) * kQkv, tid,
-                 n);
+    if constexpr (!kFold) stage_floats(reinterpret_cast<float *>(smem + kRopeBytes), bias, kQkv, tid, n);
   }
   template <int COLS>
   __device__ void run(uint32_t taddr, int n0, EpiCtx &c, Pre &pre) const {
@@ -304,16 +269,14 @@ struct EpiQkvRopeT {
       const int col = n0 + h;  // first column of this 64-wide head
       if (col >= kQkv) break;  // warp-uniform
       float lo[32], hi[32];
-      if constexpr (kFold) {
+      if constexpr (kFold) {  // the accumulator holds (LN(x) W^T + b) / rstd
         uint32_t ra[32], rb[32];
-        tmem_ld32(taddr + h, ra);  // in flight while c + b s is formed
-        tmem_ld32(taddr + h + 32, rb);
-        fold_cs32<true>(sb + 2 * col, pre.b, lo);
-        fold_cs32<true>(sb + 2 * (col + 32), pre.b, hi);
-        tmem_wait_ld(ra);
-        tmem_regs_ready(rb);
-        fold_acc32(pre.a, ra, lo);
-        fold_acc32(pre.a, rb, hi);
+        tmem_load32x2(taddr + h, ra, taddr + h + 32, rb);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          lo[i] = pre.a * u2f(ra[i]);
+          hi[i] = pre.a * u2f(rb[i]);
+        }
       } else {
         uint32_t ra[32], rb[32];
         tmem_load32x2(taddr + h, ra, taddr + h + 32, rb);
@@ -536,32 +499,26 @@ struct EpiResidWide {
 // ---------------------------------------------------------------------------------------------
 // Gate/up with SwiGLU: the weight rows are packed 64 gate rows, the matching 64 up rows, ...;
 // act[row][j] = f16(silu(g + bg) (u + bu)), silu through the hardware tanh (one MUFU op).
-// Folded form (kFold): A is x instead of LN(x), g = rstd acc_g - mean rstd s_g + c_g (and u the
-// same), from the row's (rstd, -mean rstd) and the folded vectors.
+// Folded form (kFold): A is x instead of LN(x) and the kernel's extra K=16 step adds the row's
+// -mean s + c / rstd (weights.cpp), so g = rstd acc_g and u = rstd acc_u.
 // ---------------------------------------------------------------------------------------------
 template <bool kFold>
 struct EpiSwiGLUT {
-  // packed like the weight rows; kFold (the LayerNorm before the projection folded in,
-  // GemmOp::SwiGLUFold): the pairs (c, s) of each output column, c = b + W beta, s = the row sum
-  // of W'
-  const float *bias;
+  const float *bias;  // packed like the weight rows (unused when kFold: it is in the weight aux)
   const float2 *rowstat = nullptr;  // kFold: each row's (rstd, -mean rstd)
-  // The vectors are read through L1 (every lane of a warp reads the same 32 floats) rather than
-  // staged in shared memory: without them four 48 KB stages fit beside the TMA-store staging
-  // (three with).
+  // The bias is read through L1 (every lane of a warp reads the same 32 floats) rather than staged
+  // in shared memory: without it four 48 KB stages fit beside the TMA-store staging (three with).
   static constexpr int kSmem = 0;
   static constexpr bool kTmaStore = true;
+  static constexpr bool kAuxK = kFold;  // one more K=16 step: the aux rows (gemm_kernel)
   struct Pre {
-    float a, b;  // kFold: this row's rstd and -mean rstd
+    float a;  // kFold: this row's rstd
   };
   __device__ Pre prefetch(int, const EpiCtx &c) const {
     if constexpr (kFold) {
-      if (c.row < c.M) {
-        const float2 v = __ldg(rowstat + c.row);
-        return {v.x, v.y};
-      }
+      if (c.row < c.M) return {__ldg(&rowstat[c.row].x)};
     }
-    return {1.f, 0.f};
+    return {1.f};
   }
   __device__ void init(uint8_t *, int, int) const {}
   template <int COLS>
@@ -575,22 +532,15 @@ struct EpiSwiGLUT {
     for (int g = 0; g < g1; g += 128) {
 #pragma unroll 1
       for (int sub = s0; sub < s1; sub += 32) {
-        float gv[32], uv[32];
-        if constexpr (kFold) {
-          uint32_t rg[32], ru[32];
-          tmem_ld32(taddr + g + sub, rg);  // in flight while c + b s is formed
-          tmem_ld32(taddr + g + 64 + sub, ru);
-          fold_cs32<false>(sb + 2 * (n0 + g + sub), pre.b, gv);
-          fold_cs32<false>(sb + 2 * (n0 + g + 64 + sub), pre.b, uv);
-          tmem_wait_ld(rg);
-          tmem_regs_ready(ru);
-          fold_acc32(pre.a, rg, gv);
-          fold_acc32(pre.a, ru, uv);
+        uint32_t rg[32], ru[32];
+        tmem_load32x2(taddr + g + sub, rg, taddr + g + 64 + sub, ru);
+        float gv[32];
+        if constexpr (kFold) {  // the accumulator holds (LN(x) W^T + b) / rstd
 #pragma unroll
-          for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i]) * uv[i];
+          for (int i = 0; i < 32; ++i)
+            gv[i] = silu(pre.a * u2f(rg[i])) * (pre.a * u2f(ru[i]));
         } else {
-          uint32_t rg[32], ru[32];
-          tmem_load32x2(taddr + g + sub, rg, taddr + g + 64 + sub, ru);
+          float uv[32];
           ldg32(sb + n0 + g + sub, gv);
           ldg32(sb + n0 + g + 64 + sub, uv);
 #pragma unroll
@@ -623,7 +573,7 @@ using EpiSwiGLUFold = EpiSwiGLUT<true>;
 // the staging region once the x stores have read it: three f16 blocks, or (f32 output) two
 // rounds of three 32-row x 32-column f32 blocks. With `rowstat` set (GemmOp::ResidStats*, the
 // LayerNorm folded into the next GEMM) the epilogue stops after the statistics and leaves
-// (rstd, -mean rstd) of each row instead of normalising it.
+// (rstd, -mean rstd) and the aux row of each row instead of normalising it.
 // ---------------------------------------------------------------------------------------------
 struct EpiResidLN {
   const float *bias;
@@ -632,8 +582,10 @@ struct EpiResidLN {
   const float *beta;
   bool f32_out;
   // GemmOp::ResidStats*: the LayerNorm is folded into the next GEMM, so instead of normalising
-  // the row this epilogue leaves rowstat[row] = (rstd, -mean rstd) (gamma and beta unused).
+  // the row this epilogue leaves rowstat[row] = (rstd, -mean rstd) and the row's aux row
+  // (store_row_aux) in row_aux [rows][16] (gamma and beta unused).
   float2 *rowstat = nullptr;
+  __half *row_aux = nullptr;
   static constexpr int kVecs = 4 * kHidden;  // bias, lambda, gamma, beta
   static constexpr int kSmem = kVecs * 4 + 4 * 128 * 4;  // + [mean|M2][2 halves][128 rows]
   static constexpr bool kTmaStore = true;
@@ -764,7 +716,10 @@ struct EpiResidLN {
     m2 = red[256 + c.r] + red[384 + c.r] + d * d * (kHidden / 4);
     const float rstd = rsqrtf(m2 * (1.0f / kHidden) + 1e-5f);
     if (rowstat) {  // folded LayerNorm: the consumer normalises
-      if (c.half == 0 && c.row < c.M) rowstat[c.row] = make_float2(rstd, -mean * rstd);
+      if (c.row < c.M) {
+        if (c.half == 0) rowstat[c.row] = make_float2(rstd, -mean * rstd);
+        else store_row_aux(row_aux + static_cast<size_t>(c.row) * 16, mean, rstd);
+      }
       return;
     }
     // h = (x rstd - mean rstd) gamma + beta, staged where the x blocks were. Each output block

@@ -53,10 +53,12 @@ bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uin
 // the f32 partial product of its slice (no bias) into slab s of partials [splits][rows][384]
 // (kernels/matmul_splitk_f16_wmma.loom); splitk_reduce completes it.
 // Folded LayerNorm (no counterpart in the reference; the weights in weights.cpp): ResidStats*
-// update x like ResidLN* but leave only rowstat[row] = (rstd, -mean rstd) of the updated row;
-// QkvRopeFold and SwiGLUFold then read x itself and apply the LayerNorm in their epilogues,
-// acc' = x W'^T, y = rstd acc' - mean rstd s + c (W' = f16(W gamma), s its row sums,
-// c = b + W beta), before RoPE or SwiGLU.
+// update x like ResidLN* but leave only the statistics of the updated row, rowstat[row] =
+// (rstd, -mean rstd) and the f16 aux row (-mean_hi, -mean_lo, -mean_hi, r_hi, r_lo, r_hi,
+// 0...) with r = 1 / rstd; QkvRopeFold and SwiGLUFold then read x itself with W' = f16(W gamma),
+// run one more K=16 MMA step of the aux row against W_aux = (s_hi, s_hi, s_lo, c_hi, c_hi, c_lo,
+// 0...) per output column (s the row sums of W', c = b + W beta), so that the accumulator holds
+// x W'^T - mean s + r c, and scale it by rstd in their epilogues before RoPE or SwiGLU.
 enum class GemmOp {
   Patch,
   QkvRope,
@@ -90,7 +92,9 @@ struct GemmMaps {
   CUtensorMap a;
   CUtensorMap b;
   CUtensorMap c;  // the epilogue's output, for epilogues that store through TMA
-  CUtensorMap d;  // ResidLN*: the LayerNorm output (f16 h, or the f32 final output)
+  CUtensorMap d;  // ResidLN*: the LayerNorm output (f16 h, or the f32 final output);
+                  // QkvRopeFold / SwiGLUFold: the row aux [rows][16]
+  CUtensorMap e;  // QkvRopeFold / SwiGLUFold: the weight aux [n][16]
 };
 // `out` is the tensor the epilogue writes (qkv, act or x; unused by Patch, which writes x through
 // GemmArgs). ResidLN* also takes the LayerNorm output: `ln_out` f16 [rows][384], or f32 when
@@ -99,6 +103,10 @@ struct GemmMaps {
 bool make_gemm_maps(GemmOp op, const void *a, uint32_t rows, const void *w, void *out,
                     GemmMaps *maps, std::string *err, const void *ln_out = nullptr,
                     bool ln_f32 = false, uint32_t splits = 1);
+// QkvRopeFold / SwiGLUFold: the maps of the extra K step, the row aux [rows][16] and the weight
+// aux [n][16] (f16, 16-column boxes with the 32-byte swizzle), after make_gemm_maps.
+bool make_fold_maps(GemmOp op, const void *row_aux, uint32_t rows, const void *w_aux,
+                    GemmMaps *maps, std::string *err);
 
 struct GemmArgs {
   const float *bias = nullptr;
@@ -112,10 +120,11 @@ struct GemmArgs {
   float *ln_out_f32 = nullptr;   //           f32 LayerNorm output when non-null
   float *partials = nullptr;     // SplitK1536: [splits][rows][384] f32
   uint32_t splits = 1;           // SplitK1536: K slices (a divisor of 24, the 64-wide k-blocks)
-  // Folded LayerNorm: ResidStats* write and QkvRopeFold / SwiGLUFold read (rstd, -mean rstd)
-  // per row; the folded GEMMs take (c, s) per output column in `fold_cs` (`bias` unused).
+  // Folded LayerNorm: ResidStats* write, and QkvRopeFold / SwiGLUFold read, rowstat (rstd,
+  // -mean rstd) and the row aux [rows][16] f16 of each row (`bias` unused by the folded GEMMs,
+  // whose bias is in the weight aux of their maps).
   float2 *rowstat = nullptr;
-  const float *fold_cs = nullptr;
+  __half *row_aux = nullptr;
   // Weights of a later kernel (16-byte aligned; no kernel writes them) that this launch starts
   // toward L2, so that kernel's first tiles do not wait for DRAM.
   const void *l2_next = nullptr;
@@ -179,10 +188,10 @@ cudaError_t launch_layernorm_f16(const __half *x, uint32_t rows, const float *ga
                                  const float *beta, __half *out, cudaStream_t stream);
 cudaError_t launch_layernorm_f32(const __half *x, uint32_t rows, const float *gamma,
                                  const float *beta, float *out, cudaStream_t stream);
-// The statistics of the LayerNorm only: rowstat[r] = (rstd, -mean rstd) of row r of x (the
-// folded LayerNorm of the QKV GEMM after the patch embedding).
+// The statistics of the LayerNorm only: rowstat[r] = (rstd, -mean rstd) and the aux row of row
+// r of x (GemmOp::ResidStats*; the folded LayerNorm of the QKV GEMM after the patch embedding).
 cudaError_t launch_layernorm_rowstat(const __half *x, uint32_t rows, float2 *rowstat,
-                                     cudaStream_t stream);
+                                     __half *row_aux, cudaStream_t stream);
 
 // Split-K completion (kernels/splitk_reduce_f16.loom): x[r][n] = f16(x + lambda[n] (sum over
 // s = 0..splits-1 in that order of partials[s][r][n] + b[n])), one warp per row. With gamma and

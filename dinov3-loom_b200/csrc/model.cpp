@@ -14,8 +14,9 @@
 //   out     f32 [201B][384]        final LayerNorm output
 //   status  u32 [2]                device failure bits, non-finite input flag (sticky until read)
 //   pmean   f32 [B][384]           patch-token means (patch_mean readout)
-//   rowstat f32 [201B][2]          (rstd, -mean rstd) of each token row: the LayerNorm that the
-//                                  QKV and gate/up GEMMs apply themselves (folded plan)
+//   rowstat f32 [201B][2]          (rstd, -mean rstd) of each token row, and
+//   row_aux f16 [201B][16]         its aux row: the LayerNorm that the QKV and gate/up GEMMs
+//                                  apply themselves (folded plan)
 //   image1, out1                   the second serving slot's input and output (slot 0 uses
 //                                  image and out)
 // The QKV buffer needs no headroom rows: attention reads through TMA, whose out-of-bounds rows
@@ -133,8 +134,8 @@ Model::Model(const std::string &path, dv3_options options)
       l.ls2 = fp(s + "ls2");
       l.qkv_wf = hp(s + "qkv_wf");
       l.gateup_wf = hp(s + "gateup_wf");
-      l.qkv_cs = fp(s + "qkv_cs");
-      l.gateup_cs = fp(s + "gateup_cs");
+      l.qkv_aux = hp(s + "qkv_aux");
+      l.gateup_aux = hp(s + "gateup_aux");
     }
 
     // Activations for max_batch images.
@@ -145,13 +146,13 @@ Model::Model(const std::string &path, dv3_options options)
       const uint32_t r = static_cast<uint32_t>(kTokens * b);
       partial_floats = std::max(partial_floats, static_cast<size_t>(splitk_splits(r)) * r * kHidden);
     }
-    const size_t sizes[14] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
+    const size_t sizes[15] = {B * kImageElements * 4, P * kPatchK * 2, R * kHidden * 2,
                               R * kHidden * 2,        R * kQkv * 2,    R * kHidden * 2,
                               R * kMlp * 2,           R * kHidden * 4, 256,
                               B * kHidden * 4,        B * kImageElements * 4, R * kHidden * 4,
-                              partial_floats * 4,     R * 8};
-    size_t at[14], act_total = 0;
-    for (int i = 0; i < 14; ++i) {
+                              partial_floats * 4,     R * 8,           R * 32};
+    size_t at[15], act_total = 0;
+    for (int i = 0; i < 15; ++i) {
       at[i] = act_total;
       act_total += align256(sizes[i]);
     }
@@ -160,6 +161,7 @@ Model::Model(const std::string &path, dv3_options options)
     image_ = reinterpret_cast<float *>(a + at[0]);
     partials_ = reinterpret_cast<float *>(a + at[12]);
     rowstat_ = reinterpret_cast<float2 *>(a + at[13]);
+    row_aux_ = reinterpret_cast<__half *>(a + at[14]);
     patches_ = reinterpret_cast<__half *>(a + at[1]);
     x_ = reinterpret_cast<__half *>(a + at[2]);
     h_ = reinterpret_cast<__half *>(a + at[3]);
@@ -286,6 +288,7 @@ Plan &Model::prepare(size_t b, int slot) {
   float *image = image_slot_[slot], *out = out_slot_[slot];
   __half *x = x_, *h = h_, *qkv = qkv_, *attn = attn_, *act = act_, *patches = patches_;
   float2 *rowstat = rowstat_;
+  __half *row_aux = row_aux_;
   const int fold_mask = fold_layernorm(b);
   const bool fold = fold_mask & 1, fold2 = (fold_mask & 2) != 0;  // LN1 into QKV, LN2 into gate/up
 
@@ -308,7 +311,7 @@ Plan &Model::prepare(size_t b, int slot) {
   });
   if (fold)
     add("layernorm_rowstat", [=](cudaStream_t s) {
-      return launch_layernorm_rowstat(x, r, rowstat, s);
+      return launch_layernorm_rowstat(x, r, rowstat, row_aux, s);
     });
   else
     add("layernorm_f16", [=](cudaStream_t s) {
@@ -338,9 +341,11 @@ Plan &Model::prepare(size_t b, int slot) {
     const GemmOp o_op_l = fold2 ? GemmOp::ResidStats384 : o_op;
     const GemmOp down_op_l = fold && i < 11 ? GemmOp::ResidStats1536 : down_op;
     need(make_gemm_maps(qkv_op, fold ? x : h, r, fold ? l.qkv_wf : l.qkv_w, qkv, &qkv_maps, &err));
+    if (fold) need(make_fold_maps(qkv_op, row_aux, r, l.qkv_aux, &qkv_maps, &err));
     need(make_gemm_maps(o_op_l, attn, r, l.o_w, x, &o_maps, &err, h));
     need(make_gemm_maps(gu_op, fold2 ? x : h, r, fold2 ? l.gateup_wf : l.gateup_w, act, &gu_maps,
                         &err));
+    if (fold2) need(make_fold_maps(gu_op, row_aux, r, l.gateup_aux, &gu_maps, &err));
     if (splits > 1)
       need(make_gemm_maps(GemmOp::SplitK1536, act, r, l.down_w, partials, &down_maps, &err,
                           nullptr, false, splits));
@@ -351,7 +356,6 @@ Plan &Model::prepare(size_t b, int slot) {
     add(gemm_name(qkv_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.qkv_b;
-      g.fold_cs = l.qkv_cs;
       g.rowstat = rowstat;
       g.rope_cos = w.rope_cos;
       g.rope_sin = w.rope_sin;
@@ -377,6 +381,7 @@ Plan &Model::prepare(size_t b, int slot) {
       g.beta = l.norm2_b;
       g.ln_out = h;
       g.rowstat = rowstat;
+      g.row_aux = row_aux;
       g.l2_next = l.down_w;
       g.l2_next_bytes = kDownWBytes;
       g.discard = qkv;  // the attention's input
@@ -390,7 +395,6 @@ Plan &Model::prepare(size_t b, int slot) {
     add(gemm_name(gu_op), [=](cudaStream_t s) {
       GemmArgs g;
       g.bias = l.gateup_b;
-      g.fold_cs = l.gateup_cs;
       g.rowstat = rowstat;
       g.out = act;
       g.discard = attn;  // the o-projection's input
@@ -429,6 +433,7 @@ Plan &Model::prepare(size_t b, int slot) {
       g.ln_out = last ? nullptr : h;
       g.ln_out_f32 = last ? out : nullptr;
       g.rowstat = rowstat;
+      g.row_aux = row_aux;
       return launch_gemm(down_op_l, down_maps, r, g, st, s);
     });
     if (!fuse) {

@@ -26,9 +26,8 @@ struct LayerWeights {
   const float *qkv_b, *gateup_b, *o_b, *down_b;
   const float *norm1_w, *norm1_b, *norm2_w, *norm2_b, *ls1, *ls2;
   // The QKV and gate/up projections with the LayerNorm before them folded in (weights.cpp):
-  // W' = f16(W gamma), and per output column the pair (c, s): c = b + W beta, s = row sum of W'.
-  const __half *qkv_wf, *gateup_wf;
-  const float *qkv_cs, *gateup_cs;
+  // W' = f16(W gamma) and the weight aux rows of the extra K=16 step.
+  const __half *qkv_wf, *gateup_wf, *qkv_aux, *gateup_aux;
 };
 
 struct DeviceWeights {
@@ -116,6 +115,7 @@ class Model {
   float *image_ = nullptr, *out_ = nullptr, *pmean_ = nullptr;
   float *partials_ = nullptr;  // split-K partial slabs of the down projection
   float2 *rowstat_ = nullptr;  // per token row (rstd, -mean rstd) of the folded LayerNorm
+  __half *row_aux_ = nullptr;  // per token row: its aux row of the folded LayerNorm [201B][16]
   float *image_slot_[2] = {}, *out_slot_[2] = {};  // slot 0 aliases image_ / out_
   // Per slot: upload done, forward done (input consumed, output ready), download done.
   cudaEvent_t ev_in_[2] = {}, ev_done_[2] = {}, ev_out_[2] = {};

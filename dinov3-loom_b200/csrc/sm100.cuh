@@ -390,6 +390,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
          (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// The same for a K-major tile of 32-byte rows (16 f16 columns, one MMA's K) stored with the
+// 32-byte swizzle (the layout TMA writes for a 16-column box with CU_TENSOR_MAP_SWIZZLE_32B):
+// 8-row groups 256 bytes apart, 256-byte aligned groups, layout type 6 = 32-byte swizzle.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t smem_addr) {
+  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) |
+         (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46) | (6ull << 61);
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16 with f16 A and B and an f32 accumulator:
 // D format f32 (1) at [4,6), A/B format f16 (0) at [7,10) / [10,13), A major [15], B major [16]
 // (0 = K-major, 1 = MN-major), N >> 3 at [17,23), M >> 4 at [24,29).
@@ -423,6 +431,24 @@ __device__ __forceinline__ float tanh_approx(float x) {
 __device__ __forceinline__ float silu(float a) {
   const float h = 0.5f * a;
   return fmaf(h, tanh_approx(h), h);
+}
+
+// The folded LayerNorm's aux row of a token row with statistics (mean, rstd): 16 f16 values
+// (-mean_hi, -mean_lo, -mean_hi, r_hi, r_lo, r_hi, 0, ...) with r = 1 / rstd, each *_lo the f16
+// of what the f16 *_hi leaves over; the tensor cores multiply it with the weight aux (s_hi,
+// s_hi, s_lo, c_hi, c_hi, c_lo, 0, ...) into -mean s + r c. 32 bytes at dst (16-byte aligned).
+__device__ __forceinline__ void store_row_aux(__half *dst, float mean, float rstd) {
+  const float r = 1.0f / rstd;
+  const __half mh = __float2half_rn(-mean), rh = __float2half_rn(r);
+  const __half ml = __float2half_rn(-mean - __half2float(mh));
+  const __half rl = __float2half_rn(r - __half2float(rh));
+  auto pk = [](__half a, __half b) {
+    return static_cast<uint32_t>(__half_as_ushort(a)) |
+           (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+  };
+  uint4 *d = reinterpret_cast<uint4 *>(dst);
+  d[0] = make_uint4(pk(mh, ml), pk(mh, rh), pk(rl, rh), 0u);
+  d[1] = make_uint4(0u, 0u, 0u, 0u);
 }
 
 __device__ __forceinline__ float2 unpack_half2(uint32_t v) {

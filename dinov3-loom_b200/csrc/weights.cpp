@@ -412,19 +412,23 @@ std::map<std::string, Packed> load_weights(const std::string &path) {
   }
   // LayerNorm folded into the GEMM that consumes it (no counterpart in the reference). With
   // h = (x - mu) rstd gamma + beta and W the packed f16 weights,
-  //   h W^T + b = rstd (x W'^T) - mu rstd s + c,  W' = f16(W gamma),  s[n] = sum_k W'[n][k],
+  //   h W^T + b = rstd (x W'^T - mu s + c / rstd),  W' = f16(W gamma),  s[n] = sum_k W'[n][k],
   //   c[n] = b[n] + sum_k W[n][k] beta[k],
-  // so the kernel that updates x leaves only (rstd, -mu rstd) per row and the QKV and gate/up
-  // GEMMs read x itself. s sums the rounded W', so rstd (x W'^T - mu s) = rstd ((x - mu) W'^T)
-  // up to the f32 accumulation. c and s are stored by column pairs, (c[2j], c[2j+1], s[2j],
-  // s[2j+1]), so one 16-byte load gives a kernel both terms of two columns. Emitted after every
-  // reference tensor, so the reference's first error is still the one reported.
+  // so the kernel that updates x leaves only the row's statistics and the QKV and gate/up GEMMs
+  // read x itself. The correction -mu s + c / rstd is a rank-2 product that the tensor cores add
+  // as one more K=16 step: the row side holds (-mu_hi, -mu_lo, -mu_hi, r_hi, r_lo, r_hi, 0...)
+  // with r = 1 / rstd, and W_aux[n] = (s_hi, s_hi, s_lo, c_hi, c_hi, c_lo, 0...), each value
+  // split into an f16 and the f16 of its remainder, so the products sum to -mu s + r c up to
+  // 2^-22 of their size. s sums the rounded W', so rstd (x W'^T - mu s) = rstd ((x - mu) W'^T)
+  // up to the f32 accumulation. Emitted after every reference tensor, so the reference's first
+  // error is still the one reported.
   auto fold = [&](const std::string &s, const std::string &mat, const std::string &norm) {
     const Packed &w = out.at(s + mat + "_w");
     const Packed &b = out.at(s + mat + "_b");
     const std::vector<float> &g = out.at(s + norm + "_w").f, &be = out.at(s + norm + "_b").f;
     const size_t n = b.f.size();
-    std::vector<float> wf(w.h.size()), cv(n);
+    std::vector<float> wf(w.h.size());
+    std::vector<double> cv(n);
     for (size_t r = 0; r < n; ++r) {
       double c = b.f[r];
       for (size_t k = 0; k < H; ++k) {
@@ -432,18 +436,25 @@ std::map<std::string, Packed> load_weights(const std::string &path) {
         wf[r * H + k] = v * g[k];
         c += static_cast<double>(v) * be[k];
       }
-      cv[r] = static_cast<float>(c);
+      cv[r] = c;
     }
     emit(s + mat + "_wf", wf, true);
     const std::vector<uint16_t> &packed = out.at(s + mat + "_wf").h;
-    std::vector<float> cs(2 * n);  // per column pair: c[2j], c[2j+1], s[2j], s[2j+1]
+    auto hi = [](double v) { return f16_to_f32(f32_to_f16(static_cast<float>(v))); };
+    std::vector<float> aux(16 * n, 0.0f);
     for (size_t r = 0; r < n; ++r) {
-      double acc = 0.0;
-      for (size_t k = 0; k < H; ++k) acc += f16_to_f32(packed[r * H + k]);
-      cs[4 * (r / 2) + r % 2] = cv[r];
-      cs[4 * (r / 2) + 2 + r % 2] = static_cast<float>(acc);
+      double sum = 0.0;
+      for (size_t k = 0; k < H; ++k) sum += f16_to_f32(packed[r * H + k]);
+      const float sh = hi(sum), ch = hi(cv[r]);
+      float *a = &aux[16 * r];
+      a[0] = sh;
+      a[1] = sh;
+      a[2] = static_cast<float>(sum - sh);
+      a[3] = ch;
+      a[4] = ch;
+      a[5] = static_cast<float>(cv[r] - ch);
     }
-    emit(s + mat + "_cs", cs, false);
+    emit(s + mat + "_aux", aux, true);
   };
   for (int i = 0; i < 12; ++i) {
     const std::string s = "l" + std::to_string(i) + "_";

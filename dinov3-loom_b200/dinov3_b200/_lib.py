@@ -89,10 +89,10 @@ SIGNATURES = {
     "dv3k_splitk_reduce": ([_P, _U32, _U32, _P, _P, _P, _P], _I),
     "dv3k_splitk_reduce_layernorm": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_down_splitk_noalloc": ([_P, _U32, _P, _U32, _P, _P, _P, _P, _P], _I),
-    "dv3k_matmul_resid_rowstat": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P], _I),
-    "dv3k_layernorm_rowstat": ([_P, _U32, _P, _P], _I),
-    "dv3k_qkv_rope_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P, _P], _I),
-    "dv3k_matmul_swiglu_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P], _I),
+    "dv3k_matmul_resid_rowstat": ([_P, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "dv3k_layernorm_rowstat": ([_P, _U32, _P, _P, _P], _I),
+    "dv3k_qkv_rope_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "dv3k_matmul_swiglu_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_gateup_source_row": ([_U32], _U32),
     "dv3k_bounded_wait_selftest": ([ctypes.c_uint64, _P, _P], _I),
 }

@@ -108,37 +108,43 @@ int dv3k_matmul_resid_layernorm(const uint16_t *a, uint32_t rows, uint32_t k, co
 
 /* Folded LayerNorm (no counterpart in the reference, which normalises each row into h and
  * then multiplies): for a GEMM that consumes h = LN(x) gamma + beta with f16 weights W and bias
- * b, h W^T + b = rstd (x W'^T) - mean rstd s + c with W' = f16(W gamma), s[n] = sum_k W'[n][k]
- * and c = b + W beta. So the kernel that updates x leaves only rowstat[row] = (rstd,
- * -mean rstd) (two floats per row), and the consumer reads x itself. The model folds the
+ * b, h W^T + b = rstd (x W'^T - mean s + r c) with W' = f16(W gamma), s[n] = sum_k W'[n][k],
+ * c = b + W beta and r = 1 / rstd. The correction -mean s + r c is a rank-2 product that the
+ * tensor cores add as one more K=16 step: the kernel that updates x leaves, per row, rowstat =
+ * (rstd, -mean rstd) (f32 [rows][2]) and the row aux (f16 [rows][16]: -mean_hi, -mean_lo,
+ * -mean_hi, r_hi, r_lo, r_hi, then zeros, each *_lo the f16 of what the f16 *_hi leaves over),
+ * and the consumer reads x itself with w_aux (f16 [n][16] per output column: s_hi, s_hi, s_lo,
+ * c_hi, c_hi, c_lo, then zeros) and scales its accumulator by rstd. The model folds the
  * LayerNorms before the QKV and gate/up projections this way whenever the residual GEMMs run on
- * full rows; the final LayerNorm is not folded.
+ * full rows; the final LayerNorm is not folded. The model's loader derives wf and w_aux from the
+ * checkpoint.
  *
  * dv3k_matmul_resid_rowstat: dv3k_matmul_resid_layernorm without the normalised output: x is
- * updated the same way and rowstat[row] gets the LayerNorm statistics of the f16-rounded row
- * (eps 1e-5). k is 384 or 1536. */
+ * updated the same way, and rowstat and row_aux get the LayerNorm statistics of the f16-rounded
+ * row (eps 1e-5). k is 384 or 1536. */
 int dv3k_matmul_resid_rowstat(const uint16_t *a, uint32_t rows, uint32_t k, const uint16_t *w,
                               const float *bias, const float *lambda, uint16_t *x, float *rowstat,
-                              uint32_t *status, void *stream);
+                              uint16_t *row_aux, uint32_t *status, void *stream);
 
-/* rowstat[row] = (rstd, -mean rstd) of row `row` of x [rows][384] f16 (eps 1e-5), as
- * dv3k_layernorm_f16 computes them (the folded LayerNorm of the first QKV projection). */
-int dv3k_layernorm_rowstat(const uint16_t *x, uint32_t rows, float *rowstat, void *stream);
+/* rowstat and row_aux of each row of x [rows][384] f16 (eps 1e-5), the statistics
+ * dv3k_layernorm_f16 computes (the folded LayerNorm of the first QKV projection). */
+int dv3k_layernorm_rowstat(const uint16_t *x, uint32_t rows, float *rowstat, uint16_t *row_aux,
+                           void *stream);
 
-/* dv3k_qkv_rope on x instead of h = LN(x): qkv = rope(rstd (x wf^T) - mean rstd s + c), wf =
- * f16(qkv_w gamma1) [1152][384]; cs [2304] f32 holds c and s by output column pairs, c[2j],
- * c[2j+1], s[2j], s[2j+1] at cs[4j..4j+3]; rowstat from dv3k_matmul_resid_rowstat or
- * dv3k_layernorm_rowstat. */
-int dv3k_qkv_rope_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf, const float *cs,
-                         const float *rowstat, const float *rope_cos, const float *rope_sin,
-                         uint16_t *qkv, uint32_t *status, void *stream);
+/* dv3k_qkv_rope on x instead of h = LN(x): qkv = rope(rstd (x wf^T - mean s + r c)), wf =
+ * f16(qkv_w gamma1) [1152][384], w_aux [1152][16] and rowstat, row_aux as above. */
+int dv3k_qkv_rope_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf,
+                         const uint16_t *w_aux, const float *rowstat, const uint16_t *row_aux,
+                         const float *rope_cos, const float *rope_sin, uint16_t *qkv,
+                         uint32_t *status, void *stream);
 
-/* dv3k_matmul_swiglu on x instead of h = LN(x): g and u = rstd (x wf^T) - mean rstd s + c, act =
- * f16(silu(g) u), with gateup_wf = f16(gateup_w gamma2) in the packed row order and cs [6144]
- * the c and s of the packed columns by pairs, as for dv3k_qkv_rope_folded. */
+/* dv3k_matmul_swiglu on x instead of h = LN(x): g and u = rstd (x wf^T - mean s + r c), act =
+ * f16(silu(g) u), with gateup_wf = f16(gateup_w gamma2) and w_aux [3072][16] in the packed row
+ * order. */
 int dv3k_matmul_swiglu_folded(const uint16_t *x, uint32_t rows, const uint16_t *gateup_wf,
-                              const float *cs, const float *rowstat, uint16_t *act,
-                              uint32_t *status, void *stream);
+                              const uint16_t *w_aux, const float *rowstat,
+                              const uint16_t *row_aux, uint16_t *act, uint32_t *status,
+                              void *stream);
 
 /* Down projection split over K (kernels/matmul_splitk_f16_wmma.loom, launched at batch 1 by
  * src/lib.rs:218-224 with the specialisation of :297): for each slice s < splits of the 1536-long

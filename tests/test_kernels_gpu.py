@@ -360,34 +360,68 @@ def test_matmul_swiglu(b):
 
 
 # Folded LayerNorm (no counterpart in the reference): the residual GEMM leaves (rstd, -mean rstd)
-# per row and the QKV and gate/up GEMMs read x with W' = f16(W gamma), s = row sums of W',
-# c = b + W beta (weights.cpp). References: the unrounded float64 LayerNorm of x, then the op;
-# the folded kernels are held to the accuracy of the unfolded kernels on h = f16(LN(x)).
+# and an f16 aux row (-mean_hi, -mean_lo, -mean_hi, r_hi, r_lo, r_hi, 0...) per row, r = 1/rstd;
+# the QKV and gate/up GEMMs read x with W' = f16(W gamma) and a weight aux row (s_hi, s_hi, s_lo,
+# c_hi, c_hi, c_lo, 0...) per output column (s = row sums of W', c = b + W beta; weights.cpp),
+# which one more K=16 tensor-core step multiplies into -mean s + r c. References: the unrounded
+# float64 LayerNorm of x, then the op; the folded kernels are held to the accuracy of the
+# unfolded kernels on h = f16(LN(x)).
 def ln_stats(x):
     mean = x.mean(axis=1)
     var = ((x - mean[:, None]) ** 2).mean(axis=1)
     rstd = 1.0 / np.sqrt(var + 1e-5)
-    return rstd, -mean * rstd
+    return mean, rstd
+
+
+def split16(v):
+    """v as an f16 and the f16 of what it leaves over (hi + lo, 2^-22 of |v|)."""
+    hi = np.asarray(v, np.float32).astype(np.float16)
+    return hi, (np.asarray(v, np.float64) - hi.astype(np.float64)).astype(np.float16)
 
 
 def fold(w, b, g, be):
     """The folded weights of weights.cpp from f16 weights w [n][384], bias b, LayerNorm g, be:
-    wf = f16(w g), and c and s by output column pairs (c[2j], c[2j+1], s[2j], s[2j+1])."""
+    wf = f16(w g) and the weight aux rows [n][16]."""
     g32, be32 = g.astype(np.float32), be.astype(np.float32)
     wf = (w.astype(np.float32) * g32).astype(np.float16)
     s = wf.astype(np.float64).sum(axis=1)
     c = b.astype(np.float32).astype(np.float64) + w @ be32.astype(np.float64)
-    return wf, np.stack([c.reshape(-1, 2), s.reshape(-1, 2)], axis=1).ravel()
+    aux = np.zeros((len(s), 16), np.float16)
+    aux[:, 0], aux[:, 2] = split16(s)
+    aux[:, 1] = aux[:, 0]
+    aux[:, 3], aux[:, 5] = split16(c)
+    aux[:, 4] = aux[:, 3]
+    return wf, aux
 
 
 def ln64(x, g, be):
-    rstd, nm = ln_stats(x)
-    return (x * rstd[:, None] + nm[:, None]) * g.astype(np.float32) + be.astype(np.float32)
+    mean, rstd = ln_stats(x)
+    return (x - mean[:, None]) * rstd[:, None] * g.astype(np.float32) + be.astype(np.float32)
 
 
 def rowstat_of(x):
-    rstd, nm = ln_stats(x)
-    return np.stack([rstd, nm], axis=1).astype(np.float32)
+    """(rstd, -mean rstd) f32 and the f16 aux rows, as the producers write them."""
+    mean, rstd = ln_stats(x)
+    rstd32 = rstd.astype(np.float32)
+    st = np.stack([rstd32, (-mean * rstd).astype(np.float32)], axis=1)
+    aux = np.zeros((len(mean), 16), np.float16)
+    aux[:, 0], aux[:, 1] = split16(-mean)
+    aux[:, 2] = aux[:, 0]
+    aux[:, 3], aux[:, 4] = split16(np.float32(1) / rstd32)
+    aux[:, 5] = aux[:, 3]
+    return st, aux
+
+
+def check_stats(st, aux, x):
+    """Producer outputs against the float64 statistics of x."""
+    mean, rstd = ln_stats(x)
+    st, aux = st.cpu().numpy(), aux.cpu().numpy().astype(np.float64)
+    assert np.abs(st[:, 0] / rstd - 1).max() < 1e-5
+    assert np.abs(st[:, 1] + mean * rstd).max() < 1e-5 * np.abs(mean * rstd).max() + 1e-6
+    assert np.abs(aux[:, 0] + aux[:, 1] + mean).max() < 1e-6 * np.abs(mean).max() + 1e-7
+    assert np.abs((aux[:, 3] + aux[:, 4]) * rstd - 1).max() < 1e-5
+    assert np.array_equal(aux[:, 2], aux[:, 0]) and np.array_equal(aux[:, 5], aux[:, 3])
+    assert not aux[:, 6:].any()
 
 
 def scaled_err(got, ref):
@@ -410,20 +444,18 @@ def test_layernorm_rowstat(b):
     rng = np.random.default_rng(80 + b)
     r = rows_of(b)
     x = f16(rng.standard_normal((r, 384)) * 3 + rng.standard_normal((r, 1)))
-    out = torch.empty((r, 2), dtype=torch.float32, device=DEV)
-    check_rc(lib().dv3k_layernorm_rowstat(ptr(t16(x)), r, ptr(out), stream()))
+    st = torch.empty((r, 2), dtype=torch.float32, device=DEV)
+    aux = torch.full((r, 16), 7.0, dtype=torch.float16, device=DEV)
+    check_rc(lib().dv3k_layernorm_rowstat(ptr(t16(x)), r, ptr(st), ptr(aux), stream()))
     torch.cuda.synchronize()
-    want = rowstat_of(x)
-    got = out.cpu().numpy()
-    assert np.abs(got[:, 0] / want[:, 0] - 1).max() < 1e-5
-    assert np.abs(got[:, 1] - want[:, 1]).max() < 1e-5 * np.abs(want[:, 1]).max() + 1e-6
+    check_stats(st, aux, x)
 
 
 @pytest.mark.parametrize("k", [384, 1536])
 @pytest.mark.parametrize("b", [1, 3, 64])
 def test_matmul_resid_rowstat(k, b):
-    """x is updated bit for bit as by dv3k_matmul_resid_layernorm; rowstat holds the statistics
-    of the stored f16 rows."""
+    """x is updated bit for bit as by dv3k_matmul_resid_layernorm; rowstat and the aux rows hold
+    the statistics of the stored f16 rows."""
     rng = np.random.default_rng(90 + b + k)
     r = rows_of(b)
     a = f16(rng.standard_normal((r, k)))
@@ -436,20 +468,18 @@ def test_matmul_resid_rowstat(k, b):
     x_ln, x_st = t16(x0), t16(x0)
     h = torch.empty((r, 384), dtype=torch.float16, device=DEV)
     rs = torch.empty((r, 2), dtype=torch.float32, device=DEV)
+    aux = torch.full((r, 16), 7.0, dtype=torch.float16, device=DEV)
     st = status()
     ad, wd, bd, ld = t16(a), t16(w), t32(bias), t32(lam)
     check_rc(lib().dv3k_matmul_resid_layernorm(ptr(ad), r, k, ptr(wd), ptr(bd), ptr(ld), ptr(x_ln),
                                                ptr(t32(g)), ptr(t32(be)), ptr(h), None, ptr(st),
                                                stream()))
     check_rc(lib().dv3k_matmul_resid_rowstat(ptr(ad), r, k, ptr(wd), ptr(bd), ptr(ld), ptr(x_st),
-                                             ptr(rs), ptr(st), stream()))
+                                             ptr(rs), ptr(aux), ptr(st), stream()))
     torch.cuda.synchronize()
     assert st.cpu().tolist() == [0, 0]
     np.testing.assert_array_equal(x_st.cpu().numpy().view(np.uint16), x_ln.cpu().numpy().view(np.uint16))
-    want = rowstat_of(x_st.float().cpu().numpy().astype(np.float64))
-    got = rs.cpu().numpy()
-    assert np.abs(got[:, 0] / want[:, 0] - 1).max() < 1e-5
-    assert np.abs(got[:, 1] - want[:, 1]).max() < 1e-5 * np.abs(want[:, 1]).max() + 1e-6
+    check_stats(rs, aux, x_st.float().cpu().numpy().astype(np.float64))
 
 
 @pytest.mark.parametrize("b", [1, 3, 64])
@@ -463,13 +493,14 @@ def test_qkv_rope_folded(b):
     bias = rng.standard_normal(1152) * 0.1
     bias[384:768] = 0
     ref = rope_ref(ln64(x, g, be) @ w.T + bias.astype(np.float32), r)
-    wf, cs = fold(w, bias, g, be)
+    wf, waux = fold(w, bias, g, be)
+    rst, raux = rowstat_of(x)
     cos, sin = ref_numpy.rope_tables()
     out = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
     plain = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
-    check_rc(lib().dv3k_qkv_rope_folded(ptr(t16(x)), r, ptr(t16(wf)), ptr(t32(cs)),
-                                        ptr(t32(rowstat_of(x))), ptr(t32(cos)), ptr(t32(sin)),
-                                        ptr(out), ptr(status()), stream()))
+    check_rc(lib().dv3k_qkv_rope_folded(ptr(t16(x)), r, ptr(t16(wf)), ptr(t16(waux)), ptr(t32(rst)),
+                                        ptr(t16(raux)), ptr(t32(cos)), ptr(t32(sin)), ptr(out),
+                                        ptr(status()), stream()))
     check_rc(lib().dv3k_qkv_rope(ptr(t16(ln64(x, g, be))), r, ptr(t16(w)), ptr(t32(bias)),
                                  ptr(t32(cos)), ptr(t32(sin)), ptr(plain), ptr(status()), stream()))
     torch.cuda.synchronize()
@@ -493,11 +524,12 @@ def test_matmul_swiglu_folded(b):
     ref = gv / (1 + np.exp(-gv)) * uv
     src = np.array([lib().dv3k_gateup_source_row(i) for i in range(3072)])
     w_packed, b_packed = np.concatenate([wg, wu])[src], np.concatenate([bg, bu])[src]
-    wf, cs = fold(w_packed, b_packed, gam, be)
+    wf, waux = fold(w_packed, b_packed, gam, be)
+    rst, raux = rowstat_of(x)
     act = torch.empty((r, 1536), dtype=torch.float16, device=DEV)
     plain = torch.empty((r, 1536), dtype=torch.float16, device=DEV)
-    check_rc(lib().dv3k_matmul_swiglu_folded(ptr(t16(x)), r, ptr(t16(wf)), ptr(t32(cs)),
-                                             ptr(t32(rowstat_of(x))), ptr(act), ptr(status()),
+    check_rc(lib().dv3k_matmul_swiglu_folded(ptr(t16(x)), r, ptr(t16(wf)), ptr(t16(waux)),
+                                             ptr(t32(rst)), ptr(t16(raux)), ptr(act), ptr(status()),
                                              stream()))
     check_rc(lib().dv3k_matmul_swiglu(ptr(t16(h)), r, ptr(t16(w_packed)), ptr(t32(b_packed)),
                                       ptr(plain), ptr(status()), stream()))
