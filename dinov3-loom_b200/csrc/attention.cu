@@ -44,20 +44,18 @@
 // abort flag, lets its own copies and MMAs in flight land, frees TMEM and returns.
 #include <atomic>
 
+#include "attention_softmax.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
 
 namespace dv3 {
 
 namespace {
-constexpr int kHeads = 6;
+using namespace attn;
 constexpr int kAttnThreads = 352;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;  // TMEM allocator; issues tile 0's MMAs, warp 10 tile 1's
-constexpr int kValidKeys = kTokens;  // 201
-constexpr int kSKeys = 208;          // S columns computed (201 rounded up to 16)
 constexpr int kKvBox = kSKeys;       // K, V token rows loaded per item
-constexpr int kOutBox = 32;          // token rows per output store (one warp's rows)
 constexpr int kQBytes = 128 * 128;   // 128 rows x 64 f16
 constexpr int kKvBytes = kKvBox * 128;
 // One stage: Q tile 0 | Q tile 1 | K | V, each 1024-byte aligned (8-row swizzle atoms).
@@ -75,97 +73,9 @@ constexpr int kBarOff = kStagingOff + 8 * kStagingBytes;
 // drain[2]; then the TMEM slot and the abort flag.
 constexpr int kAttnSmem = 1024 + kBarOff + 128;
 constexpr int kTmemCols = 512;
-constexpr int kTileCols = 256;  // TMEM columns per query tile
-constexpr int kOCol = 128;      // O_t within the tile's columns
 static_assert(kStageV % 1024 == 0 && kStageBytes % 1024 == 0 && kStagingOff % 1024 == 0,
               "swizzle atoms");
 static_assert(kAttnSmem <= 227 * 1024, "shared memory budget");
-
-constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
-
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// w = 2^(s c - mc) for one pair of keys, summed into `sum`, returned as packed f16.
-__device__ __forceinline__ uint32_t exp_pair(uint32_t s0, uint32_t s1, float mc, float &sum,
-                                             bool v0 = true, bool v1 = true) {
-  const float p0 = v0 ? ex2_approx(fmaf(__uint_as_float(s0), kScaleLog2, -mc)) : 0.f;
-  const float p1 = v1 ? ex2_approx(fmaf(__uint_as_float(s1), kScaleLog2, -mc)) : 0.f;
-  sum += p0 + p1;
-  return pack_half2(p0, p1);
-}
-
-// Softmax of one query row whose S sits in TMEM columns tl..tl+207 (this thread's lane): stores
-// P over columns tl..tl+103 and returns the f32 sum of the weights. Both passes walk S in
-// 32-column chunks and load chunk c+1 while computing on chunk c. Each P store lands on S
-// columns that this thread has already read.
-__device__ __forceinline__ float softmax_row(uint32_t tl) {
-  uint32_t x[32], y[32];
-  float m0 = -INFINITY, m1 = -INFINITY;
-  auto max_chunk = [&](uint32_t (&v)[32], int n) {
-#pragma unroll
-    for (int i = 0; i + 1 < n; i += 4) {
-      m0 = max3(m0, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-      if (i + 3 < n) m1 = max3(m1, __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-      else if (i + 2 < n) m1 = fmaxf(m1, __uint_as_float(v[i + 2]));
-    }
-    if (n % 2) m0 = fmaxf(m0, __uint_as_float(v[n - 1]));
-  };
-  // Pass 1: chunks 0..5 (32 keys each) and keys 192..200 of chunk 6.
-  tmem_load32(tl, x);
-#pragma unroll
-  for (int c = 0; c < 6; c += 2) {
-    tmem_ld32(tl + (c + 1) * 32, y);
-    max_chunk(x, 32);
-    tmem_wait_ld(y);
-    tmem_ld32(tl + (c + 2) * 32, x);  // c + 2 == 6: columns 192..223 (only 192..200 are used)
-    max_chunk(y, 32);
-    tmem_wait_ld(x);
-  }
-  max_chunk(x, kValidKeys - 192);
-  const float mc = fmaxf(m0, m1) * kScaleLog2;
-
-  // Pass 2: keys 32c .. 32c+31 -> P columns 16c .. 16c+15.
-  float sum = 0.f;
-  auto exp_chunk = [&](uint32_t (&v)[32], int c) {
-    uint32_t p[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) p[j] = exp_pair(v[2 * j], v[2 * j + 1], mc, sum);
-    tmem_st16(tl + c * 16, p);
-  };
-  tmem_load32(tl, x);
-#pragma unroll
-  for (int c = 0; c < 6; c += 2) {
-    tmem_ld32(tl + (c + 1) * 32, y);
-    exp_chunk(x, c);
-    tmem_wait_ld(y);
-    if (c + 2 < 6) {
-      tmem_ld32(tl + (c + 2) * 32, x);
-      exp_chunk(y, c + 1);
-      tmem_wait_ld(x);
-    } else {
-      exp_chunk(y, c + 1);
-    }
-  }
-  uint32_t e[16];
-  tmem_ld16(tl + 192, e);  // keys 192..207 -> P columns 96..103
-  tmem_ld_wait();
-  tmem_regs_ready16(e);
-  uint32_t pe[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    pe[j] = exp_pair(e[2 * j], e[2 * j + 1], mc, sum, 192 + 2 * j < kValidKeys,
-                     192 + 2 * j + 1 < kValidKeys);
-  tmem_st8(tl + 96, pe);
-  return sum;
-}
-
-__device__ __forceinline__ uint32_t scaled_pair(uint32_t a, uint32_t b, float inv) {
-  return pack_half2(__uint_as_float(a) * inv, __uint_as_float(b) * inv);
-}
 }  // namespace
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -348,19 +258,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float inv = 1.0f / sum;
         if (lane == 0) bulk_wait_read<0>();  // the previous store has read the staging tile
         __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          *reinterpret_cast<uint4 *>(stg_row + ((j ^ (lane & 7)) * 16)) =
-              make_uint4(scaled_pair(o0[8 * j], o0[8 * j + 1], inv),
-                         scaled_pair(o0[8 * j + 2], o0[8 * j + 3], inv),
-                         scaled_pair(o0[8 * j + 4], o0[8 * j + 5], inv),
-                         scaled_pair(o0[8 * j + 6], o0[8 * j + 7], inv));
-          *reinterpret_cast<uint4 *>(stg_row + (((4 + j) ^ (lane & 7)) * 16)) =
-              make_uint4(scaled_pair(o1[8 * j], o1[8 * j + 1], inv),
-                         scaled_pair(o1[8 * j + 2], o1[8 * j + 3], inv),
-                         scaled_pair(o1[8 * j + 4], o1[8 * j + 5], inv),
-                         scaled_pair(o1[8 * j + 6], o1[8 * j + 7], inv));
-        }
+        stage_output_row(stg_row, lane, o0, o1, inv);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
