@@ -83,10 +83,6 @@ def kernel_work(name: str, b: int = BATCH, last: bool = False):
                                     + fold)
     if name == "attention":
         return 4.0 * 201 * 201 * 64 * 6 * b, (r * 1152 + r * d) * f16
-    if name == "qkv_attention":  # folded QKV + RoPE + attention in one kernel: no qkv rows
-        return (2.0 * r * d * 1152 + 4.0 * 201 * 201 * 64 * 6 * b,
-                (r * d + 1152 * d + r * d) * f16 + (1152 + 2 * 196 * 64) * f32
-                + r * 2 * f32 + (r + 1152) * 16 * f16)
     if name in ("gemm_o_resid", "gemm_o_resid_layernorm", "gemm_o_resid_rowstat"):
         ln = name.endswith("layernorm")
         stats = r * (2 * f32 + 16 * f16) if name.endswith("rowstat") else 0
@@ -762,12 +758,6 @@ def run_ops(args):
                                               ptr(o[1]), ptr(o[2]), ptr(v["cos"]), ptr(v["sin"]),
                                               ptr(o[3]), ptr(st), s),
         *kernel_work("gemm_qkv_rope_folded"), r * (d + 1152 + 16) * f16b + r * 2 * f32b))
-    results.append(time_op(
-        "qkv_attention", lambda: (randn((r, d)), *stats(), empty((r, d))),
-        lambda o, s: lib.dv3k_qkv_attention_folded(ptr(o[0]), r, ptr(w["qkv"]), ptr(waux["qkv"]),
-                                                   ptr(o[1]), ptr(o[2]), ptr(v["cos"]),
-                                                   ptr(v["sin"]), ptr(o[3]), ptr(st), s),
-        *kernel_work("qkv_attention"), r * (2 * d + 16) * f16b + r * 2 * f32b))
     for k, wname in ((384, "o"), (1536, "down")):
         name = ("gemm_o_resid" if k == 384 else "gemm_down_resid") + "_rowstat"
         results.append(time_op(

@@ -1,5 +1,5 @@
-// attention_softmax.cuh - the per-row softmax of the attention kernels (attention.cu and the
-// fused QKV + attention kernel of qkv_attention.cu), on S held in tensor memory.
+// attention_softmax.cuh - the per-row softmax and output staging of the attention kernel
+// (attention.cu), on S and O held in tensor memory.
 //
 // One query row per thread (its TMEM lane). Pass 1: row max over the 201 valid keys. Pass 2:
 // w = exp(0.125 (s - max)) = 2^(s c - max c) with c = 0.125 log2(e) (one FFMA and the hardware

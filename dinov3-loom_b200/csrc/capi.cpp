@@ -492,27 +492,6 @@ int dv3k_matmul_swiglu_folded(const uint16_t *x, uint32_t rows, const uint16_t *
   return gemm_entry(dv3::GemmOp::SwiGLUFold, x, rows, gateup_wf, g, status, stream, w_aux);
 }
 
-int dv3k_qkv_attention_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf,
-                              const uint16_t *w_aux, const float *rowstat,
-                              const uint16_t *row_aux, const float *rope_cos,
-                              const float *rope_sin, uint16_t *out, uint32_t *status,
-                              void *stream) {
-  if (rows == 0) return DV3_OK;
-  if (!all_aligned(x, wf, w_aux, rowstat, row_aux, rope_cos, rope_sin, out))
-    return bad_args("pointers must be 16-byte aligned");
-  if (w_aux == nullptr || rowstat == nullptr || row_aux == nullptr)
-    return bad_args("w_aux, rowstat and row_aux are required");
-  if (rows % dv3::kTokens != 0) return bad_args("rows must be a multiple of 201");
-  dv3::QkvAttentionMaps maps;
-  std::string err;
-  if (!dv3::make_qkv_attention_maps(x, rows, wf, row_aux, w_aux, out, &maps, &err))
-    return bad_args(err.c_str());
-  return launch_status(
-      dv3::launch_qkv_attention(maps, rows, reinterpret_cast<const float2 *>(rowstat), rope_cos,
-                                rope_sin, status, static_cast<cudaStream_t>(stream)),
-      "qkv_attention");
-}
-
 uint32_t dv3k_gateup_source_row(uint32_t packed_row) { return dv3::gateup_source_row(packed_row); }
 
 }  // extern "C"

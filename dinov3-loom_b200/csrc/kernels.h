@@ -41,11 +41,6 @@ bool encode_map_f32(CUtensorMap *map, const void *base, uint64_t cols, uint64_t 
 // are clipped.
 bool encode_map_f16_images(CUtensorMap *map, const void *base, uint64_t cols, uint64_t n_images,
                            uint32_t box_rows, std::string *err);
-// The same per-image view with a box of box_cols (16, 32 or 64: box_cols * 2 bytes, the swizzle
-// width) x box_rows x 1 image.
-bool encode_map_f16_images_box(CUtensorMap *map, const void *base, uint64_t cols,
-                               uint64_t n_images, uint32_t box_cols, uint32_t box_rows,
-                               int swizzle_bytes, std::string *err);
 // 3D f32 view [slabs][rows][cols] (split-K partials), box = 32 columns x box_rows x 1 slab,
 // 128-byte swizzle; stores past `rows` are clipped inside each slab.
 bool encode_map_f32_slabs(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
@@ -183,26 +178,6 @@ cudaError_t launch_attention(const AttentionMaps &maps, uint32_t rows, uint32_t 
                              cudaStream_t stream, const void *l2_next = nullptr,
                              size_t l2_next_bytes = 0, const void *discard = nullptr,
                              size_t discard_bytes = 0);
-
-// ---- folded QKV + RoPE + attention in one kernel (qkv_attention.cu) ----
-// Per-image maps of x (128-token boxes of 64 columns) and of the row aux (128-token boxes of 16
-// columns, 32-byte swizzle), 2D maps of the folded QKV weights (64-row boxes) and of their aux
-// rows, and the per-image output map (32-token boxes), as attention_kernel's.
-struct QkvAttentionMaps {
-  CUtensorMap x, w, x_aux, w_aux, out;
-};
-bool make_qkv_attention_maps(const void *x, uint32_t rows, const void *wf, const void *row_aux,
-                             const void *w_aux, const void *out, QkvAttentionMaps *maps,
-                             std::string *err);
-// out = attention(rope(rstd (x wf^T - mean s + r c))) for rows = 201 * images; the same values as
-// the folded QKV GEMM followed by attention_kernel, without the qkv rows in global memory.
-// l2_next, l2_next2: weights of later kernels to prefetch into L2; discard: as GemmArgs.
-cudaError_t launch_qkv_attention(const QkvAttentionMaps &maps, uint32_t rows,
-                                 const float2 *rowstat, const float *rope_cos,
-                                 const float *rope_sin, uint32_t *status, cudaStream_t stream,
-                                 const void *l2_next = nullptr, size_t l2_next_bytes = 0,
-                                 const void *l2_next2 = nullptr, size_t l2_next2_bytes = 0,
-                                 const void *discard = nullptr, size_t discard_bytes = 0);
 
 // ---- bandwidth kernels (elementwise.cu) ----
 // l2_next/l2_next_bytes: weights of a later kernel to prefetch into L2 (see GemmArgs).

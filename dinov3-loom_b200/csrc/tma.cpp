@@ -95,29 +95,19 @@ bool encode_map_f32(CUtensorMap *map, const void *base, uint64_t cols, uint64_t 
 
 bool encode_map_f16_images(CUtensorMap *map, const void *base, uint64_t cols, uint64_t n_images,
                            uint32_t box_rows, std::string *err) {
-  return encode_map_f16_images_box(map, base, cols, n_images, 64, box_rows, 128, err);
-}
-
-bool encode_map_f16_images_box(CUtensorMap *map, const void *base, uint64_t cols,
-                               uint64_t n_images, uint32_t box_cols, uint32_t box_rows,
-                               int swizzle_bytes, std::string *err) {
   auto fn = encode_fn(err);
   if (!fn) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0 || n_images == 0 ||
-      box_rows == 0 || box_rows > 256 || box_cols * 2 != static_cast<uint32_t>(swizzle_bytes) ||
-      (swizzle_bytes != 32 && swizzle_bytes != 64 && swizzle_bytes != 128)) {
+      box_rows == 0 || box_rows > 256) {
     if (err) *err = "tensor map: base must be 16-byte aligned, rows of whole 16-byte units";
     return false;
   }
-  const CUtensorMapSwizzle sw = swizzle_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
-                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                      : CU_TENSOR_MAP_SWIZZLE_128B;
   const cuuint64_t dims[3] = {cols, static_cast<cuuint64_t>(kTokens), n_images};
   const cuuint64_t strides[2] = {cols * 2, cols * 2 * kTokens};
-  const cuuint32_t box[3] = {box_cols, box_rows, 1};
+  const cuuint32_t box[3] = {64, box_rows, 1};
   const cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims,
-                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     if (err) {

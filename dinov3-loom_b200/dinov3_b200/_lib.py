@@ -93,7 +93,6 @@ SIGNATURES = {
     "dv3k_layernorm_rowstat": ([_P, _U32, _P, _P, _P], _I),
     "dv3k_qkv_rope_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_matmul_swiglu_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P], _I),
-    "dv3k_qkv_attention_folded": ([_P, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dv3k_gateup_source_row": ([_U32], _U32),
     "dv3k_bounded_wait_selftest": ([ctypes.c_uint64, _P, _P], _I),
 }

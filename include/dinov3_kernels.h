@@ -146,19 +146,6 @@ int dv3k_matmul_swiglu_folded(const uint16_t *x, uint32_t rows, const uint16_t *
                               const uint16_t *row_aux, uint16_t *act, uint32_t *status,
                               void *stream);
 
-/* dv3k_qkv_rope_folded followed by dv3k_attention in one kernel, for rows = 201 * images: out
- * [rows][384] gets the attention of q, k, v = rope(rstd (x wf^T - mean s + r c)) with the inputs
- * of dv3k_qkv_rope_folded. Each (image, head) item's q, k and v go from the tensor-memory
- * accumulator into the shared-memory operands of the attention MMAs without a round trip
- * through global memory (no qkv buffer). Replaces the launch pair
- * kernels/matmul_qkv_rope_f16_wmma.loom + kernels/attention_online_f16_wmma_cf16.loom
- * (src/lib.rs:183-199) in the large-batch plan. */
-int dv3k_qkv_attention_folded(const uint16_t *x, uint32_t rows, const uint16_t *wf,
-                              const uint16_t *w_aux, const float *rowstat,
-                              const uint16_t *row_aux, const float *rope_cos,
-                              const float *rope_sin, uint16_t *out, uint32_t *status,
-                              void *stream);
-
 /* Down projection split over K (kernels/matmul_splitk_f16_wmma.loom, launched at batch 1 by
  * src/lib.rs:218-224 with the specialisation of :297): for each slice s < splits of the 1536-long
  * reduction, partials[s][row][n] = sum over k in slice s of a[row][k] * w[n][k], f32, no bias.

@@ -537,44 +537,6 @@ def test_matmul_swiglu_folded(b):
     assert_as_accurate(act, plain, ref)
 
 
-# The fused folded QKV + attention kernel (one CTA per (image, head) item, q/k/v kept in shared
-# memory): the same values as dv3k_qkv_rope_folded followed by dv3k_attention on the same inputs
-# (to within one f16 step: the RoPE products may contract differently), and as accurate as that
-# pair against the float64 reference. 1 image: 6 items on 6 CTAs; 50 and 64 images: 300 and 384
-# items, two or three per persistent CTA.
-@pytest.mark.parametrize("b", [1, 3, 50, 64])
-def test_qkv_attention_folded(b):
-    rng = np.random.default_rng(120 + b)
-    r = rows_of(b)
-    x = f16(rng.standard_normal((r, 384)) * 2 + rng.standard_normal((r, 1)))
-    g = rng.standard_normal(384) * 0.3 + 1
-    be = rng.standard_normal(384) * 0.1
-    w = f16(rng.standard_normal((1152, 384)) / np.sqrt(384))
-    bias = rng.standard_normal(1152) * 0.1
-    bias[384:768] = 0
-    ref = attention_ref(rope_ref(ln64(x, g, be) @ w.T + bias.astype(np.float32), r), b)
-    wf, waux = fold(w, bias, g, be)
-    rst, raux = rowstat_of(x)
-    cos, sin = ref_numpy.rope_tables()
-    args = (ptr(t16(x)), r, ptr(t16(wf)), ptr(t16(waux)), ptr(t32(rst)), ptr(t16(raux)),
-            ptr(t32(cos)), ptr(t32(sin)))
-    fused = torch.full((r, 384), 9.0, dtype=torch.float16, device=DEV)
-    qkv = torch.empty((r, 1152), dtype=torch.float16, device=DEV)
-    pair = torch.full((r, 384), 9.0, dtype=torch.float16, device=DEV)
-    st = status()
-    check_rc(lib().dv3k_qkv_attention_folded(*args, ptr(fused), ptr(st), stream()))
-    check_rc(lib().dv3k_qkv_rope_folded(*args, ptr(qkv), ptr(status()), stream()))
-    check_rc(lib().dv3k_attention(ptr(qkv), r, ptr(pair), ptr(status()), stream()))
-    torch.cuda.synchronize()
-    assert st.cpu().tolist() == [0, 0]
-    f = fused.float().cpu().numpy().astype(np.float64)
-    p = pair.float().cpu().numpy().astype(np.float64)
-    assert np.isfinite(f).all()
-    d = np.abs(f - p) / np.maximum(1.0, np.abs(p))
-    assert d.max() <= 2e-3, f"fused vs two launches: max scaled difference {d.max():.3e}"
-    assert_as_accurate(fused, pair, ref)
-
-
 def test_bounded_wait_expires_and_context_survives():
     """The failure path every kernel uses, made to run out on the device without a fault: a wait
     on an mbarrier that nothing arrives at expires after its limit and records its bit, the
