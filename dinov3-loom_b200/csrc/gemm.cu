@@ -608,6 +608,19 @@ bool resid_wide(uint32_t rows) {
   return 2 * m_tiles > sms && m_tiles <= sms;
 }
 
+// With the LayerNorms folded (the full-row residual GEMMs leave only the row statistics, and QKV
+// and gate/up apply the LayerNorm), the full-row plan wins as soon as the 128-wide residual
+// tiles (three per row tile) need more than one wave: on 148 SMs from 50 row tiles (batch 32),
+// where the 128-wide plan steps from 742 to 837 us per forward between batch 31 and 32 and the
+// folded plan takes 798 us (906 against 968 us at batch 47; below 32 the 128-wide plan is faster:
+// 696 against 741 us at 25, 742 against 772 at 31).
+bool resid_full_rows_plan(uint32_t rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t m_tiles = (rows + BM - 1) / BM, sms = static_cast<uint32_t>(sm_count(dev));
+  return 3 * m_tiles > sms && m_tiles <= sms;
+}
+
 // Partial slabs of the no-alloc split-K entry point (dv3k_down_splitk_noalloc): a file-scope
 // device array, so that call needs no workspace from its caller and allocates nothing. Its size
 // is fixed when the library is built (6144 partial rows of 384 floats, 9 MiB on every device that

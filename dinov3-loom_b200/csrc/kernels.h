@@ -86,6 +86,10 @@ GemmShape gemm_shape(GemmOp op, uint32_t rows);
 // Whether the residual GEMMs over `rows` rows run on full 384-wide rows (the ResidLN* ops always
 // do; they need every 128-row tile in one wave of CTAs).
 bool resid_wide(uint32_t rows);
+// Whether the forward plan over `rows` rows runs the residual GEMMs on full rows with the
+// LayerNorms fused and folded (the 128-wide residual tiles would need more than one wave, and
+// every full-row tile fits one).
+bool resid_full_rows_plan(uint32_t rows);
 
 // Tensor maps of one GEMM launch: A = activations [rows][k], B = weights [n][k].
 struct GemmMaps {

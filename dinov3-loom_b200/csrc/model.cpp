@@ -227,7 +227,7 @@ void Model::release() {
 // down-proj+LS2+residual+(LN1 of the next layer | final LN). The reference launches each
 // LayerNorm separately (87 launches at b > 1); here each one after layer 0's first rides in the
 // epilogue of the GEMM that produces its input row (3 + 12*5 = 63 launches), whenever the
-// residual GEMMs run on full rows (large batches; see resid_wide); small batches keep 128-wide
+// residual GEMMs run on full rows (batch 32 and up; see resid_full_rows_plan); small batches keep 128-wide
 // residual tiles and separate LayerNorm launches (3 + 12*7 = 87). With the full-row residual
 // GEMMs, the LayerNorms before QKV and gate/up are further folded into those GEMMs
 // (fold_layernorm): the residual GEMM (and, for layer 0, layernorm_rowstat) leaves only each
@@ -242,9 +242,16 @@ uint32_t Model::down_splits(uint32_t rows) const {
   return splitk_splits(rows);
 }
 
+// The full-row plan starts where the 128-wide residual tiles need a second wave when the
+// LayerNorms are folded (batch 32 on 148 SMs, resid_full_rows_plan), and only where the row
+// tiles outnumber half the SMs when they are not (batch 48, resid_wide): the normalise-and-store
+// phase makes the unfolded full-row GEMMs slower than 128-wide tiles in one and a half waves.
 bool Model::fuse_layernorm(size_t b) const {
   if (const char *v = std::getenv("DV3_FUSE_LAYERNORM")) return v[0] == '1';
-  return resid_wide(static_cast<uint32_t>(kTokens * b));
+  const uint32_t rows = static_cast<uint32_t>(kTokens * b);
+  const char *f = std::getenv("DV3_FOLD_LAYERNORM");
+  const bool unfolded = f != nullptr && ((f[0] - '0') & 3) == 0;
+  return unfolded ? resid_wide(rows) : resid_full_rows_plan(rows);
 }
 
 // With the LayerNorms fused into the full-row residual GEMMs, each of them except the final one

@@ -235,10 +235,8 @@ def test_every_image_of_full_batches_against_oracle(models, oracles, flavor, bat
     oracle, all-token and CLS cosine > 0.9999 each, and every output element within
     MAX_ABS_FULL, as tests/model.rs:75-94 checks every image of its batch."""
     model = models(flavor, max_batch=batch)
-    if batch == 32:
-        assert model.launches_per_forward(32) == 3 + 12 * 7  # 128-wide residual tiles
-    else:
-        assert model.launches_per_forward(64) == 3 + 12 * 5  # full-row residual + LayerNorm
+    # both run the full-row residual GEMMs with the LayerNorms folded (from 32 images on)
+    assert model.launches_per_forward(batch) == 3 + 12 * 5
     images = synth.images(5000 + batch, batch) if source == "seeded" else \
         synth.reference_test_images(batch)
     out = model.forward(images)
@@ -354,7 +352,7 @@ def test_mid_size_batch_plans(models, oracles, b):
 def test_every_batch_size_matches_single_images(models, oracles):
     """Every resident batch size 1..64 (each crosses its own mix of plan variants: split-K down
     projection up to 15 images, one attention CTA per query tile up to 12, narrow GEMM units,
-    full-row residual+LayerNorm GEMMs from 48): each image of a batch matches that image's
+    full-row residual GEMMs with the folded LayerNorms from 32): each image of a batch matches that image's
     single-image forward, and two images of the largest batch match the float64 oracle."""
     model = models("stress", max_batch=64)
     images = synth.images(4096, 64)
