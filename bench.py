@@ -31,6 +31,10 @@ barrier and the max-over-ranks of the timings).
           tests/support/reference.rs) on this host, OpenMP over images, rank 0 at N = 1 only.
 Reference arm (--impl reference): the same CPU oracle with all host threads, rank 0 only; a
 step is one forward of as many images as host threads (a bounded sample of the batch-64 step).
+--serve: BASELINE config 4, seeded call sizes uniform over 1..64 images from pinned host memory,
+synchronous dv3_forward calls and dv3_submit / dv3_wait two calls deep, aggregate images/s and
+per-call p50 / p99 latency (host clock).
+--forward-only [--batch B]: run the plan's forwards without timing (for ncu launch lists).
 --copies: the end-to-end step's host<->device transfers alone (no forward), per rank, to show how
 much copy bandwidth the host gives N GPUs at once.
 --ops: BASELINE config 3, every kernel entry point (include/dinov3_kernels.h) alone at batch 64
